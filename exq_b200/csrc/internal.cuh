@@ -1,0 +1,90 @@
+// Internal kernel parameter blocks and launchers shared by the .cu files.
+#pragma once
+
+#include "common.cuh"
+
+namespace exq {
+
+// ----------------------------------------------------------------- routing
+enum RouteMode : int {
+  kRouteAlign = 0,      // sgl_kernel moe_align_block_size
+  kRouteEndsFromSlots,  // exq_build_ends_from_slots
+  kRouteDispatch,       // exq_dispatch
+  kRouteLayer,          // GEMM tile list (optionally with shared experts)
+};
+
+struct RouteParams {
+  // inputs
+  const void* ids;  // ALIGN / DISPATCH / LAYER: flat top-k ids
+  int ids_dtype;
+  const int32_t* slot_ids;     // ENDS_FROM_SLOTS: align output
+  const int32_t* flat_router;  // ENDS_FROM_SLOTS
+  int64_t n;                   // number of elements walked
+  int64_t n_active;            // ENDS_FROM_SLOTS: valid slot bound
+  int n_buckets;               // buckets counted (experts incl. shared)
+  int n_routed;                // LAYER: ids must be < n_routed
+  int top_k;                   // LAYER: ids row length
+  int slots_per_token;         // LAYER: top_k + n_shared
+  int block_size;              // ALIGN padding
+  int mt;                      // LAYER: max rows per GEMM tile
+  // outputs
+  int32_t* sorted_i32;         // ALIGN: sorted_token_ids; LAYER: slot at each sorted position
+  int64_t sorted_cap;          // ALIGN
+  int pad_sorted;              // ALIGN
+  int32_t* block_expert;       // ALIGN: expert_ids
+  int64_t block_cap;           // ALIGN
+  int32_t* ntpp;               // ALIGN
+  int32_t* cumsum;             // ALIGN: [n_buckets + 1]
+  int32_t* ends;               // ENDS/DISPATCH/LAYER: [n_buckets + 1]
+  int64_t* order_i64;          // ENDS/DISPATCH (and LAYER if set): sort_order
+  int64_t* sorted_expert_i64;  // DISPATCH
+  int32_t* pos_of_slot;        // LAYER: sorted position of every slot, -1 if dropped
+  int32_t* tile_info;          // LAYER: [max_tiles][3] = expert, first row, rows
+  int32_t* n_tiles;            // LAYER: [1]
+  int64_t max_tiles;
+  uint32_t* status;
+};
+
+int launch_route(RouteParams& p, int mode, cudaStream_t stream);
+
+// ------------------------------------------------------------ grouped GEMM
+constexpr int kGmMTHost = 32;   // max token rows per GEMM tile
+constexpr int kGmRBHost = 128;  // weight rows per work item
+
+enum GemmMode : int { kGemmModePlain = 0, kGemmModeGateUp = 1, kGemmModeDown = 2 };
+
+struct GemmParams {
+  const exq_expert_desc* experts;
+  int proj;         // 0: w13 / w13_scales, 1: w2 / w2_scales
+  int mode;
+  int n_rows;       // output rows of the projection: PLAIN N, GATE_UP 2I, DOWN H
+  int k;            // reduction length
+  int inter;        // GATE_UP: I
+  int nblocks;      // row blocks per tile
+  const void* act;  // PLAIN/GATE_UP: hidden [T, k]; DOWN: mid [n_pos, k]
+  int64_t act_stride;
+  int gather;       // 1: activation row = token of the sorted slot
+  int spt;          // slots per token (top_k + shared)
+  int top_k;
+  const int32_t* sorted_slot;
+  const int32_t* tile_info;
+  const int32_t* n_tiles_ptr;
+  int max_tiles;
+  void* out;
+  int out_dtype;
+  int64_t out_stride;
+  const void* topk_w;
+  int w_dtype;
+  uint32_t* status;
+};
+
+int launch_gemm(const GemmParams& p, int act_dtype, int max_items, cudaStream_t stream);
+
+// ------------------------------------------------------------- elementwise
+int launch_combine_partials(const float* partial, int64_t H, const int32_t* pos_of_slot,
+                            int64_t n_tokens, int spt, void* out, int dtype,
+                            cudaStream_t stream);
+
+uint32_t* device_status_ptr();
+
+}  // namespace exq

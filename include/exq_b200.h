@@ -1,0 +1,215 @@
+/*
+ * exq_b200.h -- C ABI of the B200-native quantized MoE expert path.
+ *
+ * Drop-in replacement for the GPU hot path of alityb/exq: the
+ * `exq_dispatch_cuda` extension (exq/kernels/cuda_src/exq_dispatch.cu), the
+ * sgl_kernel steps the SGLang backend calls (`moe_align_block_size`,
+ * `silu_and_mul`, exq/runtime/sglang_backend.py:79,:108-109,:140) and the
+ * Triton INT4/FP16 grouped GEMMs of exq/kernels (moe_int4_kernel.py,
+ * moe_grouped_gemm.py).
+ *
+ * Conventions
+ *  - Every entry point takes plain device pointers, sizes and dtype tags and a
+ *    `stream` (a cudaStream_t passed as void*; NULL = legacy default stream).
+ *  - Work is only enqueued: nothing synchronises, nothing allocates, and every
+ *    launch is capturable in a CUDA graph.  Temporary storage is a
+ *    caller-provided workspace sized by the matching *_workspace_bytes query.
+ *  - Outputs are caller-preallocated, as in the reference.
+ *  - Return value: EXQ_OK (0) or a negative EXQ_ERR_* code;
+ *    exq_last_error() gives a message (thread-local).  Argument errors are
+ *    detected on the host before anything is enqueued.  Conditions that can
+ *    only be seen on the device (an expert id out of range) are recorded in
+ *    the device status word, read with exq_read_device_status().
+ */
+#ifndef EXQ_B200_H_
+#define EXQ_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define EXQ_API __attribute__((visibility("default")))
+#else
+#define EXQ_API
+#endif
+
+#define EXQ_ABI_VERSION 1
+
+/* status codes */
+#define EXQ_OK 0
+#define EXQ_ERR_INVALID -1     /* bad argument (shape, dtype, null pointer) */
+#define EXQ_ERR_UNSUPPORTED -2 /* valid but not implemented (e.g. group size) */
+#define EXQ_ERR_CUDA -3        /* a CUDA runtime call or launch failed */
+#define EXQ_ERR_WORKSPACE -4   /* workspace missing or too small */
+
+/* dtype tags */
+#define EXQ_F16 0
+#define EXQ_BF16 1
+#define EXQ_F32 2
+#define EXQ_I32 3
+#define EXQ_I64 4
+#define EXQ_U8 5
+#define EXQ_I8 6
+
+/* weight tiers, numbered as exq/kernels/exq_artifact.py:25 PRECISION_TO_INT */
+#define EXQ_TIER_BF16 0 /* 16-bit weights in the activation dtype */
+#define EXQ_TIER_INT8 1 /* int8 [N,K] + fp16 per-row scale [N] */
+#define EXQ_TIER_INT4 2 /* u8 [N,K/2] (q+8 nibbles, even k low) + fp16 [N,K/128] */
+#define EXQ_TIER_NONE -1
+
+/* device status bits (exq_read_device_status) */
+#define EXQ_DEV_BAD_EXPERT_ID 1u /* an id outside [0, n_experts) was dropped */
+#define EXQ_DEV_BAD_SLOT 2u      /* a sort_order / slot entry was out of range */
+#define EXQ_DEV_BAD_TIER 4u      /* an expert descriptor had an unknown tier */
+
+EXQ_API int exq_abi_version(void);
+EXQ_API const char* exq_last_error(void);
+EXQ_API const char* exq_status_string(int status);
+
+/* Reads (synchronously, on `stream`) and optionally clears the device status
+ * word that kernels OR their EXQ_DEV_* bits into.  Debug/validation helper,
+ * not for hot paths. */
+EXQ_API int exq_read_device_status(uint32_t* status_out, int clear, void* stream);
+
+/* ---------------------------------------------------------------- routing */
+
+/* sgl_kernel.moe_align_block_size (called at exq/runtime/sglang_backend.py:102-109).
+ * Counts the flat top-k ids over `num_experts` buckets, pads each count to a
+ * multiple of `block_size`, writes every slot index into its expert's range
+ * (ascending slot order within an expert), pads with `numel`, writes the
+ * owner expert of every block (-1 beyond num_tokens_post_pad/block_size), the
+ * padded total and the exclusive padded prefix `cumsum_buffer[num_experts+1]`.
+ * With pad_sorted_token_ids = 0 the positions not holding a slot are left
+ * untouched (the caller pre-fills them). */
+EXQ_API int exq_moe_align_block_size(const void* topk_ids, int ids_dtype, int64_t numel,
+                             int32_t num_experts, int32_t block_size,
+                             int32_t* sorted_token_ids, int64_t sorted_cap,
+                             int32_t* expert_ids, int64_t expert_ids_cap,
+                             int32_t* num_tokens_post_pad, int32_t* cumsum_buffer,
+                             int32_t pad_sorted_token_ids, void* stream);
+
+/* exq_dispatch_cuda.build_ends_from_slots (exq/kernels/cuda_src/exq_dispatch.cu:181-229).
+ * From align output `sorted_slot_ids[em]` (entries >= n_active are padding) and
+ * `flat_router[n_active]` (expert of each flat slot): expert_ends[E+1]
+ * (exclusive prefix of per-expert counts) and sort_order[n_active] (int64,
+ * valid slots compacted per expert in order of appearance).  One launch. */
+EXQ_API int exq_build_ends_from_slots(const int32_t* sorted_slot_ids, int64_t em,
+                              const int32_t* flat_router, int64_t n_active,
+                              int32_t n_experts, int32_t* expert_ends,
+                              int64_t* sort_order, void* stream);
+
+/* exq_dispatch_cuda.dispatch (exq_dispatch.cu:99-149): stable sort of the flat
+ * top-k ids by expert.  sort_order[n] and sorted_expert_ids[n] are int64,
+ * expert_ends[E+1] int32.  One launch, no temporary storage. */
+EXQ_API int exq_dispatch(const void* router_indices, int ids_dtype, int64_t n, int32_t n_experts,
+                 int64_t* sort_order, int64_t* sorted_expert_ids, int32_t* expert_ends,
+                 void* stream);
+
+/* exq_dispatch_cuda.gather_hidden (exq_dispatch.cu:234-260):
+ * out[i, :] = hidden[sort_order[i] / top_k, :].  fp16 and bf16 (the reference
+ * takes fp16 only).  `row_stride` is hidden's row stride in elements. */
+EXQ_API int exq_gather_hidden(const void* hidden, int dtype, int64_t n_tokens, int64_t hidden_size,
+                      int64_t row_stride, const int64_t* sort_order, int64_t n_active,
+                      int32_t top_k, void* out, void* stream);
+
+/* exq_dispatch_cuda.combine (exq_dispatch.cu:263-310):
+ * result[t, :] = sum_j w[t, j] * down_out[pos(t*k + j), :] with pos the
+ * inverse of sort_order; fp32 products and sum in top-k order, one rounding
+ * to the output dtype.  Deterministic (the reference uses fp32 atomics).
+ * Weights may be fp32, fp16 or bf16 (the reference reads fp16 only). */
+EXQ_API size_t exq_combine_workspace_bytes(int64_t n_active);
+EXQ_API int exq_combine(const void* down_out, int dtype, int64_t n_active, int64_t hidden_size,
+                const int64_t* sort_order, const void* router_weights, int w_dtype,
+                int64_t n_tokens, int32_t top_k, void* result, int out_dtype,
+                void* workspace, size_t workspace_bytes, void* stream);
+
+/* sgl_kernel.silu_and_mul (exq/runtime/sglang_backend.py:138-140):
+ * out[m, i] = silu(x[m, i]) * x[m, I + i], fp32 math. */
+EXQ_API int exq_silu_and_mul(const void* input, void* out, int dtype, int64_t m, int64_t inter,
+                     void* stream);
+
+/* ---------------------------------------------------------------- packing */
+
+/* pack_int4_weights / pack_experts_int4 (exq/kernels/moe_int4_kernel.py:37-119),
+ * on the GPU, bit-exact: rows x k matrix (fp16/bf16/fp32) -> packed u8
+ * [rows, k/2] + fp16 scales [rows, k/group]; group = k when k < group_size. */
+EXQ_API int exq_pack_int4(const void* w, int dtype, int64_t rows, int64_t k, int32_t group_size,
+                  uint8_t* packed, void* scales_f16, void* stream);
+
+/* The INT8 tier of a quant plan (exq/eval/quant_shim.py:84-96 semantics, scale
+ * stored as fp16): int8 [rows, k] + fp16 per-row scale [rows]. */
+EXQ_API int exq_quant_int8(const void* w, int dtype, int64_t rows, int64_t k, int8_t* q,
+                   void* scales_f16, void* stream);
+
+/* ------------------------------------------------------ grouped expert GEMMs */
+
+/* One expert's weights in one of the three tiers.  Pointers are device
+ * pointers; the array of descriptors itself lives in device memory. */
+typedef struct exq_expert_desc {
+  int32_t tier;           /* EXQ_TIER_* ; EXQ_TIER_NONE = expert absent */
+  int32_t reserved;
+  const void* w13;        /* gate_up [2I, H] in the tier's format */
+  const void* w13_scales; /* INT4: f16 [2I, H/128]; INT8: f16 [2I]; BF16: NULL */
+  const void* w2;         /* down [H, I] */
+  const void* w2_scales;  /* INT4: f16 [H, I/128]; INT8: f16 [H]; BF16: NULL */
+} exq_expert_desc;
+
+/* The Triton `_moe_gemm_int4_kernel` / `_moe_gemm_kernel` launches of
+ * moe_int4_forward (moe_int4_kernel.py:245-327) and moe_grouped_gemm
+ * (moe_grouped_gemm.py:173-227), with the token sort and the hidden-state
+ * gather fused in: out[i, :] = hidden[sort_order[i] / top_k] . W[e_i]^T in
+ * expert-sorted (stable) order, fp32 accumulation.
+ * `experts` is a device array of n_experts descriptors; only `w13` /
+ * `w13_scales` are read, as a single [n_rows, k] projection.  The output
+ * dtype is fp16 or bf16.  Optional `sort_order_out` (int64 [n]) and
+ * `expert_ends_out` (int32 [E+1]) receive the routing metadata. */
+EXQ_API size_t exq_moe_gemm_workspace_bytes(int64_t n_tokens, int32_t top_k, int32_t n_experts);
+EXQ_API int exq_moe_gemm(const exq_expert_desc* experts, int32_t n_experts, int64_t n_rows,
+                 int64_t k, const void* hidden, int act_dtype, int64_t n_tokens,
+                 const void* topk_ids, int ids_dtype, int32_t top_k, void* out,
+                 int out_dtype, int64_t* sort_order_out, int32_t* expert_ends_out,
+                 void* workspace, size_t workspace_bytes, void* stream);
+
+/* The whole MoE layer of exq/runtime/sglang_backend.py:65-158 (and
+ * moe_int4_full_forward, moe_int4_kernel.py:330-426): route -> gate_up
+ * (gather fused) -> SiLU*mul (fused epilogue) -> down -> top-k weighted
+ * combine, for a layer whose experts may mix the BF16/INT8/INT4 tiers.
+ * `experts` holds n_routed + n_shared descriptors; experts
+ * [n_routed, n_routed + n_shared) are shared experts applied to every token
+ * with weight 1.  hidden/out: [n_tokens, hidden] in act_dtype;
+ * topk_ids [n_tokens, top_k] (int32/int64), topk_weights [n_tokens, top_k]
+ * (f32/f16/bf16).  Four launches, no host synchronisation. */
+EXQ_API size_t exq_moe_layer_workspace_bytes(int64_t n_tokens, int32_t top_k, int32_t n_shared,
+                                     int32_t n_experts_total, int64_t hidden,
+                                     int64_t inter);
+EXQ_API int exq_moe_layer_forward(const exq_expert_desc* experts, int32_t n_routed,
+                          int32_t n_shared, int64_t hidden, int64_t inter,
+                          const void* hidden_states, int act_dtype, int64_t n_tokens,
+                          const void* topk_ids, int ids_dtype, const void* topk_weights,
+                          int w_dtype, int32_t top_k, void* out, void* workspace,
+                          size_t workspace_bytes, void* stream);
+
+/* The same layer, launching only its stages [first_stage, end_stage):
+ * 0 = route (sort + tile list), 1 = gate_up grouped GEMM with fused gather and
+ * SiLU*mul, 2 = down grouped GEMM writing weighted fp32 partials,
+ * 3 = top-k combine.  Stages communicate through `workspace`, so a caller may
+ * run them separately on one stream (per-kernel timing) as long as the
+ * arguments are identical; exq_moe_layer_forward = stages [0, 4). */
+#define EXQ_LAYER_STAGES 4
+EXQ_API int exq_moe_layer_forward_range(const exq_expert_desc* experts, int32_t n_routed,
+                                        int32_t n_shared, int64_t hidden, int64_t inter,
+                                        const void* hidden_states, int act_dtype,
+                                        int64_t n_tokens, const void* topk_ids, int ids_dtype,
+                                        const void* topk_weights, int w_dtype, int32_t top_k,
+                                        void* out, void* workspace, size_t workspace_bytes,
+                                        void* stream, int32_t first_stage, int32_t end_stage);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* EXQ_B200_H_ */
