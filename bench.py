@@ -296,23 +296,29 @@ def time_graphs(graphs, steps, warmup, dev):
     return e0.elapsed_time(e1) / 1e3
 
 
+STAGES = ("route", "prep", "gate_up", "down", "combine")
+
+
 def gemm_timing(banks, inputs, dev, reps=40):
-    """Average duration of each of the 4 launches, measured by replaying one
-    CUDA graph per layer that records events between the launches."""
+    """Average device time of each launch of a layer call: one CUDA graph per
+    layer records an (external) event between consecutive launches."""
     import torch
-    from exq_b200 import _lib as L
-    names = ("route", "gate_up", "down", "combine")
-    sums = [0.0] * 4
-    n = 0
+    sums = [0.0] * len(STAGES)
     s = torch.cuda.Stream(dev)
     s.wait_stream(torch.cuda.current_stream(dev))
     ev_graphs = []
     with torch.cuda.stream(s):
         for bank, (x, ids, w, _) in zip(banks, inputs):
-            evs = [torch.cuda.Event(enable_timing=True) for _ in range(5)]
+            bank.reserve(x.shape[0], ids.shape[1])
+            out = torch.empty(x.shape[0], bank.hidden, dtype=x.dtype, device=dev)
+            evs = [torch.cuda.Event(enable_timing=True, external=True)
+                   for _ in range(len(STAGES) + 1)]
             g = torch.cuda.CUDAGraph()
             with torch.cuda.graph(g, stream=s):
-                _split_forward(bank, x, ids, w, evs, s)
+                evs[0].record(s)
+                for i in range(len(STAGES)):
+                    bank.forward_range(x, ids, w, i, i + 1, out=out)
+                    evs[i + 1].record(s)
             ev_graphs.append((g, evs))
     torch.cuda.current_stream(dev).wait_stream(s)
     torch.cuda.synchronize(dev)
@@ -320,43 +326,9 @@ def gemm_timing(banks, inputs, dev, reps=40):
         g, evs = ev_graphs[r % len(ev_graphs)]
         g.replay()
         torch.cuda.synchronize(dev)
-        for i in range(4):
+        for i in range(len(STAGES)):
             sums[i] += evs[i].elapsed_time(evs[i + 1])
-        n += 1
-    return {nm: sums[i] / n / 1e3 for i, nm in enumerate(names)}
-
-
-def _split_forward(bank, x, ids, w, evs, stream):
-    """The layer forward with an event recorded between its launches."""
-    import torch
-    from exq_b200 import _lib as L
-    lib = L.lib()
-    t, k = ids.shape
-    bank.reserve(t, k)
-    ws = bank._ws
-    out = torch.empty(t, bank.hidden, dtype=bank.act_dtype, device=x.device)
-    evs[0].record(stream)
-    L.check(lib.exq_moe_layer_forward_range(
-        L.ptr(bank.desc), bank.n_routed, bank.n_shared, bank.hidden, bank.inter, L.ptr(x), L.tag(x),
-        t, L.ptr(ids), L.tag(ids), L.ptr(w), L.tag(w), k, L.ptr(out), L.ptr(ws), ws.numel(),
-        stream.cuda_stream, 0, 1), "route")
-    evs[1].record(stream)
-    L.check(lib.exq_moe_layer_forward_range(
-        L.ptr(bank.desc), bank.n_routed, bank.n_shared, bank.hidden, bank.inter, L.ptr(x), L.tag(x),
-        t, L.ptr(ids), L.tag(ids), L.ptr(w), L.tag(w), k, L.ptr(out), L.ptr(ws), ws.numel(),
-        stream.cuda_stream, 1, 2), "gate_up")
-    evs[2].record(stream)
-    L.check(lib.exq_moe_layer_forward_range(
-        L.ptr(bank.desc), bank.n_routed, bank.n_shared, bank.hidden, bank.inter, L.ptr(x), L.tag(x),
-        t, L.ptr(ids), L.tag(ids), L.ptr(w), L.tag(w), k, L.ptr(out), L.ptr(ws), ws.numel(),
-        stream.cuda_stream, 2, 3), "down")
-    evs[3].record(stream)
-    L.check(lib.exq_moe_layer_forward_range(
-        L.ptr(bank.desc), bank.n_routed, bank.n_shared, bank.hidden, bank.inter, L.ptr(x), L.tag(x),
-        t, L.ptr(ids), L.tag(ids), L.ptr(w), L.tag(w), k, L.ptr(out), L.ptr(ws), ws.numel(),
-        stream.cuda_stream, 3, 4), "combine")
-    evs[4].record(stream)
-    return out
+    return {nm: sums[i] / reps / 1e3 for i, nm in enumerate(STAGES)}
 
 
 def e2e_timing(banks, inputs, dev, steps, warmup):
@@ -505,7 +477,7 @@ def main():
                    "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
                    "us_per_layer": round(1e6 * t_max / args.steps, 2),
                    "hbm_frac_of_" + peak_kind: round(value / world / peak, 3)},
-        "roofline": {"bound": "hbm", "kernel": "moe_gemm_kernel (gate_up launch)",
+        "roofline": {"bound": "hbm", "kernel": "moe_tc_kernel (gate_up launch)",
                      "achieved": round(gu_ach, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(gu_ach / peak, 3),
                      "traffic": (traffic or {}).get("gate_up_bytes_per_launch"),
@@ -516,7 +488,7 @@ def main():
         "e2e": {"value": round(e2e_val, 1), "unit": UNIT, "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "steps": e2e_steps,
                 "us_per_layer": round(1e6 * t_e2e / e2e_steps, 2)},
-        "gpu_launches": 4 * args.steps,
+        "gpu_launches": len(STAGES) * args.steps,
         "clocks": clk.summary(),
         "sweep": sweep,
     }

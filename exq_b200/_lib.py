@@ -19,7 +19,7 @@ LIB_PATH = Path(__file__).resolve().parent / "_lib" / "libexq_b200.so"
 OK, ERR_INVALID, ERR_UNSUPPORTED, ERR_CUDA, ERR_WORKSPACE = 0, -1, -2, -3, -4
 F16, BF16, F32, I32, I64, U8, I8 = 0, 1, 2, 3, 4, 5, 6
 TIER_BF16, TIER_INT8, TIER_INT4, TIER_NONE = 0, 1, 2, -1
-DEV_BAD_EXPERT_ID, DEV_BAD_SLOT, DEV_BAD_TIER = 1, 2, 4
+DEV_BAD_EXPERT_ID, DEV_BAD_SLOT, DEV_BAD_TIER, DEV_TIMEOUT = 1, 2, 4, 8
 
 _DTYPE_TAG = {
     torch.float16: F16,
@@ -54,11 +54,10 @@ SIGNATURES = {
     "exq_moe_gemm": (C.c_int, [vp, i32, i64, i64, vp, C.c_int, i64, vp, C.c_int, i32, vp, C.c_int,
                                vp, vp, vp, sz, vp]),
     "exq_moe_layer_workspace_bytes": (sz, [i64, i32, i32, i32, i64, i64]),
-    "exq_moe_layer_forward": (C.c_int, [vp, i32, i32, i64, i64, vp, C.c_int, i64, vp, C.c_int, vp,
-                                        C.c_int, i32, vp, vp, sz, vp]),
-    "exq_moe_layer_forward_range": (C.c_int, [vp, i32, i32, i64, i64, vp, C.c_int, i64, vp,
-                                              C.c_int, vp, C.c_int, i32, vp, vp, sz, vp, i32,
-                                              i32]),
+    "exq_moe_layer_forward": (C.c_int, [vp, vp, C.c_int, i64, vp, C.c_int, vp, C.c_int, i32, vp,
+                                        vp, sz, vp]),
+    "exq_moe_layer_forward_range": (C.c_int, [vp, vp, C.c_int, i64, vp, C.c_int, vp, C.c_int, i32,
+                                              vp, vp, sz, vp, i32, i32]),
 }
 
 _lock = threading.Lock()

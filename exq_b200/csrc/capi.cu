@@ -189,132 +189,3 @@ extern "C" int exq_moe_gemm(const exq_expert_desc* experts, int32_t n_experts, i
   return launch_gemm(gp, act_dtype, static_cast<int>(max_items < INT32_MAX ? max_items : INT32_MAX), s);
 }
 
-extern "C" size_t exq_moe_layer_workspace_bytes(int64_t n_tokens, int32_t top_k, int32_t n_shared,
-                                                int32_t n_experts_total, int64_t hidden,
-                                                int64_t inter) {
-  if (n_tokens < 0 || top_k <= 0 || n_shared < 0 || n_experts_total <= 0) return 0;
-  return carve(nullptr, n_tokens * (top_k + n_shared), n_experts_total, inter, hidden, true).bytes;
-}
-
-extern "C" int exq_moe_layer_forward(const exq_expert_desc* experts, int32_t n_routed,
-                                     int32_t n_shared, int64_t hidden, int64_t inter,
-                                     const void* hidden_states, int act_dtype, int64_t n_tokens,
-                                     const void* topk_ids, int ids_dtype, const void* topk_weights,
-                                     int w_dtype, int32_t top_k, void* out, void* workspace,
-                                     size_t workspace_bytes, void* stream) {
-  return exq_moe_layer_forward_range(experts, n_routed, n_shared, hidden, inter, hidden_states,
-                                     act_dtype, n_tokens, topk_ids, ids_dtype, topk_weights,
-                                     w_dtype, top_k, out, workspace, workspace_bytes, stream, 0,
-                                     EXQ_LAYER_STAGES);
-}
-
-extern "C" int exq_moe_layer_forward_range(const exq_expert_desc* experts, int32_t n_routed,
-                                           int32_t n_shared, int64_t hidden, int64_t inter,
-                                           const void* hidden_states, int act_dtype,
-                                           int64_t n_tokens, const void* topk_ids, int ids_dtype,
-                                           const void* topk_weights, int w_dtype, int32_t top_k,
-                                           void* out, void* workspace, size_t workspace_bytes,
-                                           void* stream, int32_t first_stage,
-                                           int32_t end_stage) {
-  EXQ_CHECK_ARG(0 <= first_stage && first_stage <= end_stage && end_stage <= EXQ_LAYER_STAGES,
-                "moe_layer: stage range [%d, %d) outside [0, %d)", first_stage, end_stage,
-                EXQ_LAYER_STAGES);
-  EXQ_CHECK_ARG(is_act(act_dtype), "moe_layer: activations must be fp16 or bf16");
-  EXQ_CHECK_ARG(ids_dtype == EXQ_I32 || ids_dtype == EXQ_I64, "moe_layer: ids must be int32/int64");
-  EXQ_CHECK_ARG(w_dtype == EXQ_F32 || is_act(w_dtype), "moe_layer: weights dtype unsupported");
-  EXQ_CHECK_ARG(n_routed > 0 && n_shared >= 0 && top_k > 0 && n_tokens >= 0,
-                "moe_layer: bad sizes");
-  if (hidden <= 0 || hidden % 128 != 0 || inter <= 0 || inter % 128 != 0) {
-    set_error("moe_layer: hidden=%lld and inter=%lld must be positive multiples of 128",
-              (long long)hidden, (long long)inter);
-    return EXQ_ERR_UNSUPPORTED;
-  }
-  EXQ_CHECK_ARG(experts, "moe_layer: experts is null");
-  const int32_t n_total = n_routed + n_shared;
-  const int spt = top_k + n_shared;
-  const int64_t n_slots = n_tokens * spt;
-  const size_t need =
-      exq_moe_layer_workspace_bytes(n_tokens, top_k, n_shared, n_total, hidden, inter);
-  if (!workspace || workspace_bytes < need) {
-    set_error("moe_layer: workspace of %zu bytes needed", need);
-    return EXQ_ERR_WORKSPACE;
-  }
-  if (n_tokens == 0) return EXQ_OK;
-  EXQ_CHECK_ARG(hidden_states && topk_ids && topk_weights && out, "moe_layer: null pointer");
-  auto s = static_cast<cudaStream_t>(stream);
-  LayerWs w = carve(workspace, n_slots, n_total, inter, hidden, true);
-
-  RouteParams rp{};
-  rp.ids = topk_ids;
-  rp.ids_dtype = ids_dtype;
-  rp.n = n_slots;
-  rp.n_buckets = n_total;
-  rp.n_routed = n_routed;
-  rp.top_k = top_k;
-  rp.slots_per_token = spt;
-  rp.mt = kGmMTHost;
-  rp.sorted_i32 = w.sorted_slot;
-  rp.pos_of_slot = w.pos_of_slot;
-  rp.ends = w.ends;
-  rp.tile_info = w.tile_info;
-  rp.n_tiles = w.n_tiles;
-  rp.max_tiles = max_tiles_for(n_slots, n_total);
-  int st = EXQ_OK;
-  if (first_stage <= 0 && end_stage > 0) {
-    st = launch_route(rp, kRouteLayer, s);
-    if (st != EXQ_OK) return st;
-  }
-
-  uint32_t* status = device_status_ptr();
-  GemmParams gp{};
-  gp.experts = experts;
-  gp.proj = 0;
-  gp.mode = kGemmModeGateUp;
-  gp.n_rows = static_cast<int>(2 * inter);
-  gp.k = static_cast<int>(hidden);
-  gp.inter = static_cast<int>(inter);
-  gp.nblocks = static_cast<int>((inter + kGmRBHost / 2 - 1) / (kGmRBHost / 2));
-  gp.act = hidden_states;
-  gp.act_stride = hidden;
-  gp.gather = 1;
-  gp.spt = spt;
-  gp.top_k = top_k;
-  gp.sorted_slot = w.sorted_slot;
-  gp.tile_info = w.tile_info;
-  gp.n_tiles_ptr = w.n_tiles;
-  gp.max_tiles = static_cast<int>(rp.max_tiles);
-  gp.out = w.mid;
-  gp.out_dtype = act_dtype;
-  gp.out_stride = inter;
-  gp.topk_w = topk_weights;
-  gp.w_dtype = w_dtype;
-  gp.status = status;
-  int64_t max_items = rp.max_tiles * gp.nblocks;
-  if (first_stage <= 1 && end_stage > 1) {
-    st = launch_gemm(gp, act_dtype,
-                     static_cast<int>(max_items < INT32_MAX ? max_items : INT32_MAX), s);
-    if (st != EXQ_OK) return st;
-  }
-
-  gp.proj = 1;
-  gp.mode = kGemmModeDown;
-  gp.n_rows = static_cast<int>(hidden);
-  gp.k = static_cast<int>(inter);
-  gp.nblocks = static_cast<int>((hidden + kGmRBHost - 1) / kGmRBHost);
-  gp.act = w.mid;
-  gp.act_stride = inter;
-  gp.gather = 0;
-  gp.out = w.partial;
-  gp.out_dtype = EXQ_F32;
-  gp.out_stride = hidden;
-  max_items = rp.max_tiles * gp.nblocks;
-  if (first_stage <= 2 && end_stage > 2) {
-    st = launch_gemm(gp, act_dtype,
-                     static_cast<int>(max_items < INT32_MAX ? max_items : INT32_MAX), s);
-    if (st != EXQ_OK) return st;
-  }
-  if (first_stage <= 3 && end_stage > 3)
-    return launch_combine_partials(w.partial, hidden, w.pos_of_slot, n_tokens, spt, out,
-                                   act_dtype, s);
-  return EXQ_OK;
-}

@@ -39,6 +39,9 @@ struct RouteParams {
   int64_t* order_i64;          // ENDS/DISPATCH (and LAYER if set): sort_order
   int64_t* sorted_expert_i64;  // DISPATCH
   int32_t* pos_of_slot;        // LAYER: sorted position of every slot, -1 if dropped
+  float* sorted_w;             // LAYER: router weight of the slot at each sorted position
+  const void* topk_w;          // LAYER: router weights [T, top_k] (shared slots weigh 1)
+  int w_dtype;
   int32_t* tile_info;          // LAYER: [max_tiles][3] = expert, first row, rows
   int32_t* n_tiles;            // LAYER: [1]
   int64_t max_tiles;

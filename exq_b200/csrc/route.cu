@@ -230,6 +230,12 @@ __global__ void __launch_bounds__(kRouteThreads, 1) route_kernel(RouteParams p, 
         default:
           p.sorted_i32[pos] = static_cast<int32_t>(val);
           if (p.pos_of_slot) p.pos_of_slot[val] = pos;
+          if (p.sorted_w) {
+            const int64_t t = val / p.slots_per_token;
+            const int j = static_cast<int>(val - t * p.slots_per_token);
+            p.sorted_w[pos] =
+                j < p.top_k ? load_as_f32(p.topk_w, p.w_dtype, t * p.top_k + j) : 1.0f;
+          }
           if (p.order_i64) p.order_i64[pos] = val;
           break;
       }

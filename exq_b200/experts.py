@@ -1,43 +1,56 @@
 """Packed expert weights of one MoE layer (any mix of BF16 / INT8 / INT4) and
 its single-call forward.
 
-An ``ExpertBank`` owns one contiguous tensor set per tier and a device array
-of ``exq_expert_desc`` records (include/exq_b200.h) pointing into them, so a
-layer whose experts follow a compiled quant plan (``quant_assignments``,
+An ``ExpertBank`` owns one contiguous storage per tier plus a device array
+``expert_slot`` (tier << 24 | index inside the tier storage), described to the
+library by ``exq_moe_weights`` (include/exq_b200.h), so a layer whose experts
+follow a compiled quant plan (``quant_assignments``,
 exq/kernels/exq_artifact.py:120-138) runs as one grouped launch per
 projection.  Routed experts come first; ``n_shared`` always-on experts (e.g.
 DeepSeek-V2's shared experts) follow and receive every token with weight 1.
 
-HBM layout per tier (E_t experts of that tier, in expert order):
-  INT4: w13 u8 [E_t, 2I, H/2], w13_scales f16 [E_t, 2I, H/128],
-        w2 u8 [E_t, H, I/2],   w2_scales f16 [E_t, H, I/128]
-  INT8: w13 i8 [E_t, 2I, H], w13_scales f16 [E_t, 2I], w2 i8 [E_t, H, I], w2_scales f16 [E_t, H]
-  BF16: w13 [E_t, 2I, H], w2 [E_t, H, I] in the activation dtype
+HBM layout per tier (n = experts in the tier; "permuted" = inside each octet
+of k the order [0,4,1,5,2,6,3,7], the order the tcgen05 kernel consumes):
+  INT4: w13 u8 [n, 2I, H/2], w2 u8 [n, H, I/2]  (reference nibble format)
+        w13_scales f16 [n, H/128, 2I], w2_scales f16 [n, I/128, H]  (group-major)
+  INT8: w13 i8 [n, 2I, H], w2 i8 [n, H, I] (permuted); scales f16 [n, 2I], [n, H]
+  BF16: w13 f16 [n, 2I, H], w2 f16 [n, H, I] (permuted); 16-bit weights are held
+        as fp16, the operand type of the kernel's matrix products
 """
 from __future__ import annotations
 
+import ctypes as C
 from dataclasses import dataclass, field
 
-import numpy as np
 import torch
 
 from . import _lib as L
 
 TIER_NAMES = {"BF16": L.TIER_BF16, "INT8": L.TIER_INT8, "INT4": L.TIER_INT4}
 GROUP = 128
+OCTET_PERM = (0, 4, 1, 5, 2, 6, 3, 7)
+OCTET_INV = (0, 2, 4, 6, 1, 3, 5, 7)
 
 
-def _desc_rows(tier: int, n: int, tensors, extra_rows=None):
-    """int64 [n, 5] descriptor rows for experts 0..n-1 of one tier tensor set."""
-    w13, s13, w2, s2 = tensors
-    rows = np.zeros((n, 5), dtype=np.int64)
-    rows[:, 0] = tier & 0xFFFFFFFF
-    for j, t in enumerate((w13, s13, w2, s2)):
-        if t is None:
-            continue
-        step = t.stride(0) * t.element_size()
-        rows[:, 1 + j] = t.data_ptr() + np.arange(n, dtype=np.int64) * step
-    return rows
+class MoeWeightsC(C.Structure):
+    """ctypes mirror of ``exq_moe_weights``."""
+    _fields_ = [("n_routed", C.c_int32), ("n_shared", C.c_int32), ("hidden", C.c_int64),
+                ("inter", C.c_int64), ("n_tier", C.c_int32 * 3), ("reserved", C.c_int32),
+                ("w13", C.c_void_p * 3), ("w13_scales", C.c_void_p * 3), ("w2", C.c_void_p * 3),
+                ("w2_scales", C.c_void_p * 3), ("expert_slot", C.c_void_p)]
+
+
+def octet_permute(t: torch.Tensor) -> torch.Tensor:
+    """Reorder every 8-element group of the last dimension to [0,4,1,5,2,6,3,7]."""
+    k = t.shape[-1]
+    idx = torch.tensor(OCTET_PERM, device=t.device)
+    return t.reshape(*t.shape[:-1], k // 8, 8).index_select(-1, idx).reshape(t.shape).contiguous()
+
+
+def octet_unpermute(t: torch.Tensor) -> torch.Tensor:
+    k = t.shape[-1]
+    idx = torch.tensor(OCTET_INV, device=t.device)
+    return t.reshape(*t.shape[:-1], k // 8, 8).index_select(-1, idx).reshape(t.shape).contiguous()
 
 
 def pack_int4(w: torch.Tensor, group_size: int = GROUP):
@@ -60,7 +73,7 @@ def pack_int4(w: torch.Tensor, group_size: int = GROUP):
 
 
 def quant_int8(w: torch.Tensor):
-    """GPU INT8 tier: per-row symmetric, fp16 scale."""
+    """GPU INT8 tier: per-row symmetric, fp16 scale (natural k order)."""
     dev = L.require_cuda(w)
     w = w.contiguous()
     k = w.shape[-1]
@@ -72,9 +85,14 @@ def quant_int8(w: torch.Tensor):
     return q, scales
 
 
+def _int4_storage(packed13, scales13, packed2, scales2):
+    return (packed13.contiguous(), scales13.transpose(-1, -2).contiguous(), packed2.contiguous(),
+            scales2.transpose(-1, -2).contiguous())
+
+
 @dataclass
 class ExpertBank:
-    """Packed experts of one layer plus their device descriptor array."""
+    """Packed experts of one layer in the tcgen05 storage format."""
 
     hidden: int
     inter: int
@@ -83,7 +101,9 @@ class ExpertBank:
     n_shared: int
     tiers: list  # per expert (routed then shared): "BF16" / "INT8" / "INT4"
     storage: dict = field(default_factory=dict)  # tier -> (w13, s13, w2, s2)
-    desc: torch.Tensor | None = None  # int64 [E_total, 5] on device
+    index: dict = field(default_factory=dict)    # tier -> expert ids in storage order
+    expert_slot: torch.Tensor | None = None
+    cstruct: MoeWeightsC | None = None
     _ws: torch.Tensor | None = None
 
     @property
@@ -92,7 +112,7 @@ class ExpertBank:
 
     @property
     def device(self) -> torch.device:
-        return self.desc.device
+        return self.expert_slot.device
 
     # ------------------------------------------------------------ builders
     @classmethod
@@ -113,6 +133,8 @@ class ExpertBank:
         tiers = list(tiers) if tiers is not None else ["INT4"] * e
         if len(tiers) != e:
             raise ValueError("one tier per routed expert")
+        if any(t not in TIER_NAMES for t in tiers):
+            raise ValueError(f"unknown tier in {sorted(set(tiers))}")
         all_w13, all_w2 = w13, w2
         n_shared = 0
         if shared_w13 is not None:
@@ -129,20 +151,27 @@ class ExpertBank:
             idx = torch.tensor(sel, device=w13.device)
             a, b = all_w13.index_select(0, idx), all_w2.index_select(0, idx)
             if name == "INT4":
-                bank.storage[name] = (*pack_int4(a), *pack_int4(b))
+                bank.storage[name] = _int4_storage(*pack_int4(a), *pack_int4(b))
             elif name == "INT8":
-                bank.storage[name] = (*quant_int8(a), *quant_int8(b))
+                qa, sa = quant_int8(a)
+                qb, sb = quant_int8(b)
+                bank.storage[name] = (octet_permute(qa), sa, octet_permute(qb), sb)
             else:
-                bank.storage[name] = (a.to(act_dtype).contiguous(), None,
-                                      b.to(act_dtype).contiguous(), None)
-            bank.storage[name + "_index"] = sel
-        bank._build_desc(w13.device)
+                bank.storage[name] = (octet_permute(a.to(torch.float16)), None,
+                                      octet_permute(b.to(torch.float16)), None)
+            bank.index[name] = sel
+            del a, b
+        bank._finalize(w13.device)
         return bank
 
     @classmethod
     def from_int4_packed(cls, w13_packed, w13_scales, w2_packed, w2_scales,
                          act_dtype: torch.dtype = torch.float16):
-        """Wrap already-packed INT4 tensors (reference format) without copying."""
+        """Wrap reference-format INT4 tensors (packed u8 + [E, N, K/128] scales).
+
+        The packed weights are used in place; only the (1/32-size) scales are
+        copied into the group-major order the kernel reads.
+        """
         L.require_cuda(w13_packed, w13_scales, w2_packed, w2_scales)
         e, i2, h2 = w13_packed.shape
         h = h2 * 2
@@ -152,24 +181,46 @@ class ExpertBank:
             if tuple(t.shape) != shape:
                 raise NotImplementedError(
                     f"expected {shape} for group size {GROUP}, got {tuple(t.shape)}")
-            if not t.is_contiguous():
-                raise ValueError("packed weights must be contiguous")
         bank = cls(hidden=h, inter=inter, act_dtype=act_dtype, n_routed=e, n_shared=0,
                    tiers=["INT4"] * e)
-        bank.storage["INT4"] = (w13_packed, w13_scales, w2_packed, w2_scales)
-        bank.storage["INT4_index"] = list(range(e))
-        bank._build_desc(w13_packed.device)
+        bank.storage["INT4"] = _int4_storage(w13_packed, w13_scales, w2_packed, w2_scales)
+        bank.index["INT4"] = list(range(e))
+        bank._finalize(w13_packed.device)
         return bank
 
-    def _build_desc(self, device):
-        rows = np.zeros((self.n_total, 5), dtype=np.int64)
-        rows[:, 0] = L.TIER_NONE & 0xFFFFFFFF
+    def _finalize(self, device):
+        slot = [-1] * self.n_total
+        for name, sel in self.index.items():
+            for j, e in enumerate(sel):
+                slot[e] = (TIER_NAMES[name] << 24) | j
+        self.expert_slot = torch.tensor(slot, dtype=torch.int32, device=device)
+        cs = MoeWeightsC()
+        cs.n_routed, cs.n_shared = self.n_routed, self.n_shared
+        cs.hidden, cs.inter = self.hidden, self.inter
         for name, code in TIER_NAMES.items():
-            if name not in self.storage:
+            st = self.storage.get(name)
+            cs.n_tier[code] = len(self.index.get(name, []))
+            if st is None:
                 continue
-            sel = self.storage[name + "_index"]
-            rows[sel] = _desc_rows(code, len(sel), self.storage[name])
-        self.desc = torch.from_numpy(rows).to(device)
+            w13, s13, w2, s2 = st
+            cs.w13[code], cs.w2[code] = w13.data_ptr(), w2.data_ptr()
+            cs.w13_scales[code] = s13.data_ptr() if s13 is not None else None
+            cs.w2_scales[code] = s2.data_ptr() if s2 is not None else None
+        cs.expert_slot = self.expert_slot.data_ptr()
+        self.cstruct = cs
+
+    # ------------------------------------------------------------ inspection
+    def expert_reference_format(self, e: int):
+        """Expert ``e`` in the reference's layouts: INT4 -> (packed, scales [N, K/128])
+        per projection, INT8 -> (q natural order, row scales), BF16 -> fp16 tensors."""
+        tier = self.tiers[e]
+        j = self.index[tier].index(e)
+        w13, s13, w2, s2 = self.storage[tier]
+        if tier == "INT4":
+            return tier, (w13[j], s13[j].transpose(0, 1)), (w2[j], s2[j].transpose(0, 1))
+        if tier == "INT8":
+            return tier, (octet_unpermute(w13[j]), s13[j]), (octet_unpermute(w2[j]), s2[j])
+        return tier, octet_unpermute(w13[j]), octet_unpermute(w2[j])
 
     def weight_bytes(self, expert: int) -> int:
         """HBM bytes one call streams for this expert when it is touched."""
@@ -192,31 +243,40 @@ class ExpertBank:
         if self._ws is None or self._ws.numel() < need:
             self._ws = L.workspace(self.device, need)
 
-    def forward(self, hidden_states: torch.Tensor, topk_ids: torch.Tensor,
-                topk_weights: torch.Tensor, out: torch.Tensor | None = None,
-                workspace: torch.Tensor | None = None) -> torch.Tensor:
-        """route -> gate_up -> SiLU*mul -> down -> weighted combine, in 4 launches."""
+    def _args(self, hidden_states, topk_ids, topk_weights, out, workspace):
         dev = L.require_cuda(hidden_states, topk_ids, topk_weights)
-        if hidden_states.dtype != self.act_dtype:
-            raise ValueError(f"hidden_states must be {self.act_dtype}")
+        if hidden_states.dtype not in (torch.float16, torch.bfloat16):
+            raise ValueError("hidden_states must be fp16 or bf16")
         x = hidden_states.contiguous()
         t = x.shape[0]
-        if x.shape[1] != self.hidden:
-            raise ValueError("hidden size mismatch")
+        if x.dim() != 2 or x.shape[1] != self.hidden:
+            raise ValueError("hidden_states must be [T, hidden]")
         ids = topk_ids.contiguous()
         w = topk_weights.contiguous()
         if ids.dim() != 2 or ids.shape != w.shape or ids.shape[0] != t:
             raise ValueError("topk_ids / topk_weights must both be [T, k]")
         k = ids.shape[1]
         if out is None:
-            out = torch.empty(t, self.hidden, dtype=self.act_dtype, device=dev)
+            out = torch.empty(t, self.hidden, dtype=x.dtype, device=dev)
         if workspace is None:
             self.reserve(t, k)
             workspace = self._ws
-        L.check(L.lib().exq_moe_layer_forward(
-            L.ptr(self.desc), self.n_routed, self.n_shared, self.hidden, self.inter, L.ptr(x),
-            L.tag(x), t, L.ptr(ids), L.tag(ids), L.ptr(w), L.tag(w), k, L.ptr(out),
-            L.ptr(workspace), workspace.numel(), L.stream_of(dev)), "moe_layer_forward")
+        return dev, x, ids, w, k, out, workspace
+
+    def forward(self, hidden_states: torch.Tensor, topk_ids: torch.Tensor,
+                topk_weights: torch.Tensor, out: torch.Tensor | None = None,
+                workspace: torch.Tensor | None = None) -> torch.Tensor:
+        """route -> prep -> gate_up -> down -> weighted combine (5 launches)."""
+        return self.forward_range(hidden_states, topk_ids, topk_weights, 0, 5, out, workspace)
+
+    def forward_range(self, hidden_states, topk_ids, topk_weights, first: int, end: int,
+                      out=None, workspace=None):
+        dev, x, ids, w, k, out, workspace = self._args(hidden_states, topk_ids, topk_weights, out,
+                                                      workspace)
+        L.check(L.lib().exq_moe_layer_forward_range(
+            C.byref(self.cstruct), L.ptr(x), L.tag(x), x.shape[0], L.ptr(ids), L.tag(ids), L.ptr(w),
+            L.tag(w), k, L.ptr(out), L.ptr(workspace), workspace.numel(), L.stream_of(dev),
+            first, end), "moe_layer_forward")
         return out
 
     __call__ = forward

@@ -65,6 +65,7 @@ extern "C" {
 #define EXQ_DEV_BAD_EXPERT_ID 1u /* an id outside [0, n_experts) was dropped */
 #define EXQ_DEV_BAD_SLOT 2u      /* a sort_order / slot entry was out of range */
 #define EXQ_DEV_BAD_TIER 4u      /* an expert descriptor had an unknown tier */
+#define EXQ_DEV_TIMEOUT 8u       /* a pipeline wait gave up (the kernel unwound) */
 
 EXQ_API int exq_abi_version(void);
 EXQ_API const char* exq_last_error(void);
@@ -174,34 +175,59 @@ EXQ_API int exq_moe_gemm(const exq_expert_desc* experts, int32_t n_experts, int6
                  int out_dtype, int64_t* sort_order_out, int32_t* expert_ends_out,
                  void* workspace, size_t workspace_bytes, void* stream);
 
+/* Packed weights of one MoE layer for the tcgen05 path, one contiguous
+ * storage per tier.  Experts [0, n_routed) are routed; [n_routed,
+ * n_routed + n_shared) are shared experts applied to every token with weight 1.
+ * expert_slot (device, int32 [n_routed + n_shared]) = tier << 24 | index of
+ * the expert inside its tier storage.  Layouts (H = hidden, I = inter; inside
+ * each 8-element octet of k the "permuted" order is [0,4,1,5,2,6,3,7]):
+ *   INT4: w13 u8 [n, 2I, H/2] and w2 u8 [n, H, I/2] in the reference nibble
+ *         format (moe_int4_kernel.py:37-93); scales f16 group-major
+ *         w13_scales [n, H/128, 2I], w2_scales [n, I/128, H]
+ *   INT8: w13 i8 [n, 2I, H], w2 i8 [n, H, I], bytes octet-permuted; per-row f16
+ *         scales w13_scales [n, 2I], w2_scales [n, H]
+ *   BF16: w13 f16 [n, 2I, H], w2 f16 [n, H, I], octet-permuted; no scales
+ * Requirements: H % 128 == 0, I % 128 == 0, every storage pointer 16-byte
+ * aligned. */
+typedef struct exq_moe_weights {
+  int32_t n_routed;
+  int32_t n_shared;
+  int64_t hidden;
+  int64_t inter;
+  int32_t n_tier[3];            /* experts per tier storage, indexed by EXQ_TIER_* */
+  int32_t reserved;
+  const void* w13[3];
+  const void* w13_scales[3];
+  const void* w2[3];
+  const void* w2_scales[3];
+  const int32_t* expert_slot;
+} exq_moe_weights;
+
 /* The whole MoE layer of exq/runtime/sglang_backend.py:65-158 (and
- * moe_int4_full_forward, moe_int4_kernel.py:330-426): route -> gate_up
- * (gather fused) -> SiLU*mul (fused epilogue) -> down -> top-k weighted
- * combine, for a layer whose experts may mix the BF16/INT8/INT4 tiers.
- * `experts` holds n_routed + n_shared descriptors; experts
- * [n_routed, n_routed + n_shared) are shared experts applied to every token
- * with weight 1.  hidden/out: [n_tokens, hidden] in act_dtype;
- * topk_ids [n_tokens, top_k] (int32/int64), topk_weights [n_tokens, top_k]
- * (f32/f16/bf16).  Four launches, no host synchronisation. */
+ * moe_int4_full_forward, moe_int4_kernel.py:330-426): route -> activation
+ * prep (gather + fp16 + octet permutation) -> gate_up tcgen05 grouped GEMM with
+ * fused SiLU*mul -> down tcgen05 grouped GEMM writing router-weighted fp32
+ * partials -> deterministic top-k combine.  The experts may mix the three
+ * tiers.  hidden_states/out: [n_tokens, hidden] (fp16 or bf16; the matrix
+ * products run on fp16 operands with fp32 accumulation, as the reference's
+ * kernel does); topk_ids [n_tokens, top_k] int32/int64; topk_weights
+ * [n_tokens, top_k] f32/f16/bf16.  Five launches, no host synchronisation. */
 EXQ_API size_t exq_moe_layer_workspace_bytes(int64_t n_tokens, int32_t top_k, int32_t n_shared,
-                                     int32_t n_experts_total, int64_t hidden,
-                                     int64_t inter);
-EXQ_API int exq_moe_layer_forward(const exq_expert_desc* experts, int32_t n_routed,
-                          int32_t n_shared, int64_t hidden, int64_t inter,
-                          const void* hidden_states, int act_dtype, int64_t n_tokens,
-                          const void* topk_ids, int ids_dtype, const void* topk_weights,
-                          int w_dtype, int32_t top_k, void* out, void* workspace,
-                          size_t workspace_bytes, void* stream);
+                                             int32_t n_experts_total, int64_t hidden,
+                                             int64_t inter);
+EXQ_API int exq_moe_layer_forward(const exq_moe_weights* weights, const void* hidden_states,
+                                  int act_dtype, int64_t n_tokens, const void* topk_ids,
+                                  int ids_dtype, const void* topk_weights, int w_dtype,
+                                  int32_t top_k, void* out, void* workspace,
+                                  size_t workspace_bytes, void* stream);
 
 /* The same layer, launching only its stages [first_stage, end_stage):
- * 0 = route (sort + tile list), 1 = gate_up grouped GEMM with fused gather and
- * SiLU*mul, 2 = down grouped GEMM writing weighted fp32 partials,
- * 3 = top-k combine.  Stages communicate through `workspace`, so a caller may
- * run them separately on one stream (per-kernel timing) as long as the
- * arguments are identical; exq_moe_layer_forward = stages [0, 4). */
-#define EXQ_LAYER_STAGES 4
-EXQ_API int exq_moe_layer_forward_range(const exq_expert_desc* experts, int32_t n_routed,
-                                        int32_t n_shared, int64_t hidden, int64_t inter,
+ * 0 = route (sort + tile list), 1 = activation prep, 2 = gate_up GEMM,
+ * 3 = down GEMM, 4 = top-k combine.  Stages communicate through `workspace`,
+ * so a caller may run them separately on one stream (per-kernel timing) with
+ * identical arguments; exq_moe_layer_forward = stages [0, 5). */
+#define EXQ_LAYER_STAGES 5
+EXQ_API int exq_moe_layer_forward_range(const exq_moe_weights* weights,
                                         const void* hidden_states, int act_dtype,
                                         int64_t n_tokens, const void* topk_ids, int ids_dtype,
                                         const void* topk_weights, int w_dtype, int32_t top_k,

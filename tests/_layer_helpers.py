@@ -8,28 +8,22 @@ from oracle import quant as OQ
 
 def oracle_expert_fn(bank):
     """e -> fp32 (w13, w2) dequantised on the CPU from the bank's packed tiers."""
-    index = {}
-    for name in ("INT4", "INT8", "BF16"):
-        if name in bank.storage:
-            for j, e in enumerate(bank.storage[name + "_index"]):
-                index[e] = (name, j)
     cache = {}
 
     def fn(e):
         if e in cache:
             return cache[e]
-        name, j = index[e]
-        w13, s13, w2, s2 = bank.storage[name]
-        if name == "INT4":
-            a = OQ.dequant_int4(w13[j].cpu().numpy(), s13[j].cpu().numpy())
-            b = OQ.dequant_int4(w2[j].cpu().numpy(), s2[j].cpu().numpy())
-        elif name == "INT8":
-            a = OQ.dequant_int8(w13[j].cpu().numpy(), s13[j].cpu().numpy())
-            b = OQ.dequant_int8(w2[j].cpu().numpy(), s2[j].cpu().numpy())
+        tier, a, b = bank.expert_reference_format(e)
+        if tier == "INT4":
+            wa = OQ.dequant_int4(a[0].cpu().numpy(), a[1].cpu().numpy())
+            wb = OQ.dequant_int4(b[0].cpu().numpy(), b[1].cpu().numpy())
+        elif tier == "INT8":
+            wa = OQ.dequant_int8(a[0].cpu().numpy(), a[1].cpu().numpy())
+            wb = OQ.dequant_int8(b[0].cpu().numpy(), b[1].cpu().numpy())
         else:
-            a = w13[j].float().cpu().numpy()
-            b = w2[j].float().cpu().numpy()
-        out = (torch.from_numpy(np.asarray(a, np.float32)), torch.from_numpy(np.asarray(b, np.float32)))
+            wa = a.float().cpu().numpy()
+            wb = b.float().cpu().numpy()
+        out = (torch.from_numpy(np.asarray(wa, np.float32)), torch.from_numpy(np.asarray(wb, np.float32)))
         if len(cache) < 16:
             cache[e] = out
         return out

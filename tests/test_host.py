@@ -43,11 +43,23 @@ def test_invalid_arguments_rejected_on_host(lib_path):
     # unsupported group size for the GEMM
     assert lib.exq_moe_gemm(1, 4, 64, 96, 1, L.F16, 2, 1, L.I32, 2, 1, L.F16, None, None, 1,
                             1 << 20, None) == -2
-    # workspace too small
+    # workspace too small, unsupported inter, bad stage range
+    from exq_b200.experts import MoeWeightsC
     need = lib.exq_moe_layer_workspace_bytes(4, 2, 0, 8, 256, 256)
     assert need > 0
-    assert lib.exq_moe_layer_forward(1, 8, 0, 256, 256, 1, L.F16, 4, 1, L.I32, 1, L.F32, 2, 1, 1,
+    w = MoeWeightsC()
+    w.n_routed, w.hidden, w.inter = 8, 256, 256
+    w.n_tier[2] = 8
+    w.w13[2] = w.w2[2] = w.w13_scales[2] = w.w2_scales[2] = 256
+    w.expert_slot = 256
+    assert lib.exq_moe_layer_forward(C.byref(w), 1, L.F16, 4, 1, L.I32, 1, L.F32, 2, 1, 1,
                                      need - 1, None) == -4
+    w.inter = 96
+    assert lib.exq_moe_layer_forward(C.byref(w), 1, L.F16, 4, 1, L.I32, 1, L.F32, 2, 1, 1,
+                                     1 << 30, None) == -2
+    w.inter = 256
+    assert lib.exq_moe_layer_forward_range(C.byref(w), 1, L.F16, 4, 1, L.I32, 1, L.F32, 2, 1, 1,
+                                           1 << 30, None, 3, 9) == -1
 
 
 def test_workspace_sizes_grow_with_tokens(lib_path):
