@@ -12,7 +12,7 @@
 #include <stdio.h>
 #include <stdarg.h>
 
-#include "../../include/exq_b200.h"
+#include "exq_b200.h"
 
 #if defined(__CUDA_ARCH__) && (__CUDA_ARCH__ < 1000)
 #error "exq_b200 is built for sm_100a (B200) only"

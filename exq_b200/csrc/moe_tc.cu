@@ -6,28 +6,36 @@
 // exq/runtime/sglang_backend.py:117-156) for experts that mix BF16, INT8 and
 // INT4 weight tiers.
 //
-// One persistent CTA per SM (480 threads, 15 warps):
-//   warp 0       weight producer: TMA 2D loads of packed weights (+ INT4 group
-//                scales) into a 12-slot ring of 4 KB slots
+// One persistent CTA per SM (736 threads, 23 warps):
+//   warp 0       weight producer: one TMA per 16 KB slot brings 128 weight rows
+//                x 256 k (INT4; INT8 128 k, 16-bit 64 k) into a 6-slot smem
+//                ring, plus one TMA for the INT4 group scales of the slot
 //   warp 1       activation producer: TMA 2D loads (128B swizzle) of the
-//                item's token rows into a 3-slot ring (<= 256 rows x 64 k)
-//   warp 2       MMA issuer: one thread issues tcgen05.mma (M=128, N=tokens,
-//                K=16) into a double-buffered TMEM accumulator (2 x 256 cols)
+//                item's token rows into a 4-slot ring of 16 KB slots; a slot
+//                holds 128/N k-stages of N rows, so small items prefetch deep
+//   warp 2       MMA issuer: one thread issues tcgen05.mma with A (weights) in
+//                tensor memory and B (tokens) in shared memory, M=128 rows,
+//                N=tokens, K=16, into a double-buffered accumulator
 //   warps 3-6    epilogue: tcgen05.ld of the accumulator, fused SiLU*mul
 //                (gate_up) or router-weighted fp32 partials (down)
-//   warps 7-14   dequantisers: packed weights -> fp16 (scale applied) written
-//                into the 128B-swizzled K-major A tile the MMA reads
-// A work item is (expert, 128-row block of the projection, up to 256 tokens
+//   warps 7-22   dequantisers: warp (lane quarter q, k-slice j) turns, for every
+//                weight slot, 64 k of the 32 rows of quarter q into fp16 (scale
+//                applied) in registers and writes them to its tensor-memory
+//                lanes with one tcgen05.st; a slot is one "super-stage"
+//                (INT4 256 k, INT8 128 k, 16-bit 64 k) of the A operand
+// A work item is (expert, 128-row block of the projection, up to 128 tokens
 // of that expert): every weight byte is dequantised once per item and all the
-// expert's tokens ride in the MMA's N dimension, so hot experts do not re-read
-// or re-dequantise weights.
+// expert's tokens ride in the MMA's N dimension.
+//
+// Tensor memory (512 columns): accumulators at [0,128) and [128,256); two A
+// buffers of 128 columns (128 rows x 256 fp16) at [256,512).
 //
 // K order.  Inside every 8-element octet the k order is permuted to
 // [0,4,1,5,2,6,3,7] identically for weights and activations (a dot product
 // does not depend on term order).  With it a packed INT4 word dequantises with
-// the 1024.0 magic-number trick straight into K-adjacent fp16 pairs (4 LOP3 +
-// 2 HSUB2 + 2 HFMA2 per 8 weights), the INT8 / 16-bit tiers are stored
-// pre-permuted at pack time, and the activation prep kernel permutes rows.
+// the 1024.0 magic-number trick straight into K-adjacent fp16 pairs, the INT8
+// and 16-bit tiers are stored pre-permuted at pack time, and the activation
+// prep kernel permutes rows.
 #include <string.h>
 
 #include <type_traits>
@@ -37,24 +45,24 @@
 namespace exq {
 namespace tc {
 
-constexpr int kWarps = 15;
+constexpr int kWarps = 23;
 constexpr int kThreads = kWarps * 32;
 constexpr int kWarpW = 0, kWarpB = 1, kWarpMma = 2;
 constexpr int kEpiWarp0 = 3, kNumEpiWarps = 4;
-constexpr int kDqWarp0 = 7, kNumDqWarps = 8;
-constexpr int kDqThreads = kNumDqWarps * 32;
-constexpr int kWStages = 12, kAStages = 3, kBStages = 3;
-constexpr int kWSlot = 4096, kSSlot = 256, kASlot = 16384, kBSlot = 32768;
-constexpr int kMaxN = 256;
+constexpr int kDqWarp0 = 7, kNumDqWarps = 16;  // 4 lane quarters x 4 k-slices of 64
+constexpr int kWStages = 6, kABufs = 2, kBStages = 4;  // weight slots, TMEM A buffers, B slots
+constexpr int kWSlot = 16384, kSSlot = 512, kBSlot = 16384;
+constexpr int kACols = 128;  // tensor-memory columns per A buffer (128 rows x 256 fp16)
+constexpr int kMaxN = 128;       // tokens per item (the MMA's N)
 constexpr int kTmemCols = 512;
-constexpr int kKS = 64;  // k per pipeline stage (one 128B swizzle atom of fp16)
+constexpr int kTmemA = 256;      // first tensor-memory column of the A buffers
+constexpr int kKS = 64;          // k per pipeline stage
 
-constexpr int kOffA = 0;
-constexpr int kOffB = kOffA + kAStages * kASlot;
+constexpr int kOffB = 0;
 constexpr int kOffW = kOffB + kBStages * kBSlot;
 constexpr int kOffS = kOffW + kWStages * kWSlot;
 constexpr int kOffBar = kOffS + kWStages * kSSlot;
-constexpr int kNumBars = 2 * kWStages + 2 * kAStages + 2 * kBStages + 4;
+constexpr int kNumBars = 2 * kWStages + 2 * kABufs + 2 * kBStages + 4;
 constexpr int kOffMisc = kOffBar + kNumBars * 8;
 constexpr int kSmemBytes = kOffMisc + 64 + 1024;  // + slack to align the base to 1024 B
 
@@ -63,7 +71,7 @@ enum : int { kTierBF16 = EXQ_TIER_BF16, kTierINT8 = EXQ_TIER_INT8, kTierINT4 = E
 struct TcParams {
   CUtensorMap tm_w[3];  // weights of this projection per tier storage
   CUtensorMap tm_s;     // INT4 group scales (group-major) of this projection
-  CUtensorMap tm_b;     // activations [n_pos, k] fp16, octet-permuted
+  CUtensorMap tm_b[4];  // activations [n_pos, k] fp16, octet-permuted; box rows 16/32/64/128
   const int32_t* expert_slot;  // tier << 24 | index inside the tier storage
   const int32_t* tile_info;
   const int32_t* n_tiles_ptr;
@@ -98,8 +106,9 @@ __device__ __forceinline__ bool decode_item(const TcParams& p, int item, int n_t
   return it.tier == kTierINT4 || it.tier == kTierINT8 || it.tier == kTierBF16;
 }
 
-__device__ __forceinline__ int wslots_of(int tier) {
-  return tier == kTierINT4 ? 1 : (tier == kTierINT8 ? 2 : 4);
+// k-stages (64 k each) carried by one 16 KB weight slot: 128 rows x 128 bytes.
+__device__ __forceinline__ int stages_per_slot(int tier) {
+  return tier == kTierINT4 ? 4 : (tier == kTierINT8 ? 2 : 1);
 }
 
 struct Ring {
@@ -119,7 +128,7 @@ __device__ __forceinline__ int perm_pos(int o) {
 
 // INT4: one packed word (8 weights, reference nibble order) -> 4 fp16 pairs in
 // permuted octet order, each multiplied by the group scale.
-__device__ __forceinline__ uint4 dq_int4_word(uint32_t w, __half2 s) {
+__device__ __forceinline__ void dq_int4_word(uint32_t w, __half2 s, uint32_t* o) {
   const __half2 sub = __float2half2_rn(1032.0f);
   const __half2 mul16 = __float2half2_rn(0.0625f);
   const __half2 add72 = __float2half2_rn(-72.0f);
@@ -132,34 +141,52 @@ __device__ __forceinline__ uint4 dq_int4_word(uint32_t w, __half2 s) {
   __half2 h1 = __hmul2(__hfma2(*reinterpret_cast<__half2*>(&r1), mul16, add72), s);
   __half2 h2 = __hmul2(__hsub2(*reinterpret_cast<__half2*>(&r2), sub), s);
   __half2 h3 = __hmul2(__hfma2(*reinterpret_cast<__half2*>(&r3), mul16, add72), s);
-  uint4 o;
-  o.x = *reinterpret_cast<uint32_t*>(&h0);
-  o.y = *reinterpret_cast<uint32_t*>(&h1);
-  o.z = *reinterpret_cast<uint32_t*>(&h2);
-  o.w = *reinterpret_cast<uint32_t*>(&h3);
-  return o;
+  o[0] = *reinterpret_cast<uint32_t*>(&h0);
+  o[1] = *reinterpret_cast<uint32_t*>(&h1);
+  o[2] = *reinterpret_cast<uint32_t*>(&h2);
+  o[3] = *reinterpret_cast<uint32_t*>(&h3);
 }
 
 // INT8 (bytes stored in permuted octet order): 4 weights -> 2 fp16 pairs.
-__device__ __forceinline__ uint2 dq_int8_word(uint32_t w) {
+__device__ __forceinline__ void dq_int8_word(uint32_t w, uint32_t* o) {
   const uint32_t u = w ^ 0x80808080u;
   uint32_t a = prmt(u, 0x64646464u, 0x4140u);
   uint32_t b = prmt(u, 0x64646464u, 0x4342u);
   const __half2 sub = __float2half2_rn(1152.0f);
   __half2 ha = __hsub2(*reinterpret_cast<__half2*>(&a), sub);
   __half2 hb = __hsub2(*reinterpret_cast<__half2*>(&b), sub);
-  return make_uint2(*reinterpret_cast<uint32_t*>(&ha), *reinterpret_cast<uint32_t*>(&hb));
+  o[0] = *reinterpret_cast<uint32_t*>(&ha);
+  o[1] = *reinterpret_cast<uint32_t*>(&hb);
 }
 
-__device__ __forceinline__ void sts128(uint32_t addr, uint4 v) {
-  asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};\n" ::"r"(addr), "r"(v.x), "r"(v.y),
-               "r"(v.z), "r"(v.w)
-               : "memory");
-}
 __device__ __forceinline__ uint16_t lds16(uint32_t addr) {
   uint16_t v;
   asm volatile("ld.shared.u16 %0, [%1];\n" : "=h"(v) : "r"(addr));
   return v;
+}
+
+// 32 lanes x 32 consecutive 32-bit columns from registers to tensor memory.
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&v)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"
+      "%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};\n" ::"r"(taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]),
+      "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]),
+      "r"(v[16]), "r"(v[17]), "r"(v[18]), "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]),
+      "r"(v[23]), "r"(v[24]), "r"(v[25]), "r"(v[26]), "r"(v[27]), "r"(v[28]), "r"(v[29]),
+      "r"(v[30]), "r"(v[31]));
+}
+__device__ __forceinline__ void tmem_wait_st() {
+  asm volatile("tcgen05.wait::st.sync.aligned;\n" ::: "memory");
+}
+// A from tensor memory, B from shared memory.
+__device__ __forceinline__ void tc_mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
+                                              uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n"
+      " setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}\n" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate));
 }
 
 __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_constant__ TcParams p) {
@@ -167,18 +194,18 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
   uint8_t* gbase = smem_raw + (base - raw);
-  const uint32_t sA = base + kOffA, sB = base + kOffB, sW = base + kOffW, sS = base + kOffS;
+  const uint32_t sB = base + kOffB, sW = base + kOffW, sS = base + kOffS;
   const uint32_t bar0 = base + kOffBar;
   auto W_full = [&](int i) { return bar0 + 8u * i; };
   auto W_empty = [&](int i) { return bar0 + 8u * (kWStages + i); };
-  auto A_full = [&](int i) { return bar0 + 8u * (2 * kWStages + i); };
-  auto A_empty = [&](int i) { return bar0 + 8u * (2 * kWStages + kAStages + i); };
-  auto B_full = [&](int i) { return bar0 + 8u * (2 * kWStages + 2 * kAStages + i); };
-  auto B_empty = [&](int i) { return bar0 + 8u * (2 * kWStages + 2 * kAStages + kBStages + i); };
-  auto Acc_full = [&](int i) { return bar0 + 8u * (2 * kWStages + 2 * kAStages + 2 * kBStages + i); };
-  auto Acc_empty = [&](int i) {
-    return bar0 + 8u * (2 * kWStages + 2 * kAStages + 2 * kBStages + 2 + i);
-  };
+  constexpr int kBarA = 2 * kWStages, kBarAe = kBarA + kABufs, kBarB = kBarAe + kABufs;
+  constexpr int kBarAcc = kBarB + 2 * kBStages;
+  auto A_full = [&](int i) { return bar0 + 8u * (kBarA + i); };
+  auto A_empty = [&](int i) { return bar0 + 8u * (kBarAe + i); };
+  auto B_full = [&](int i) { return bar0 + 8u * (kBarB + i); };
+  auto B_empty = [&](int i) { return bar0 + 8u * (kBarB + kBStages + i); };
+  auto Acc_full = [&](int i) { return bar0 + 8u * (kBarAcc + i); };
+  auto Acc_empty = [&](int i) { return bar0 + 8u * (kBarAcc + 2 + i); };
   volatile uint32_t* misc = reinterpret_cast<volatile uint32_t*>(gbase + kOffMisc);
   // misc[0] = TMEM base address, misc[1] = abort flag
 
@@ -189,10 +216,10 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
   if (threadIdx.x == 0) {
     for (int i = 0; i < kWStages; ++i) {
       mbar_init(W_full(i), 1);
-      mbar_init(W_empty(i), 1);
+      mbar_init(W_empty(i), kNumDqWarps);
     }
-    for (int i = 0; i < kAStages; ++i) {
-      mbar_init(A_full(i), 1);
+    for (int i = 0; i < kABufs; ++i) {
+      mbar_init(A_full(i), kNumDqWarps);
       mbar_init(A_empty(i), 1);
     }
     for (int i = 0; i < kBStages; ++i) {
@@ -230,42 +257,34 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
           continue;
         }
         const int nk = p.k / kKS;
-        const int ns = wslots_of(it.tier);
-        const int rows = p.n_rows;
-        for (int kc = 0; kc < nk && !aborted(); ++kc) {
-          for (int q = 0; q < ns; ++q) {
-            if (!mbar_wait(W_empty(r.idx), r.phase ^ 1, p.status)) {
-              do_abort();
-              break;
-            }
-            const uint32_t dst = sW + r.idx * kWSlot, bar = W_full(r.idx);
-            if (it.tier == kTierINT4) {
-              mbar_arrive_tx(bar, kWSlot + kSSlot);
-              const int ybase = it.idx * rows;
-              const int y0 = ybase + (p.gate_up ? it.r0 : it.r0);
-              const int y1 = ybase + (p.gate_up ? p.inter + it.r0 : it.r0 + 64);
-              tma_load_2d(dst, &p.tm_w[kTierINT4], bar, kc * 32, y0);
-              tma_load_2d(dst + 2048, &p.tm_w[kTierINT4], bar, kc * 32, y1);
-              const int ys = it.idx * G + (kc >> 1);
-              const int xs0 = it.r0;
-              const int xs1 = p.gate_up ? p.inter + it.r0 : it.r0 + 64;
-              tma_load_2d(sS + r.idx * kSSlot, &p.tm_s, bar, xs0, ys);
-              tma_load_2d(sS + r.idx * kSSlot + 128, &p.tm_s, bar, xs1, ys);
-            } else if (it.tier == kTierINT8) {
-              mbar_arrive_tx(bar, kWSlot);
-              const int y = it.idx * rows +
-                            (p.gate_up ? (q ? p.inter : 0) + it.r0 : it.r0 + 64 * q);
-              tma_load_2d(dst, &p.tm_w[kTierINT8], bar, kc * 64, y);
-            } else {
-              mbar_arrive_tx(bar, kWSlot);
-              const int y = it.idx * rows +
-                            (p.gate_up ? (q >= 2 ? p.inter : 0) + it.r0 + 32 * (q & 1)
-                                       : it.r0 + 32 * q);
-              tma_load_2d(dst, &p.tm_w[kTierBF16], bar, kc * 64, y);
-            }
-            r.next(kWStages);
-            ++issued;
+        const int sps = stages_per_slot(it.tier);
+        for (int kc0 = 0; kc0 < nk && !aborted(); kc0 += sps) {
+          if (!mbar_wait(W_empty(r.idx), r.phase ^ 1, p.status)) {
+            do_abort();
+            break;
           }
+          const uint32_t dst = sW + r.idx * kWSlot, bar = W_full(r.idx);
+          const int xb = kc0 * (it.tier == kTierINT4 ? 32 : (it.tier == kTierINT8 ? 64 : 64));
+          if (it.tier == kTierINT4) {
+            mbar_arrive_tx(bar, kWSlot + kSSlot);
+            if (p.gate_up) {
+              // weights: (byte, row in block, block, gate/up, expert)
+              tma_load_5d(dst, &p.tm_w[kTierINT4], bar, xb, 0, it.nb, 0, it.idx);
+              // scales: (element in block, block, gate/up, group, expert); 2 groups
+              tma_load_5d(sS + r.idx * kSSlot, &p.tm_s, bar, 0, it.nb, 0, kc0 >> 1, it.idx);
+            } else {
+              tma_load_2d(dst, &p.tm_w[kTierINT4], bar, xb, it.idx * p.n_rows + it.r0);
+              tma_load_2d(sS + r.idx * kSSlot, &p.tm_s, bar, it.r0, it.idx * G + (kc0 >> 1));
+            }
+          } else {
+            mbar_arrive_tx(bar, kWSlot);
+            if (p.gate_up)
+              tma_load_5d(dst, &p.tm_w[it.tier], bar, xb, 0, it.nb, 0, it.idx);
+            else
+              tma_load_2d(dst, &p.tm_w[it.tier], bar, xb, it.idx * p.n_rows + it.r0);
+          }
+          r.next(kWStages);
+          ++issued;
         }
       }
       if (aborted()) {  // let in-flight copies land before the CTA exits
@@ -286,16 +305,27 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
         Item it;
         if (!decode_item(p, item, n_tiles, it)) continue;
         const int nk = p.k / kKS;
-        const int nbox = (it.mc + 31) >> 5;
-        for (int kc = 0; kc < nk; ++kc) {
+        const int per_slot = kMaxN / it.n;
+        const uint32_t stage_bytes = static_cast<uint32_t>(it.n) * 128u;
+        for (int kc0 = 0; kc0 < nk; kc0 += per_slot) {
           if (!mbar_wait(B_empty(r.idx), r.phase ^ 1, p.status)) {
             do_abort();
             break;
           }
+          const int ns = min(per_slot, nk - kc0);
           const uint32_t bar = B_full(r.idx);
-          mbar_arrive_tx(bar, nbox * 4096);
-          for (int i = 0; i < nbox; ++i)
-            tma_load_2d(sB + r.idx * kBSlot + i * 4096, &p.tm_b, bar, kc * kKS, it.m0 + 32 * i);
+          mbar_arrive_tx(bar, ns * stage_bytes);
+          for (int sidx = 0; sidx < ns; ++sidx) {
+            const uint32_t dst = sB + r.idx * kBSlot + sidx * stage_bytes;
+            int row = 0;
+            for (int b = 3; b >= 0; --b) {  // rows in boxes of 128, 64, 32, 16
+              const int h = 16 << b;
+              while (it.n - row >= h) {
+                tma_load_2d(dst + row * 128, &p.tm_b[b], bar, (kc0 + sidx) * kKS, it.m0 + row);
+                row += h;
+              }
+            }
+          }
           r.next(kBStages);
           ++issued;
         }
@@ -330,23 +360,41 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
         const uint32_t d = tmem + ab * kMaxN;
         const uint32_t idesc = idesc_f16_m128(it.n);
         const int nk = p.k / kKS;
+        const int sps = stages_per_slot(it.tier);
+        const int per_slot = kMaxN / it.n;
+        const uint32_t stage_bytes = static_cast<uint32_t>(it.n) * 128u;
         bool ok = true;
-        for (int kc = 0; kc < nk; ++kc) {
-          if (!mbar_wait(A_full(ra.idx), ra.phase, p.status) ||
-              !mbar_wait(B_full(rb.idx), rb.phase, p.status)) {
+        int sidx = 0;
+        for (int kc0 = 0; kc0 < nk && ok; kc0 += sps) {
+          if (!mbar_wait(A_full(ra.idx), ra.phase, p.status)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t a = sA + ra.idx * kASlot, b = sB + rb.idx * kBSlot;
+          const uint32_t abuf = tmem + kTmemA + ra.idx * kACols;
+          const int ns = min(sps, nk - kc0);
+          for (int sub = 0; sub < ns; ++sub) {
+            const int kc = kc0 + sub;
+            if (sidx == 0) {
+              if (!mbar_wait(B_full(rb.idx), rb.phase, p.status)) {
+                ok = false;
+                break;
+              }
+              tc_fence_after();
+            }
+            const uint64_t bd = smem_desc_sw128(sB + rb.idx * kBSlot + sidx * stage_bytes);
 #pragma unroll
-          for (int k = 0; k < kKS / 16; ++k)
-            tc_mma_f16(d, smem_desc_sw128(a + 32 * k), smem_desc_sw128(b + 32 * k), idesc,
-                       (kc | k) != 0);
+            for (int k = 0; k < kKS / 16; ++k)
+              tc_mma_f16_ts(d, abuf + 32 * sub + 8 * k, bd + 2 * k, idesc, (kc | k) != 0);
+            if (++sidx == per_slot || kc == nk - 1) {  // B slot fully consumed
+              tc_commit(B_empty(rb.idx));
+              rb.next(kBStages);
+              sidx = 0;
+            }
+          }
+          if (!ok) break;
           tc_commit(A_empty(ra.idx));
-          tc_commit(B_empty(rb.idx));
-          ra.next(kAStages);
-          rb.next(kBStages);
+          ra.next(kABufs);
         }
         if (!ok) {
           do_abort();
@@ -376,9 +424,9 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
       tc_fence_after();
       const uint32_t taddr = tmem + (static_cast<uint32_t>(32 * quarter) << 16) + ab * kMaxN;
       if (p.gate_up) {
-        // row 2j = gate g, row 2j+1 = up g, with g = r0 + row/2
-        const int g = it.r0 + (row >> 1);
-        const bool is_up = row & 1;
+        // rows in blocks of 8: gate rows have bit 3 clear, the matching up row is row ^ 8
+        const int g = it.r0 + ((row >> 4) << 3) + (row & 7);
+        const bool is_up = (row & 8) != 0;
         float sg = 1.f, su = 1.f;
         if (it.tier == kTierINT8) {
           const int64_t rb = static_cast<int64_t>(it.idx) * p.n_rows;
@@ -394,10 +442,10 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
             const float own = __uint_as_float(v[i]);
-            const float other = __shfl_xor_sync(0xffffffffu, own, 1);
+            const float other = __shfl_xor_sync(0xffffffffu, own, 8);
             const float gate = (is_up ? other : own) * sg;
             const float up = (is_up ? own : other) * su;
-            // even lanes store tokens c..c+7, odd lanes c+8..c+15
+            // gate lanes store tokens c..c+7, up lanes c+8..c+15
             if ((i >> 3) == (is_up ? 1 : 0)) {
               const int tok = c + i;
               if (tok < it.mc) {
@@ -433,69 +481,77 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
     }
   } else {
     // ---------------------------------------------------------- dequant
-    const int dt = threadIdx.x - kDqWarp0 * 32;
-    const int r = dt >> 1, hh = dt & 1;  // A row, half of its 64 k
-    const uint32_t arow_off = (r >> 3) * 1024 + (r & 7) * 128;
-    const int sw = r & 7;
+    // Warp (quarter q = warp & 3, slice j) converts, for every weight slot, the
+    // j-th 64 k of its 32 rows (tensor-memory lanes 32q..32q+31).  Every warp
+    // consumes every slot in order, so each slot has one consumer set.
+    const int dw = warp - kDqWarp0;
+    const int j = dw >> 2;
+    const int m = 32 * (warp & 3) + lane;
+    const uint32_t tlane = static_cast<uint32_t>(32 * (warp & 3)) << 16;
     Ring rw, ra;
     for (int item = blockIdx.x; item < n_items && !aborted(); item += gridDim.x) {
       Item it;
       if (!decode_item(p, item, n_tiles, it)) continue;
-      const int lw = p.gate_up ? ((r & 1) ? 64 + (r >> 1) : (r >> 1)) : r;
       const int nk = p.k / kKS;
-      const int ns = wslots_of(it.tier);
+      const int sps = stages_per_slot(it.tier);
+      // gate_up interleaves gate/up rows in blocks of 8 (the epilogue pairs lanes m, m^8)
+      const int lw = p.gate_up ? (((m >> 4) << 3) + (m & 7) + ((m & 8) ? 64 : 0)) : m;
+      const int swz = lw & 7;
       bool ok = true;
-      for (int kc = 0; kc < nk && ok; ++kc) {
-        bool mine = mbar_wait(A_empty(ra.idx), ra.phase ^ 1, p.status);
-        uint32_t slots[4];
-        Ring rq = rw;
-        for (int q = 0; q < ns; ++q) {
-          slots[q] = rq.idx;
-          if (mine && !mbar_wait(W_full(rq.idx), rq.phase, p.status)) mine = false;
-          rq.next(kWStages);
-        }
-        // every dequant thread reaches this barrier; one failed wait stops all
-        if (named_barrier_or(2, kDqThreads, !mine)) {
+      for (int kc0 = 0; kc0 < nk; kc0 += sps) {
+        const int ns = min(sps, nk - kc0);
+        bool got = mbar_wait(A_empty(ra.idx), ra.phase ^ 1, p.status);
+        if (got) got = mbar_wait(W_full(rw.idx), rw.phase, p.status);
+        if (!__all_sync(0xffffffffu, got)) {
           ok = false;
           break;
         }
-        const uint32_t adst = sA + ra.idx * kASlot + arow_off;
-        if (it.tier == kTierINT4) {
-          const uint32_t src = sW + slots[0] * kWSlot + lw * 32 + hh * 16;
-          const uint4 wv = lds128(src);
-          const uint16_t sraw = lds16(sS + slots[0] * kSSlot + lw * 2);
-          const __half2 s2 = __halves2half2(__ushort_as_half(sraw), __ushort_as_half(sraw));
-          sts128(adst + (((4 * hh + 0) ^ sw) << 4), dq_int4_word(wv.x, s2));
-          sts128(adst + (((4 * hh + 1) ^ sw) << 4), dq_int4_word(wv.y, s2));
-          sts128(adst + (((4 * hh + 2) ^ sw) << 4), dq_int4_word(wv.z, s2));
-          sts128(adst + (((4 * hh + 3) ^ sw) << 4), dq_int4_word(wv.w, s2));
-        } else if (it.tier == kTierINT8) {
-          const uint32_t src = sW + slots[lw >> 6] * kWSlot + (lw & 63) * 64 + hh * 32;
-          const uint4 w0 = lds128(src), w1 = lds128(src + 16);
-          const uint32_t ws[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+        if (j < ns) {
+          const uint32_t src = sW + rw.idx * kWSlot + lw * 128;  // 128B-swizzled row
+          uint32_t v[32];
+          if (it.tier == kTierINT4) {
+            const uint4 w0 = lds128(src + (((2 * j) ^ swz) << 4));
+            const uint4 w1 = lds128(src + (((2 * j + 1) ^ swz) << 4));
+            const uint16_t sraw = lds16(sS + rw.idx * kSSlot + (j >> 1) * 256 + lw * 2);
+            const __half2 s2 = __halves2half2(__ushort_as_half(sraw), __ushort_as_half(sraw));
+            dq_int4_word(w0.x, s2, v + 0);
+            dq_int4_word(w0.y, s2, v + 4);
+            dq_int4_word(w0.z, s2, v + 8);
+            dq_int4_word(w0.w, s2, v + 12);
+            dq_int4_word(w1.x, s2, v + 16);
+            dq_int4_word(w1.y, s2, v + 20);
+            dq_int4_word(w1.z, s2, v + 24);
+            dq_int4_word(w1.w, s2, v + 28);
+          } else if (it.tier == kTierINT8) {
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const uint2 a = dq_int8_word(ws[2 * j]), b = dq_int8_word(ws[2 * j + 1]);
-            sts128(adst + (((4 * hh + j) ^ sw) << 4), make_uint4(a.x, a.y, b.x, b.y));
-          }
-        } else {
-          // 16-bit rows arrive 128B-swizzled: chunk c of slot row t at c ^ (t & 7)
-          const int t = lw & 31;
-          const uint32_t src = sW + slots[lw >> 5] * kWSlot + t * 128;
+            for (int c = 0; c < 4; ++c) {
+              const uint4 wv = lds128(src + (((4 * j + c) ^ swz) << 4));
+              dq_int8_word(wv.x, v + 8 * c + 0);
+              dq_int8_word(wv.y, v + 8 * c + 2);
+              dq_int8_word(wv.z, v + 8 * c + 4);
+              dq_int8_word(wv.w, v + 8 * c + 6);
+            }
+          } else {
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const int c = 4 * hh + j;
-            sts128(adst + ((c ^ sw) << 4), lds128(src + ((c ^ (t & 7)) << 4)));
+            for (int c = 0; c < 8; ++c) {
+              const uint4 wv = lds128(src + ((c ^ swz) << 4));
+              v[4 * c + 0] = wv.x;
+              v[4 * c + 1] = wv.y;
+              v[4 * c + 2] = wv.z;
+              v[4 * c + 3] = wv.w;
+            }
           }
+          tmem_st32(tmem + tlane + kTmemA + ra.idx * kACols + 32 * j, v);
+          tmem_wait_st();
         }
-        fence_proxy_async_smem();
-        named_barrier(1, kDqThreads);
-        if (dt == 0) {
-          for (int q = 0; q < ns; ++q) mbar_arrive(W_empty(slots[q]));
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(W_empty(rw.idx));
           mbar_arrive(A_full(ra.idx));
         }
-        for (int q = 0; q < ns; ++q) rw.next(kWStages);
-        ra.next(kAStages);
+        rw.next(kWStages);
+        ra.next(kABufs);
       }
       if (!ok) {
         do_abort();
@@ -516,13 +572,19 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
 // Activation prep: A[pos, :] = fp16(hidden[token(pos), :]) with every octet of
 // k permuted to [0,4,1,5,2,6,3,7].
 template <typename T>
-__global__ void prep_act_kernel(const T* __restrict__ hidden, int64_t hid, const int32_t* sorted_slot,
-                                int spt, int64_t n_pos, __half* __restrict__ out) {
+__global__ void prep_act_kernel(const T* __restrict__ hidden, int64_t hid, int64_t n_tokens,
+                                const int32_t* sorted_slot, int spt, int64_t n_pos,
+                                __half* __restrict__ out) {
   const int64_t octs = hid / 8;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n_pos * octs;
        i += (int64_t)gridDim.x * blockDim.x) {
     const int64_t pos = i / octs, o = i - pos * octs;
-    const int64_t tok = sorted_slot[pos] / spt;
+    const int32_t slot = sorted_slot[pos];
+    const int64_t tok = slot / spt;
+    if (slot < 0 || tok >= n_tokens) {  // unused position (dropped slot): zero row
+      reinterpret_cast<uint4*>(out + pos * hid)[o] = make_uint4(0, 0, 0, 0);
+      continue;
+    }
     const uint4 v = reinterpret_cast<const uint4*>(hidden + tok * hid)[o];
     uint32_t w[4] = {v.x, v.y, v.z, v.w};
     if (!std::is_same<T, __half>::value) {
@@ -591,41 +653,92 @@ static bool make_map(CUtensorMap* m, CUtensorMapDataType dt, const void* ptr, ui
   return true;
 }
 
+static bool make_map_nd(CUtensorMap* m, CUtensorMapDataType dt, const void* ptr, int rank,
+                        const uint64_t* dims, const uint64_t* strides_bytes, const uint32_t* box,
+                        CUtensorMapSwizzle sw, CUtensorMapL2promotion l2) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) {
+    set_error("cuTensorMapEncodeTiled is unavailable from the driver");
+    return false;
+  }
+  cuuint64_t d[5], st[4];
+  cuuint32_t b[5], e[5];
+  for (int i = 0; i < rank; ++i) {
+    d[i] = dims[i];
+    b[i] = box[i];
+    e[i] = 1;
+    if (i + 1 < rank) st[i] = strides_bytes[i];
+  }
+  CUresult r = fn(m, dt, rank, const_cast<void*>(ptr), d, st, b, e,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, sw, l2, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    set_error("cuTensorMapEncodeTiled failed (%d) for a rank-%d tensor", (int)r, rank);
+    return false;
+  }
+  return true;
+}
+
 // Fill the per-projection maps.  proj 0 = w13 (rows 2I, k = H), 1 = w2 (rows H, k = I).
 static int build_maps(const exq_moe_weights* w, int proj, const void* act, int64_t n_pos,
                       TcParams& p) {
-  const int64_t rows = proj == 0 ? 2 * w->inter : w->hidden;
-  const int64_t k = proj == 0 ? w->hidden : w->inter;
+  const int64_t I = w->inter, H = w->hidden;
+  const int64_t rows = proj == 0 ? 2 * I : H;
+  const int64_t k = proj == 0 ? H : I;
+  const int64_t G = k / 128;
   memset(p.tm_w, 0, sizeof(p.tm_w));
   memset(&p.tm_s, 0, sizeof(p.tm_s));
   const int n4 = w->n_tier[EXQ_TIER_INT4], n8 = w->n_tier[EXQ_TIER_INT8],
             n16 = w->n_tier[EXQ_TIER_BF16];
   const void* const* wt = proj == 0 ? w->w13 : w->w2;
   const void* const* st = proj == 0 ? w->w13_scales : w->w2_scales;
+  const auto L2W = CU_TENSOR_MAP_L2_PROMOTION_L2_256B;
+  const auto SW = CU_TENSOR_MAP_SWIZZLE_128B;
+  // One 16 KB slot = 128 weight rows x 128 bytes (INT4 256 k, INT8 128 k, 16-bit 64 k).
+  // gate_up views the [n, 2I, row_bytes] storage as (x, row in 64-row block, block,
+  // gate/up, expert) so one box holds 64 gate rows and the matching 64 up rows.
+  for (int t = 0; t < 3; ++t) {
+    const int n = w->n_tier[t];
+    if (n <= 0) continue;
+    const CUtensorMapDataType dt =
+        t == EXQ_TIER_BF16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8;
+    const uint64_t esz = t == EXQ_TIER_BF16 ? 2 : 1;
+    const uint64_t xdim = t == EXQ_TIER_INT4 ? k / 2 : k;  // elements per row
+    const uint64_t rb = xdim * esz;                          // bytes per row
+    const uint32_t box_x = static_cast<uint32_t>(128 / esz);
+    bool ok;
+    if (proj == 0) {
+      const uint64_t d[5] = {xdim, 64, (uint64_t)(I / 64), 2, (uint64_t)n};
+      const uint64_t st5[4] = {rb, 64 * rb, (uint64_t)I * rb, 2 * (uint64_t)I * rb};
+      const uint32_t b[5] = {box_x, 64, 1, 2, 1};
+      ok = make_map_nd(&p.tm_w[t], dt, wt[t], 5, d, st5, b, SW, L2W);
+    } else {
+      ok = make_map(&p.tm_w[t], dt, wt[t], xdim, (uint64_t)n * rows, rb, box_x, 128, SW, L2W);
+    }
+    if (!ok) return EXQ_ERR_CUDA;
+  }
   if (n4 > 0) {
-    if (!make_map(&p.tm_w[EXQ_TIER_INT4], CU_TENSOR_MAP_DATA_TYPE_UINT8, wt[EXQ_TIER_INT4], k / 2,
-                  (uint64_t)n4 * rows, k / 2, 32, 64, CU_TENSOR_MAP_SWIZZLE_NONE,
-                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B) ||
-        !make_map(&p.tm_s, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, st[EXQ_TIER_INT4], rows,
-                  (uint64_t)n4 * (k / 128), rows * 2, 64, 1, CU_TENSOR_MAP_SWIZZLE_NONE,
-                  CU_TENSOR_MAP_L2_PROMOTION_L2_128B))
+    bool ok;
+    if (proj == 0) {
+      // scales [n4, G, 2I] as (element in block, block, gate/up, group, expert); 2 groups
+      const uint64_t ds[5] = {64, (uint64_t)(I / 64), 2, (uint64_t)G, (uint64_t)n4};
+      const uint64_t ss[4] = {128, (uint64_t)(2 * I), (uint64_t)(4 * I), (uint64_t)(4 * I * G)};
+      const uint32_t bs[5] = {64, 1, 2, 2, 1};
+      ok = make_map_nd(&p.tm_s, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, st[EXQ_TIER_INT4], 5, ds, ss, bs,
+                       CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B);
+    } else {
+      ok = make_map(&p.tm_s, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, st[EXQ_TIER_INT4], rows,
+                    (uint64_t)n4 * G, rows * 2, 128, 2, CU_TENSOR_MAP_SWIZZLE_NONE,
+                    CU_TENSOR_MAP_L2_PROMOTION_L2_128B);
+    }
+    if (!ok) return EXQ_ERR_CUDA;
+  }
+  (void)n8;
+  (void)n16;
+  for (int b = 0; b < 4; ++b) {
+    if (!make_map(&p.tm_b[b], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, act, k, (uint64_t)n_pos, 2 * k, 64,
+                  16u << b, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B))
       return EXQ_ERR_CUDA;
   }
-  if (n8 > 0) {
-    if (!make_map(&p.tm_w[EXQ_TIER_INT8], CU_TENSOR_MAP_DATA_TYPE_UINT8, wt[EXQ_TIER_INT8], k,
-                  (uint64_t)n8 * rows, k, 64, 64, CU_TENSOR_MAP_SWIZZLE_NONE,
-                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B))
-      return EXQ_ERR_CUDA;
-  }
-  if (n16 > 0) {
-    if (!make_map(&p.tm_w[EXQ_TIER_BF16], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, wt[EXQ_TIER_BF16], k,
-                  (uint64_t)n16 * rows, 2 * k, 64, 32, CU_TENSOR_MAP_SWIZZLE_128B,
-                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B))
-      return EXQ_ERR_CUDA;
-  }
-  if (!make_map(&p.tm_b, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, act, k, (uint64_t)n_pos, 2 * k, 64, 32,
-                CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B))
-    return EXQ_ERR_CUDA;
   p.s8 = static_cast<const __half*>(st[EXQ_TIER_INT8]);
   p.n_rows = static_cast<int>(rows);
   p.k = static_cast<int>(k);
@@ -657,18 +770,19 @@ int launch_tc(const TcParams& p, int max_items, cudaStream_t stream) {
   return EXQ_OK;
 }
 
-int launch_prep(const void* hidden, int act_dtype, int64_t hid, const int32_t* sorted_slot,
-                int spt, int64_t n_pos, __half* out, cudaStream_t stream) {
+int launch_prep(const void* hidden, int act_dtype, int64_t hid, int64_t n_tokens,
+                const int32_t* sorted_slot, int spt, int64_t n_pos, __half* out,
+                cudaStream_t stream) {
   if (n_pos == 0) return EXQ_OK;
   const int64_t work = n_pos * (hid / 8);
   int64_t grid = (work + 255) / 256;
   if (grid > 65535) grid = 65535;
   if (act_dtype == EXQ_F16)
     prep_act_kernel<__half><<<(int)grid, 256, 0, stream>>>(static_cast<const __half*>(hidden), hid,
-                                                           sorted_slot, spt, n_pos, out);
+                                                           n_tokens, sorted_slot, spt, n_pos, out);
   else
     prep_act_kernel<__nv_bfloat16><<<(int)grid, 256, 0, stream>>>(
-        static_cast<const __nv_bfloat16*>(hidden), hid, sorted_slot, spt, n_pos, out);
+        static_cast<const __nv_bfloat16*>(hidden), hid, n_tokens, sorted_slot, spt, n_pos, out);
   EXQ_CHECK_LAUNCH("prep_act_kernel");
   return EXQ_OK;
 }
@@ -815,7 +929,8 @@ extern "C" int exq_moe_layer_forward_range(const exq_moe_weights* w, const void*
     if (st != EXQ_OK) return st;
   }
   if (first_stage <= 1 && end_stage > 1) {
-    st = tc::launch_prep(hidden_states, act_dtype, H, ws.sorted_slot, spt, n_slots, ws.act, s);
+    st = tc::launch_prep(hidden_states, act_dtype, H, n_tokens, ws.sorted_slot, spt, n_slots, ws.act,
+                         s);
     if (st != EXQ_OK) return st;
   }
   for (int proj = 0; proj < 2; ++proj) {

@@ -183,6 +183,11 @@ __global__ void __launch_bounds__(kRouteThreads, 1) route_kernel(RouteParams p, 
     }
   }
   if (mode == kRouteLayer) {
+    // positions past the routed total (slots dropped for a bad expert id) hold -1
+    for (int64_t i = carry + threadIdx.x; i < p.n; i += kRouteThreads) {
+      p.sorted_i32[i] = -1;
+      if (p.order_i64) p.order_i64[i] = -1;
+    }
     // tile list: (expert, first sorted row, rows) ; counts from the next base
     for (int e = threadIdx.x; e < nb; e += kRouteThreads) {
       const int c = ((e + 1 < nb) ? base[e + 1] : carry) - base[e];
