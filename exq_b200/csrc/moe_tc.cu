@@ -159,6 +159,15 @@ __device__ __forceinline__ void dq_int8_word(uint32_t w, uint32_t* o) {
   o[1] = *reinterpret_cast<uint32_t*>(&hb);
 }
 
+// One lane of a converged warp (the same lane on every call with a full mask).
+__device__ __forceinline__ bool elect_one() {
+  uint32_t pred = 0;
+  asm volatile(
+      "{\n .reg .b32 r;\n .reg .pred p;\n elect.sync r|p, 0xffffffff;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(pred));
+  return pred != 0;
+}
+
 __device__ __forceinline__ uint16_t lds16(uint32_t addr) {
   uint16_t v;
   asm volatile("ld.shared.u16 %0, [%1];\n" : "=h"(v) : "r"(addr));
@@ -246,25 +255,28 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
 
   if (warp == kWarpW) {
     // ---------------------------------------------------------- weights
-    if (lane == 0) {
-      Ring r;
-      int issued = 0;
-      const int G = p.k >> 7;
-      for (int item = blockIdx.x; item < n_items && !aborted(); item += gridDim.x) {
-        Item it;
-        if (!decode_item(p, item, n_tiles, it)) {
-          atomicOr(p.status, EXQ_DEV_BAD_TIER);
-          continue;
+    // The whole warp walks the loop (waits are uniform); one elected lane
+    // issues, which keeps the issue path on the warp-uniform datapath.
+    Ring r;
+    int issued = 0;
+    const int G = p.k >> 7;
+    for (int item = blockIdx.x; item < n_items && !aborted(); item += gridDim.x) {
+      Item it;
+      if (!decode_item(p, item, n_tiles, it)) {
+        if (lane == 0) atomicOr(p.status, EXQ_DEV_BAD_TIER);
+        continue;
+      }
+      const int nk = p.k / kKS;
+      const int sps = stages_per_slot(it.tier);
+      bool ok = true;
+      for (int kc0 = 0; kc0 < nk; kc0 += sps) {
+        if (!__all_sync(0xffffffffu, mbar_wait(W_empty(r.idx), r.phase ^ 1, p.status))) {
+          ok = false;
+          break;
         }
-        const int nk = p.k / kKS;
-        const int sps = stages_per_slot(it.tier);
-        for (int kc0 = 0; kc0 < nk && !aborted(); kc0 += sps) {
-          if (!mbar_wait(W_empty(r.idx), r.phase ^ 1, p.status)) {
-            do_abort();
-            break;
-          }
-          const uint32_t dst = sW + r.idx * kWSlot, bar = W_full(r.idx);
-          const int xb = kc0 * (it.tier == kTierINT4 ? 32 : (it.tier == kTierINT8 ? 64 : 64));
+        const uint32_t dst = sW + r.idx * kWSlot, bar = W_full(r.idx);
+        const int xb = kc0 * (it.tier == kTierINT4 ? 32 : 64);
+        if (elect_one()) {
           if (it.tier == kTierINT4) {
             mbar_arrive_tx(bar, kWSlot + kSSlot);
             if (p.gate_up) {
@@ -283,37 +295,43 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
             else
               tma_load_2d(dst, &p.tm_w[it.tier], bar, xb, it.idx * p.n_rows + it.r0);
           }
-          r.next(kWStages);
-          ++issued;
         }
+        __syncwarp();
+        r.next(kWStages);
+        ++issued;
       }
-      if (aborted()) {  // let in-flight copies land before the CTA exits
-        Ring q = r;
-        for (int i = 0; i < min(issued, kWStages); ++i) {
-          if (q.idx == 0) q.phase ^= 1;
-          q.idx = (q.idx + kWStages - 1) % kWStages;
-          mbar_wait(W_full(q.idx), q.phase, p.status);
-        }
+      if (!ok) {
+        do_abort();
+        break;
+      }
+    }
+    if (aborted()) {  // let in-flight copies land before the CTA exits
+      Ring q = r;
+      for (int i = 0; i < min(issued, kWStages); ++i) {
+        if (q.idx == 0) q.phase ^= 1;
+        q.idx = (q.idx + kWStages - 1) % kWStages;
+        mbar_wait(W_full(q.idx), q.phase, p.status);
       }
     }
   } else if (warp == kWarpB) {
     // ---------------------------------------------------------- activations
-    if (lane == 0) {
-      Ring r;
-      int issued = 0;
-      for (int item = blockIdx.x; item < n_items && !aborted(); item += gridDim.x) {
-        Item it;
-        if (!decode_item(p, item, n_tiles, it)) continue;
-        const int nk = p.k / kKS;
-        const int per_slot = kMaxN / it.n;
-        const uint32_t stage_bytes = static_cast<uint32_t>(it.n) * 128u;
-        for (int kc0 = 0; kc0 < nk; kc0 += per_slot) {
-          if (!mbar_wait(B_empty(r.idx), r.phase ^ 1, p.status)) {
-            do_abort();
-            break;
-          }
-          const int ns = min(per_slot, nk - kc0);
-          const uint32_t bar = B_full(r.idx);
+    Ring r;
+    int issued = 0;
+    for (int item = blockIdx.x; item < n_items && !aborted(); item += gridDim.x) {
+      Item it;
+      if (!decode_item(p, item, n_tiles, it)) continue;
+      const int nk = p.k / kKS;
+      const int per_slot = kMaxN / it.n;
+      const uint32_t stage_bytes = static_cast<uint32_t>(it.n) * 128u;
+      bool ok = true;
+      for (int kc0 = 0; kc0 < nk; kc0 += per_slot) {
+        if (!__all_sync(0xffffffffu, mbar_wait(B_empty(r.idx), r.phase ^ 1, p.status))) {
+          ok = false;
+          break;
+        }
+        const int ns = min(per_slot, nk - kc0);
+        const uint32_t bar = B_full(r.idx);
+        if (elect_one()) {
           mbar_arrive_tx(bar, ns * stage_bytes);
           for (int sidx = 0; sidx < ns; ++sidx) {
             const uint32_t dst = sB + r.idx * kBSlot + sidx * stage_bytes;
@@ -326,82 +344,94 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
               }
             }
           }
-          r.next(kBStages);
-          ++issued;
         }
+        __syncwarp();
+        r.next(kBStages);
+        ++issued;
       }
-      if (aborted()) {
-        Ring q = r;
-        for (int i = 0; i < min(issued, kBStages); ++i) {
-          if (q.idx == 0) q.phase ^= 1;
-          q.idx = (q.idx + kBStages - 1) % kBStages;
-          mbar_wait(B_full(q.idx), q.phase, p.status);
-        }
+      if (!ok) {
+        do_abort();
+        break;
+      }
+    }
+    if (aborted()) {
+      Ring q = r;
+      for (int i = 0; i < min(issued, kBStages); ++i) {
+        if (q.idx == 0) q.phase ^= 1;
+        q.idx = (q.idx + kBStages - 1) % kBStages;
+        mbar_wait(B_full(q.idx), q.phase, p.status);
       }
     }
   } else if (warp == kWarpMma) {
     // ---------------------------------------------------------- MMA issue
-    if (lane == 0) {
-      Ring ra, rb;
-      int count = 0;
-      for (int item = blockIdx.x; item < n_items && !aborted(); item += gridDim.x, ++count) {
-        Item it;
-        if (!decode_item(p, item, n_tiles, it)) {
-          --count;
-          continue;
-        }
-        const int ab = count & 1;
-        const uint32_t acc_phase = (count >> 1) & 1;
-        if (!mbar_wait(Acc_empty(ab), acc_phase ^ 1, p.status)) {
-          do_abort();
+    // Converged warp; the elected lane issues each group of 4 MMAs (K = 64)
+    // and the commits.  Descriptors advance by constants from one base.
+    Ring ra, rb;
+    int count = 0;
+    const uint64_t bdesc0 = smem_desc_sw128(sB);
+    for (int item = blockIdx.x; item < n_items && !aborted(); item += gridDim.x) {
+      Item it;
+      if (!decode_item(p, item, n_tiles, it)) continue;
+      const int ab = count & 1;
+      const uint32_t acc_phase = (count >> 1) & 1;
+      ++count;
+      if (!__all_sync(0xffffffffu, mbar_wait(Acc_empty(ab), acc_phase ^ 1, p.status))) {
+        do_abort();
+        break;
+      }
+      tc_fence_after();
+      const uint32_t d = tmem + ab * kMaxN;
+      const uint32_t idesc = idesc_f16_m128(it.n);
+      const int nk = p.k / kKS;
+      const int sps = stages_per_slot(it.tier);
+      const int per_slot = kMaxN / it.n;
+      const uint32_t stage_desc = static_cast<uint32_t>(it.n) * 8u;  // n rows x 128 B, in 16 B units
+      bool ok = true;
+      int sidx = 0;
+      for (int kc0 = 0; kc0 < nk && ok; kc0 += sps) {
+        if (!__all_sync(0xffffffffu, mbar_wait(A_full(ra.idx), ra.phase, p.status))) {
+          ok = false;
           break;
         }
         tc_fence_after();
-        const uint32_t d = tmem + ab * kMaxN;
-        const uint32_t idesc = idesc_f16_m128(it.n);
-        const int nk = p.k / kKS;
-        const int sps = stages_per_slot(it.tier);
-        const int per_slot = kMaxN / it.n;
-        const uint32_t stage_bytes = static_cast<uint32_t>(it.n) * 128u;
-        bool ok = true;
-        int sidx = 0;
-        for (int kc0 = 0; kc0 < nk && ok; kc0 += sps) {
-          if (!mbar_wait(A_full(ra.idx), ra.phase, p.status)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          const uint32_t abuf = tmem + kTmemA + ra.idx * kACols;
-          const int ns = min(sps, nk - kc0);
-          for (int sub = 0; sub < ns; ++sub) {
-            const int kc = kc0 + sub;
-            if (sidx == 0) {
-              if (!mbar_wait(B_full(rb.idx), rb.phase, p.status)) {
-                ok = false;
-                break;
-              }
-              tc_fence_after();
+        const uint32_t abuf = tmem + kTmemA + ra.idx * kACols;
+        const int ns = min(sps, nk - kc0);
+        for (int sub = 0; sub < ns; ++sub) {
+          const int kc = kc0 + sub;
+          if (sidx == 0) {
+            if (!__all_sync(0xffffffffu, mbar_wait(B_full(rb.idx), rb.phase, p.status))) {
+              ok = false;
+              break;
             }
-            const uint64_t bd = smem_desc_sw128(sB + rb.idx * kBSlot + sidx * stage_bytes);
-#pragma unroll
-            for (int k = 0; k < kKS / 16; ++k)
-              tc_mma_f16_ts(d, abuf + 32 * sub + 8 * k, bd + 2 * k, idesc, (kc | k) != 0);
-            if (++sidx == per_slot || kc == nk - 1) {  // B slot fully consumed
-              tc_commit(B_empty(rb.idx));
-              rb.next(kBStages);
-              sidx = 0;
-            }
+            tc_fence_after();
           }
-          if (!ok) break;
-          tc_commit(A_empty(ra.idx));
-          ra.next(kABufs);
+          const uint64_t bd = bdesc0 + rb.idx * (kBSlot >> 4) + sidx * stage_desc;
+          const uint32_t a = abuf + 32 * sub;
+          const bool release_b = (++sidx == per_slot) || kc == nk - 1;  // B slot fully consumed
+          if (elect_one()) {
+            tc_mma_f16_ts(d, a, bd, idesc, kc != 0);
+            tc_mma_f16_ts(d, a + 8, bd + 2, idesc, 1u);
+            tc_mma_f16_ts(d, a + 16, bd + 4, idesc, 1u);
+            tc_mma_f16_ts(d, a + 24, bd + 6, idesc, 1u);
+            if (release_b) tc_commit(B_empty(rb.idx));
+          }
+          __syncwarp();
+          if (release_b) {
+            rb.next(kBStages);
+            sidx = 0;
+          }
         }
-        if (!ok) {
-          do_abort();
-          break;
-        }
-        tc_commit(Acc_full(ab));
+        if (!ok) break;
+        if (elect_one()) tc_commit(A_empty(ra.idx));
+        __syncwarp();
+        ra.next(kABufs);
       }
+      if (!ok) {
+        do_abort();
+        break;
+      }
+      if (elect_one()) tc_commit(Acc_full(ab));
+      __syncwarp();
     }
   } else if (warp < kDqWarp0) {
     // ---------------------------------------------------------- epilogue
