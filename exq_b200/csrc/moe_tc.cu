@@ -198,6 +198,48 @@ __device__ __forceinline__ void tc_mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, 
       "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate));
 }
 
+// Per-item constants of the MMA warp.
+struct MmaItem {
+  uint32_t d, idesc, stage_desc, bar_bfull, bar_bempty;
+  int nk, per_slot;
+  uint64_t bdesc0;
+  uint32_t* status;
+};
+
+// MMAs of one weight slot (SPS k-stages of 64, A in tensor memory at `abuf`).
+// B stages are consumed from the activation ring; a ring slot is released
+// once its last stage has been issued.  Runs on the whole (converged) warp.
+template <int SPS>
+__device__ __forceinline__ bool mma_slot(const MmaItem& mi, uint32_t abuf, int kc0, Ring& rb,
+                                         int& sidx) {
+#pragma unroll
+  for (int sub = 0; sub < SPS; ++sub) {
+    const int kc = kc0 + sub;
+    if (kc >= mi.nk) break;
+    if (sidx == 0) {
+      if (!__all_sync(0xffffffffu, mbar_wait(mi.bar_bfull + 8u * rb.idx, rb.phase, mi.status)))
+        return false;
+      tc_fence_after();
+    }
+    const uint64_t bd = mi.bdesc0 + rb.idx * (kBSlot >> 4) + sidx * mi.stage_desc;
+    const uint32_t a = abuf + 32 * sub;
+    const bool release_b = (++sidx == mi.per_slot) || kc == mi.nk - 1;
+    if (elect_one()) {
+      tc_mma_f16_ts(mi.d, a, bd, mi.idesc, kc != 0);
+      tc_mma_f16_ts(mi.d, a + 8, bd + 2, mi.idesc, 1u);
+      tc_mma_f16_ts(mi.d, a + 16, bd + 4, mi.idesc, 1u);
+      tc_mma_f16_ts(mi.d, a + 24, bd + 6, mi.idesc, 1u);
+      if (release_b) tc_commit(mi.bar_bempty + 8u * rb.idx);
+    }
+    __syncwarp();
+    if (release_b) {
+      rb.next(kBStages);
+      sidx = 0;
+    }
+  }
+  return true;
+}
+
 __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_constant__ TcParams p) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
@@ -365,7 +407,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
   } else if (warp == kWarpMma) {
     // ---------------------------------------------------------- MMA issue
     // Converged warp; the elected lane issues each group of 4 MMAs (K = 64)
-    // and the commits.  Descriptors advance by constants from one base.
+    // and the commits.  The k-stages of one weight slot are unrolled per tier.
     Ring ra, rb;
     int count = 0;
     const uint64_t bdesc0 = smem_desc_sw128(sB);
@@ -380,47 +422,29 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
         break;
       }
       tc_fence_after();
-      const uint32_t d = tmem + ab * kMaxN;
-      const uint32_t idesc = idesc_f16_m128(it.n);
-      const int nk = p.k / kKS;
-      const int sps = stages_per_slot(it.tier);
-      const int per_slot = kMaxN / it.n;
-      const uint32_t stage_desc = static_cast<uint32_t>(it.n) * 8u;  // n rows x 128 B, in 16 B units
+      MmaItem mi;
+      mi.d = tmem + ab * kMaxN;
+      mi.idesc = idesc_f16_m128(it.n);
+      mi.nk = p.k / kKS;
+      mi.per_slot = kMaxN / it.n;
+      mi.stage_desc = static_cast<uint32_t>(it.n) * 8u;  // n rows x 128 B, in 16 B units
+      mi.bdesc0 = bdesc0;
+      mi.bar_bfull = B_full(0);
+      mi.bar_bempty = B_empty(0);
+      mi.status = p.status;
       bool ok = true;
       int sidx = 0;
-      for (int kc0 = 0; kc0 < nk && ok; kc0 += sps) {
+      const int sps = stages_per_slot(it.tier);
+      for (int kc0 = 0; kc0 < mi.nk; kc0 += sps) {
         if (!__all_sync(0xffffffffu, mbar_wait(A_full(ra.idx), ra.phase, p.status))) {
           ok = false;
           break;
         }
         tc_fence_after();
         const uint32_t abuf = tmem + kTmemA + ra.idx * kACols;
-        const int ns = min(sps, nk - kc0);
-        for (int sub = 0; sub < ns; ++sub) {
-          const int kc = kc0 + sub;
-          if (sidx == 0) {
-            if (!__all_sync(0xffffffffu, mbar_wait(B_full(rb.idx), rb.phase, p.status))) {
-              ok = false;
-              break;
-            }
-            tc_fence_after();
-          }
-          const uint64_t bd = bdesc0 + rb.idx * (kBSlot >> 4) + sidx * stage_desc;
-          const uint32_t a = abuf + 32 * sub;
-          const bool release_b = (++sidx == per_slot) || kc == nk - 1;  // B slot fully consumed
-          if (elect_one()) {
-            tc_mma_f16_ts(d, a, bd, idesc, kc != 0);
-            tc_mma_f16_ts(d, a + 8, bd + 2, idesc, 1u);
-            tc_mma_f16_ts(d, a + 16, bd + 4, idesc, 1u);
-            tc_mma_f16_ts(d, a + 24, bd + 6, idesc, 1u);
-            if (release_b) tc_commit(B_empty(rb.idx));
-          }
-          __syncwarp();
-          if (release_b) {
-            rb.next(kBStages);
-            sidx = 0;
-          }
-        }
+        if (sps == 4) ok = mma_slot<4>(mi, abuf, kc0, rb, sidx);
+        else if (sps == 2) ok = mma_slot<2>(mi, abuf, kc0, rb, sidx);
+        else ok = mma_slot<1>(mi, abuf, kc0, rb, sidx);
         if (!ok) break;
         if (elect_one()) tc_commit(A_empty(ra.idx));
         __syncwarp();
@@ -465,25 +489,23 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
         }
         __half* mid = static_cast<__half*>(p.out);
         const int col = perm_pos(g);
+        __half* mrow = mid + static_cast<int64_t>(it.m0) * p.out_stride + col;
         for (int c = 0; c < it.n; c += 16) {
           uint32_t v[16];
           tmem_ld16(taddr + c, v);
           tmem_wait_ld();
+          // gate lanes finish tokens c..c+7, up lanes c+8..c+15: each lane sends
+          // its partner (lane ^ 8) the value the partner is missing
 #pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const float own = __uint_as_float(v[i]);
-            const float other = __shfl_xor_sync(0xffffffffu, own, 8);
-            const float gate = (is_up ? other : own) * sg;
-            const float up = (is_up ? own : other) * su;
-            // gate lanes store tokens c..c+7, up lanes c+8..c+15
-            if ((i >> 3) == (is_up ? 1 : 0)) {
-              const int tok = c + i;
-              if (tok < it.mc) {
-                const float m = gate / (1.0f + expf(-gate)) * up;
-                mid[static_cast<int64_t>(it.m0 + tok) * p.out_stride + col] =
-                    __float2half_rn(m);
-              }
-            }
+          for (int i = 0; i < 8; ++i) {
+            const float lo = __uint_as_float(v[i]), hi = __uint_as_float(v[8 + i]);
+            const float recv = __shfl_xor_sync(0xffffffffu, is_up ? lo : hi, 8);
+            const float gate = (is_up ? recv : lo) * sg;
+            const float up = (is_up ? hi : recv) * su;
+            const int tok = c + i + (is_up ? 8 : 0);
+            if (tok < it.mc)
+              mrow[static_cast<int64_t>(tok) * p.out_stride] =
+                  __float2half_rn(__fdividef(gate, 1.0f + __expf(-gate)) * up);
           }
         }
       } else {
