@@ -72,6 +72,8 @@ template <typename Tout>
 __global__ void combine_partials_kernel(const float* __restrict__ partial, int64_t H,
                                         const int32_t* __restrict__ pos_of_slot,
                                         int64_t n_tokens, int spt, Tout* __restrict__ out) {
+  pdl_wait();
+  pdl_trigger();
   const int64_t hv = H / 4;
   for (int64_t t = blockIdx.x; t < n_tokens; t += gridDim.x) {
     for (int64_t c = threadIdx.x; c < hv; c += blockDim.x) {
@@ -184,12 +186,17 @@ int launch_combine_partials(const float* partial, int64_t H, const int32_t* pos_
   if (n_tokens == 0) return EXQ_OK;
   const int threads = static_cast<int>(H / 4 < 256 ? (H / 4 < 32 ? 32 : H / 4) : 256);
   const int grid = static_cast<int>(n_tokens < 65535 ? n_tokens : 65535);
+  cudaError_t e;
   if (dtype == EXQ_F16)
-    combine_partials_kernel<__half><<<grid, threads, 0, stream>>>(
-        partial, H, pos_of_slot, n_tokens, spt, static_cast<__half*>(out));
+    e = launch_pdl(combine_partials_kernel<__half>, dim3(grid), dim3(threads), 0, stream, partial,
+                   H, pos_of_slot, n_tokens, spt, static_cast<__half*>(out));
   else
-    combine_partials_kernel<__nv_bfloat16><<<grid, threads, 0, stream>>>(
-        partial, H, pos_of_slot, n_tokens, spt, static_cast<__nv_bfloat16*>(out));
+    e = launch_pdl(combine_partials_kernel<__nv_bfloat16>, dim3(grid), dim3(threads), 0, stream,
+                   partial, H, pos_of_slot, n_tokens, spt, static_cast<__nv_bfloat16*>(out));
+  if (e != cudaSuccess) {
+    set_error("combine_partials_kernel: %s", cudaGetErrorString(e));
+    return EXQ_ERR_CUDA;
+  }
   EXQ_CHECK_LAUNCH("combine_partials_kernel");
   return EXQ_OK;
 }

@@ -5,6 +5,33 @@
 
 namespace exq {
 
+// Programmatic dependent launch.  A kernel launched with launch_pdl may start
+// while its predecessor in the stream is still running: it must call
+// pdl_wait() before touching anything the predecessor writes, and calls
+// pdl_trigger() to let its own successor launch early.  Both are no-ops for
+// ordinary launches.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                              cudaStream_t stream, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
+
 // ----------------------------------------------------------------- routing
 enum RouteMode : int {
   kRouteAlign = 0,      // sgl_kernel moe_align_block_size
@@ -48,7 +75,9 @@ struct RouteParams {
   uint32_t* status;
 };
 
-int launch_route(RouteParams& p, int mode, cudaStream_t stream);
+// `pdl`: launch as a programmatic dependent of the previous kernel in the
+// stream (the kernel waits on griddepcontrol before reading its inputs).
+int launch_route(RouteParams& p, int mode, cudaStream_t stream, bool pdl = false);
 
 // ------------------------------------------------------------ grouped GEMM
 constexpr int kGmMTHost = 32;   // max token rows per GEMM tile

@@ -261,8 +261,6 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
   // misc[0] = TMEM base address, misc[1] = abort flag
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n_tiles = min(*p.n_tiles_ptr, p.max_tiles);
-  const int n_items = n_tiles * p.nblocks;
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < kWStages; ++i) {
@@ -292,6 +290,11 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = misc[0];
+  // everything above overlaps the tail of the previous kernel in the stream
+  pdl_wait();
+  pdl_trigger();
+  const int n_tiles = min(*p.n_tiles_ptr, p.max_tiles);
+  const int n_items = n_tiles * p.nblocks;
   auto aborted = [&]() { return misc[1] != 0; };
   auto do_abort = [&]() { misc[1] = 1; };
 
@@ -627,6 +630,8 @@ template <typename T>
 __global__ void prep_act_kernel(const T* __restrict__ hidden, int64_t hid, int64_t n_tokens,
                                 const int32_t* sorted_slot, int spt, int64_t n_pos,
                                 __half* __restrict__ out) {
+  pdl_wait();
+  pdl_trigger();
   const int64_t octs = hid / 8;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n_pos * octs;
        i += (int64_t)gridDim.x * blockDim.x) {
@@ -817,7 +822,11 @@ int launch_tc(const TcParams& p, int max_items, cudaStream_t stream) {
   int grid = sms[dev];
   if (max_items < grid) grid = max_items;
   if (grid < 1) grid = 1;
-  moe_tc_kernel<<<grid, kThreads, kSmemBytes, stream>>>(p);
+  const cudaError_t e = launch_pdl(moe_tc_kernel, dim3(grid), dim3(kThreads), kSmemBytes, stream, p);
+  if (e != cudaSuccess) {
+    set_error("moe_tc_kernel: %s", cudaGetErrorString(e));
+    return EXQ_ERR_CUDA;
+  }
   EXQ_CHECK_LAUNCH("moe_tc_kernel");
   return EXQ_OK;
 }
@@ -829,12 +838,18 @@ int launch_prep(const void* hidden, int act_dtype, int64_t hid, int64_t n_tokens
   const int64_t work = n_pos * (hid / 8);
   int64_t grid = (work + 255) / 256;
   if (grid > 65535) grid = 65535;
+  cudaError_t e;
   if (act_dtype == EXQ_F16)
-    prep_act_kernel<__half><<<(int)grid, 256, 0, stream>>>(static_cast<const __half*>(hidden), hid,
-                                                           n_tokens, sorted_slot, spt, n_pos, out);
+    e = launch_pdl(prep_act_kernel<__half>, dim3((int)grid), dim3(256), 0, stream,
+                   static_cast<const __half*>(hidden), hid, n_tokens, sorted_slot, spt, n_pos, out);
   else
-    prep_act_kernel<__nv_bfloat16><<<(int)grid, 256, 0, stream>>>(
-        static_cast<const __nv_bfloat16*>(hidden), hid, n_tokens, sorted_slot, spt, n_pos, out);
+    e = launch_pdl(prep_act_kernel<__nv_bfloat16>, dim3((int)grid), dim3(256), 0, stream,
+                   static_cast<const __nv_bfloat16*>(hidden), hid, n_tokens, sorted_slot, spt, n_pos,
+                   out);
+  if (e != cudaSuccess) {
+    set_error("prep_act_kernel: %s", cudaGetErrorString(e));
+    return EXQ_ERR_CUDA;
+  }
   EXQ_CHECK_LAUNCH("prep_act_kernel");
   return EXQ_OK;
 }
@@ -977,7 +992,7 @@ extern "C" int exq_moe_layer_forward_range(const exq_moe_weights* w, const void*
     rp.tile_info = ws.tile_info;
     rp.n_tiles = ws.n_tiles;
     rp.max_tiles = ws.max_tiles;
-    st = launch_route(rp, kRouteLayer, s);
+    st = launch_route(rp, kRouteLayer, s, true);
     if (st != EXQ_OK) return st;
   }
   if (first_stage <= 1 && end_stage > 1) {

@@ -92,6 +92,8 @@ __global__ void __launch_bounds__(kRouteThreads, 1) route_kernel(RouteParams p, 
   int* warp_tmp = tstart + p.n_buckets;              // [33]
   const int nb = p.n_buckets;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  pdl_wait();
+  pdl_trigger();
 
   for (int i = threadIdx.x; i < kRouteWarps * nb; i += kRouteThreads) cnt[i] = 0;
   if (mode == kRouteAlign && p.pad_sorted) {
@@ -255,7 +257,7 @@ size_t route_smem_bytes(int n_buckets) {
   return sizeof(int) * (static_cast<size_t>(kRouteWarps) * n_buckets + 2 * n_buckets + 33);
 }
 
-int launch_route(RouteParams& p, int mode, cudaStream_t stream) {
+int launch_route(RouteParams& p, int mode, cudaStream_t stream, bool pdl) {
   if (p.n_buckets < 1 || p.n_buckets > kMaxBuckets) {
     set_error("route: number of experts %d outside [1, %d]", p.n_buckets, kMaxBuckets);
     return EXQ_ERR_UNSUPPORTED;
@@ -275,7 +277,15 @@ int launch_route(RouteParams& p, int mode, cudaStream_t stream) {
                          route_smem_bytes(kMaxBuckets));
     attr_set[dev] = true;
   }
-  route_kernel<<<1, kRouteThreads, smem, stream>>>(p, mode);
+  if (pdl) {
+    const cudaError_t e = launch_pdl(route_kernel, dim3(1), dim3(kRouteThreads), smem, stream, p, mode);
+    if (e != cudaSuccess) {
+      set_error("route_kernel: %s", cudaGetErrorString(e));
+      return EXQ_ERR_CUDA;
+    }
+  } else {
+    route_kernel<<<1, kRouteThreads, smem, stream>>>(p, mode);
+  }
   EXQ_CHECK_LAUNCH("route_kernel");
   return EXQ_OK;
 }
