@@ -69,30 +69,59 @@ __global__ void combine_kernel(const Tin* __restrict__ down, int64_t H,
 // Layer combine: y[t, h] = sum_j partial[pos(t, j), h] (partials already weighted,
 // fp32, in sorted-position order; pos < 0 = slot dropped).
 template <typename Tout>
+__device__ __forceinline__ void store4(Tout* o, float4 a) {
+  o[0] = from_f32<Tout>(a.x);
+  o[1] = from_f32<Tout>(a.y);
+  o[2] = from_f32<Tout>(a.z);
+  o[3] = from_f32<Tout>(a.w);
+}
+template <>
+__device__ __forceinline__ void store4<__half>(__half* o, float4 a) {
+  __half2 lo = __floats2half2_rn(a.x, a.y), hi = __floats2half2_rn(a.z, a.w);
+  uint2 v = make_uint2(*reinterpret_cast<uint32_t*>(&lo), *reinterpret_cast<uint32_t*>(&hi));
+  *reinterpret_cast<uint2*>(o) = v;
+}
+template <>
+__device__ __forceinline__ void store4<__nv_bfloat16>(__nv_bfloat16* o, float4 a) {
+  __nv_bfloat162 lo = __floats2bfloat162_rn(a.x, a.y), hi = __floats2bfloat162_rn(a.z, a.w);
+  uint2 v = make_uint2(*reinterpret_cast<uint32_t*>(&lo), *reinterpret_cast<uint32_t*>(&hi));
+  *reinterpret_cast<uint2*>(o) = v;
+}
+
+// The token's slot positions are staged in shared memory first so that the
+// row loads of all its slots are independent and issue together.
+template <typename Tout>
 __global__ void combine_partials_kernel(const float* __restrict__ partial, int64_t H,
                                         const int32_t* __restrict__ pos_of_slot,
                                         int64_t n_tokens, int spt, Tout* __restrict__ out) {
+  extern __shared__ int32_t spos[];  // [spt]
   pdl_wait();
   pdl_trigger();
   const int64_t hv = H / 4;
   for (int64_t t = blockIdx.x; t < n_tokens; t += gridDim.x) {
+    for (int j = threadIdx.x; j < spt; j += blockDim.x) spos[j] = pos_of_slot[t * spt + j];
+    __syncthreads();
     for (int64_t c = threadIdx.x; c < hv; c += blockDim.x) {
       float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-      for (int j = 0; j < spt; ++j) {
-        const int32_t r = pos_of_slot[t * spt + j];
-        if (r < 0) continue;
-        const float4 v = reinterpret_cast<const float4*>(partial + (int64_t)r * H)[c];
-        acc.x += v.x;
-        acc.y += v.y;
-        acc.z += v.z;
-        acc.w += v.w;
+      for (int j0 = 0; j0 < spt; j0 += 8) {
+        float4 v[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const int r = j0 + u < spt ? spos[j0 + u] : -1;
+          v[u] = r >= 0 ? __ldg(reinterpret_cast<const float4*>(partial + (int64_t)r * H) + c)
+                        : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {  // sum in slot order
+          acc.x += v[u].x;
+          acc.y += v[u].y;
+          acc.z += v[u].z;
+          acc.w += v[u].w;
+        }
       }
-      Tout* o = out + t * H + 4 * c;
-      o[0] = from_f32<Tout>(acc.x);
-      o[1] = from_f32<Tout>(acc.y);
-      o[2] = from_f32<Tout>(acc.z);
-      o[3] = from_f32<Tout>(acc.w);
+      store4<Tout>(out + t * H + 4 * c, acc);
     }
+    __syncthreads();
   }
 }
 
@@ -188,11 +217,13 @@ int launch_combine_partials(const float* partial, int64_t H, const int32_t* pos_
   const int grid = static_cast<int>(n_tokens < 65535 ? n_tokens : 65535);
   cudaError_t e;
   if (dtype == EXQ_F16)
-    e = launch_pdl(combine_partials_kernel<__half>, dim3(grid), dim3(threads), 0, stream, partial,
-                   H, pos_of_slot, n_tokens, spt, static_cast<__half*>(out));
+    e = launch_pdl(combine_partials_kernel<__half>, dim3(grid), dim3(threads),
+                   sizeof(int32_t) * spt, stream, partial, H, pos_of_slot, n_tokens, spt,
+                   static_cast<__half*>(out));
   else
-    e = launch_pdl(combine_partials_kernel<__nv_bfloat16>, dim3(grid), dim3(threads), 0, stream,
-                   partial, H, pos_of_slot, n_tokens, spt, static_cast<__nv_bfloat16*>(out));
+    e = launch_pdl(combine_partials_kernel<__nv_bfloat16>, dim3(grid), dim3(threads),
+                   sizeof(int32_t) * spt, stream, partial, H, pos_of_slot, n_tokens, spt,
+                   static_cast<__nv_bfloat16*>(out));
   if (e != cudaSuccess) {
     set_error("combine_partials_kernel: %s", cudaGetErrorString(e));
     return EXQ_ERR_CUDA;

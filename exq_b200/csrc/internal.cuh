@@ -79,6 +79,33 @@ struct RouteParams {
 // stream (the kernel waits on griddepcontrol before reading its inputs).
 int launch_route(RouteParams& p, int mode, cudaStream_t stream, bool pdl = false);
 
+// ------------------------------------------------------------ route + gather
+// One layer call's routing fused with the activation gather (route_gather.cu).
+constexpr int kRouteGatherMaxBuckets = 1024;
+constexpr int64_t kRouteGatherMaxSlots = 4096;
+
+struct RouteGatherParams {
+  const void* ids;      // [T, top_k] expert ids
+  int ids_dtype;
+  const void* topk_w;   // [T, top_k] router weights
+  int w_dtype;
+  const void* hidden;   // [T, hidden_size] activations
+  int act_dtype;
+  int64_t hidden_size;
+  int top_k, spt, n_routed, n_buckets, mt;
+  int64_t n;            // slots = T * spt
+  __half* act;          // [n, hidden_size] gathered, fp16, octet-permuted
+  int32_t* pos_of_slot; // [n]
+  float* sorted_w;      // [n]
+  int32_t* ends;        // [n_buckets + 1] or null
+  int32_t* tile_info;   // [max_tiles][3]
+  int32_t* n_tiles;     // [1]
+  int64_t max_tiles;
+  uint32_t* status;
+};
+
+int launch_route_gather(RouteGatherParams& p, cudaStream_t stream);
+
 // ------------------------------------------------------------ grouped GEMM
 constexpr int kGmMTHost = 32;   // max token rows per GEMM tile
 constexpr int kGmRBHost = 128;  // weight rows per work item

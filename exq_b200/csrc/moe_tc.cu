@@ -973,7 +973,34 @@ extern "C" int exq_moe_layer_forward_range(const exq_moe_weights* w, const void*
   if (!status) return EXQ_ERR_CUDA;
   int st = EXQ_OK;
 
-  if (first_stage <= 0 && end_stage > 0) {
+  // decode-sized calls route and gather in one kernel (stage 0; stage 1 is empty)
+  const bool fused = n_slots <= kRouteGatherMaxSlots && n_total <= kRouteGatherMaxBuckets;
+  if (fused && first_stage <= 0 && end_stage > 0) {
+    RouteGatherParams rg{};
+    rg.ids = topk_ids;
+    rg.ids_dtype = ids_dtype;
+    rg.topk_w = topk_weights;
+    rg.w_dtype = w_dtype;
+    rg.hidden = hidden_states;
+    rg.act_dtype = act_dtype;
+    rg.hidden_size = H;
+    rg.top_k = top_k;
+    rg.spt = spt;
+    rg.n_routed = w->n_routed;
+    rg.n_buckets = n_total;
+    rg.mt = kLayerMT;
+    rg.n = n_slots;
+    rg.act = ws.act;
+    rg.pos_of_slot = ws.pos_of_slot;
+    rg.sorted_w = ws.sorted_w;
+    rg.ends = ws.ends;
+    rg.tile_info = ws.tile_info;
+    rg.n_tiles = ws.n_tiles;
+    rg.max_tiles = ws.max_tiles;
+    st = launch_route_gather(rg, s);
+    if (st != EXQ_OK) return st;
+  }
+  if (!fused && first_stage <= 0 && end_stage > 0) {
     RouteParams rp{};
     rp.ids = topk_ids;
     rp.ids_dtype = ids_dtype;
@@ -995,7 +1022,7 @@ extern "C" int exq_moe_layer_forward_range(const exq_moe_weights* w, const void*
     st = launch_route(rp, kRouteLayer, s, true);
     if (st != EXQ_OK) return st;
   }
-  if (first_stage <= 1 && end_stage > 1) {
+  if (!fused && first_stage <= 1 && end_stage > 1) {
     st = tc::launch_prep(hidden_states, act_dtype, H, n_tokens, ws.sorted_slot, spt, n_slots, ws.act,
                          s);
     if (st != EXQ_OK) return st;

@@ -1,0 +1,299 @@
+// Layer routing fused with the activation gather (decode-sized inputs).
+//
+// Replaces, for one MoE layer call, the sort/align step and the gather of
+// exq/runtime/sglang_backend.py:102-131 (moe_align_block_size, then the
+// hidden-state gather the Triton GEMM performs through sorted_token_ids).
+//
+// Every CTA recomputes the same stable counting sort of the T*(top_k+shared)
+// slots in shared memory (a few thousand elements; the ids are read from L2),
+// so all CTAs agree on the placement without a grid-wide barrier.  The sorted
+// positions are then split into contiguous chunks, one per CTA, and each CTA
+//   - copies the hidden-state rows of its positions into the fp16 activation
+//     buffer, converting bf16 and permuting every octet of k to
+//     [0,4,1,5,2,6,3,7] (the k order of the dequantised weights),
+//   - writes the router weight and the slot -> position map of its positions.
+// CTA 0 also writes the GEMM tile list, the expert ends and the -1 entries of
+// dropped slots (expert id out of range).
+//
+// The sort is the same three-pass scheme as route.cu (per-warp histograms
+// built with shared-memory atomics, a column scan plus a block scan, stable
+// placement), with 8 warps instead of 32; pass 3 ranks lanes with one ballot per
+// bit of the expert id.
+#include <type_traits>
+
+#include "internal.cuh"
+
+namespace exq {
+
+constexpr int kRgThreads = 256;
+constexpr int kRgWarps = kRgThreads / 32;
+
+size_t route_gather_smem_bytes(int n_buckets, int64_t n) {
+  return sizeof(int) * (static_cast<size_t>(kRgWarps + 2) * n_buckets + 34 + 3 * n);
+}
+
+namespace {
+
+__device__ __forceinline__ int rg_exclusive_scan(int v, int* tmp, int* excl) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int x = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
+  }
+  if (lane == 31) tmp[warp] = x;
+  __syncthreads();
+  if (warp == 0) {
+    const int w = lane < kRgWarps ? tmp[lane] : 0;
+    int s = w;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, s, o);
+      if (lane >= o) s += y;
+    }
+    if (lane < kRgWarps) tmp[lane] = s - w;
+    if (lane == 31) tmp[32] = s;
+  }
+  __syncthreads();
+  *excl = tmp[warp] + x - v;
+  const int total = tmp[32];
+  __syncthreads();
+  return total;
+}
+
+// Lanes of the warp holding the same bucket as this lane (e = -1 for none):
+// one ballot per bit of the bucket id plus one for validity.
+__device__ __forceinline__ unsigned same_bucket_lanes(int e, int nbits) {
+  const bool valid = e >= 0;
+  const unsigned v = __ballot_sync(0xffffffffu, valid);
+  unsigned m = valid ? v : ~v;
+  for (int b = 0; b < nbits; ++b) {
+    const bool bit = valid && ((e >> b) & 1);
+    const unsigned x = __ballot_sync(0xffffffffu, bit);
+    m &= bit ? x : ~x;
+  }
+  return m;
+}
+
+// fp16 or bf16 octet -> fp16 octet in [0,4,1,5,2,6,3,7] order
+template <typename T>
+__device__ __forceinline__ uint4 permute_octet(uint4 v) {
+  uint32_t w[4] = {v.x, v.y, v.z, v.w};
+  if (!std::is_same<T, __half>::value) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 f = __bfloat1622float2(*reinterpret_cast<__nv_bfloat162*>(&w[j]));
+      __half2 h = __floats2half2_rn(f.x, f.y);
+      w[j] = *reinterpret_cast<uint32_t*>(&h);
+    }
+  }
+  uint4 r;
+  r.x = prmt(w[0], w[2], 0x5410u);  // (k0, k4)
+  r.y = prmt(w[0], w[2], 0x7632u);  // (k1, k5)
+  r.z = prmt(w[1], w[3], 0x5410u);  // (k2, k6)
+  r.w = prmt(w[1], w[3], 0x7632u);  // (k3, k7)
+  return r;
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kRgThreads) route_gather_kernel(const RouteGatherParams p) {
+  extern __shared__ int smem[];
+  const int nb = p.n_buckets;
+  const int n = static_cast<int>(p.n);
+  int* cnt = smem;                   // [8 warps][nb] counts, then write cursors
+  int* base = cnt + kRgWarps * nb;   // [nb] first sorted position of every bucket
+  int* tstart = base + nb;           // [nb] first tile of every bucket
+  int* tmp = tstart + nb;            // [33] scan scratch, [33] routed total
+  int* bkt = tmp + 34;               // [n] bucket of every slot (-1: dropped)
+  int* slot_at = bkt + n;            // [n] slot at every sorted position
+  float* wslot = reinterpret_cast<float*>(slot_at + n);  // [n] router weight of every slot
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int nbits = 32 - __clz(nb > 1 ? nb - 1 : 1);
+
+  pdl_wait();
+  pdl_trigger();
+
+  for (int i = threadIdx.x; i < kRgWarps * nb; i += kRgThreads) cnt[i] = 0;
+  // bucket of every slot; the id loads of 8 slots are issued before any is used
+  for (int i0 = threadIdx.x; i0 < n; i0 += 8 * kRgThreads) {
+    int64_t v[8];
+    float wv[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int i = i0 + u * kRgThreads;
+      const int t = i / p.spt, j = i - t * p.spt;
+      const bool routed = i < n && j < p.top_k;
+      const int64_t src = routed ? static_cast<int64_t>(t) * p.top_k + j : 0;
+      v[u] = load_index(p.ids, p.ids_dtype, src);
+      wv[u] = load_as_f32(p.topk_w, p.w_dtype, src);
+    }
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int i = i0 + u * kRgThreads;
+      if (i >= n) break;
+      const int t = i / p.spt, j = i - t * p.spt;
+      int e;
+      if (j >= p.top_k) {
+        e = p.n_routed + (j - p.top_k);  // always-on shared expert
+      } else {
+        e = (v[u] >= 0 && v[u] < p.n_routed) ? static_cast<int>(v[u]) : -1;
+        if (e < 0 && blockIdx.x == 0) atomicOr(p.status, EXQ_DEV_BAD_EXPERT_ID);
+      }
+      bkt[i] = e;
+      wslot[i] = j < p.top_k ? wv[u] : 1.0f;  // shared experts weigh 1
+    }
+  }
+  __syncthreads();
+
+  // pass 1: per-warp histograms over contiguous segments (counts do not
+  // depend on the order of the atomics)
+  const int per_warp = ((n + kRgWarps - 1) / kRgWarps + 31) / 32 * 32;
+  const int seg_lo = warp * per_warp, seg_hi = min(n, seg_lo + per_warp);
+  for (int i = seg_lo + lane; i < seg_hi; i += 32) {
+    const int e = bkt[i];
+    if (e >= 0) atomicAdd(&cnt[warp * nb + e], 1);
+  }
+  __syncthreads();
+
+  // pass 2: per-(warp, bucket) offsets, bucket bases and tile starts
+  int carry = 0, tile_carry = 0;
+  for (int c0 = 0; c0 < nb; c0 += kRgThreads) {
+    const int e = c0 + threadIdx.x;
+    int total = 0;
+    if (e < nb) {
+      for (int w = 0; w < kRgWarps; ++w) {
+        const int v = cnt[w * nb + e];
+        cnt[w * nb + e] = total;
+        total += v;
+      }
+    }
+    // one scan of (tiles << 16 | rows): both stay below 2^16 (n <= 4096)
+    int packed_excl;
+    const int packed = rg_exclusive_scan(((total + p.mt - 1) / p.mt) << 16 | total, tmp, &packed_excl);
+    const int sum = packed & 0xFFFF, tsum = packed >> 16;
+    const int excl = packed_excl & 0xFFFF, texcl = packed_excl >> 16;
+    if (e < nb) {
+      base[e] = carry + excl;
+      tstart[e] = tile_carry + texcl;
+      for (int w = 0; w < kRgWarps; ++w) cnt[w * nb + e] += carry + excl;
+    }
+    carry += sum;
+    tile_carry += tsum;
+  }
+  __syncthreads();
+
+  // pass 3: stable placement
+  const unsigned lt_mask = (1u << lane) - 1u;
+  for (int b0 = seg_lo; b0 < seg_hi; b0 += 32) {
+    const int i = b0 + lane;
+    const int e = i < seg_hi ? bkt[i] : -1;
+    const unsigned peers = same_bucket_lanes(e, nbits);
+    if (e >= 0) slot_at[cnt[warp * nb + e] + __popc(peers & lt_mask)] = i;
+    __syncwarp();
+    if (e >= 0 && lane == __ffs(peers) - 1) cnt[warp * nb + e] += __popc(peers);
+    __syncwarp();
+  }
+  __syncthreads();
+
+  if (blockIdx.x == 0) {
+    for (int e = threadIdx.x; e < nb; e += kRgThreads) {
+      const int c = ((e + 1 < nb) ? base[e + 1] : carry) - base[e];
+      if (p.ends) p.ends[e] = base[e];
+      for (int t = 0; t * p.mt < c; ++t) {
+        const int64_t ti = tstart[e] + t;
+        if (ti < p.max_tiles) {
+          p.tile_info[ti * 3 + 0] = e;
+          p.tile_info[ti * 3 + 1] = base[e] + t * p.mt;
+          p.tile_info[ti * 3 + 2] = min(p.mt, c - t * p.mt);
+        }
+      }
+    }
+    if (threadIdx.x == 0) {
+      if (p.ends) p.ends[nb] = carry;
+      p.n_tiles[0] = tile_carry;
+    }
+    for (int i = threadIdx.x; i < n; i += kRgThreads)
+      if (bkt[i] < 0) p.pos_of_slot[i] = -1;
+  }
+
+  // this CTA's chunk of sorted positions
+  const int chunk = (n + gridDim.x - 1) / gridDim.x;
+  const int p0 = blockIdx.x * chunk, p1 = min(n, p0 + chunk);
+  for (int pos = p0 + threadIdx.x; pos < p1; pos += kRgThreads) {
+    if (pos >= carry) continue;
+    const int slot = slot_at[pos];
+    p.pos_of_slot[slot] = pos;
+    p.sorted_w[pos] = wslot[slot];
+  }
+  // row copies: each thread issues 8 independent 16-byte loads before storing
+  const int octs = static_cast<int>(p.hidden_size / 8);
+  const T* hid = static_cast<const T*>(p.hidden);
+  const int total = max(0, p1 - p0) * octs;
+  constexpr int kU = 8;
+  for (int i0 = threadIdx.x; i0 < total; i0 += kU * kRgThreads) {
+    uint4 v[kU];
+#pragma unroll
+    for (int u = 0; u < kU; ++u) {  // unconditional loads (row 0 stands in for unused ones)
+      const int idx = i0 + u * kRgThreads;
+      const int r = idx / octs, pos = p0 + r;
+      const bool used = idx < total && pos < carry;
+      const int64_t tok = used ? slot_at[pos] / p.spt : 0;
+      v[u] = __ldg(reinterpret_cast<const uint4*>(hid + tok * p.hidden_size) + (used ? idx - r * octs : 0));
+    }
+#pragma unroll
+    for (int u = 0; u < kU; ++u) {
+      const int idx = i0 + u * kRgThreads;
+      if (idx < total) {
+        const int r = idx / octs, pos = p0 + r;
+        // positions past the routed total: zero rows
+        reinterpret_cast<uint4*>(p.act + static_cast<int64_t>(pos) * p.hidden_size)[idx - r * octs] =
+            pos < carry ? permute_octet<T>(v[u]) : make_uint4(0, 0, 0, 0);
+      }
+    }
+  }
+}
+
+}  // namespace
+
+int launch_route_gather(RouteGatherParams& p, cudaStream_t stream) {
+  if (p.n_buckets < 1 || p.n_buckets > kRouteGatherMaxBuckets || p.n > kRouteGatherMaxSlots) {
+    set_error("route_gather: %d buckets / %lld slots outside the fused path", p.n_buckets,
+              (long long)p.n);
+    return EXQ_ERR_UNSUPPORTED;
+  }
+  if (p.n == 0) return EXQ_OK;
+  p.status = device_status_ptr();
+  if (!p.status) return EXQ_ERR_CUDA;
+  const size_t smem = route_gather_smem_bytes(p.n_buckets, p.n);
+  static bool attr_set[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+    const size_t mx = route_gather_smem_bytes(kRouteGatherMaxBuckets, kRouteGatherMaxSlots);
+    cudaFuncSetAttribute(route_gather_kernel<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         static_cast<int>(mx));
+    cudaFuncSetAttribute(route_gather_kernel<__nv_bfloat16>,
+                         cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(mx));
+    attr_set[dev] = true;
+  }
+  // at least one sorted position per CTA, at most two CTAs per SM
+  int64_t grid = p.n;
+  const int64_t cap = 2 * static_cast<int64_t>(num_sms());
+  if (grid > cap) grid = cap;
+  cudaError_t e;
+  if (p.act_dtype == EXQ_F16)
+    e = launch_pdl(route_gather_kernel<__half>, dim3(static_cast<int>(grid)), dim3(kRgThreads),
+                   smem, stream, p);
+  else
+    e = launch_pdl(route_gather_kernel<__nv_bfloat16>, dim3(static_cast<int>(grid)),
+                   dim3(kRgThreads), smem, stream, p);
+  if (e != cudaSuccess) {
+    set_error("route_gather_kernel: %s", cudaGetErrorString(e));
+    return EXQ_ERR_CUDA;
+  }
+  EXQ_CHECK_LAUNCH("route_gather_kernel");
+  return EXQ_OK;
+}
+
+}  // namespace exq
