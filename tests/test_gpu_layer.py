@@ -148,6 +148,25 @@ def test_layer_full_size_sampled_tokens(cuda):
     assert OM.rel_l2(y[sample], ref) < TOL
 
 
+def test_layer_full_size_exact_properties(cuda):
+    """Size-independent properties at the full Qwen3 T=256 size, both exact:
+    permuting tokens permutes the output rows (a token's result does not depend
+    on which tokens share its expert tile), and halving every router weight
+    halves the output (the weight multiplies an fp32 partial; halving is exact)."""
+    from exq_b200.synth import hidden_states, zipf_router
+    bank, c = _bank("qwen3", cuda)
+    ids, w = zipf_router(256, 128, 8, seed=12)
+    x = hidden_states(256, c.hidden, seed=12)
+    x, ids, w = x.to(cuda), ids.to(cuda), w.to(cuda)
+    y = bank(x, ids, w)
+    perm = torch.randperm(256, generator=torch.Generator().manual_seed(5)).to(cuda)
+    y_perm = bank(x[perm], ids[perm], w[perm])
+    assert torch.equal(y_perm, y[perm])
+    y_half = bank(x, ids, w * 0.5)
+    # atol: one fp16 subnormal step, for outputs that halve into the subnormal range
+    torch.testing.assert_close(y_half, y * 0.5, rtol=0, atol=6e-8)
+
+
 def test_layer_deterministic_and_token_count_edges(cuda):
     from exq_b200.synth import hidden_states, zipf_router
     bank, c = _bank("qwen3", cuda, n_experts=16)
