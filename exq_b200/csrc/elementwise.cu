@@ -1,4 +1,6 @@
 // Row gather, top-k combine, SiLU*mul and the GPU weight packers.
+#include <atomic>
+
 #include "internal.cuh"
 
 namespace exq {
@@ -323,6 +325,55 @@ extern "C" int exq_combine(const void* down_out, int dtype, int64_t n_active,
 #undef EXQ_COMBINE
   EXQ_CHECK_LAUNCH("combine_kernel");
   return EXQ_OK;
+}
+
+// ---------------------------------------------------------------- combine, no allocation
+// Scratch for exq_combine_noalloc: the inverse permutation of one call,
+// EXQ_COMBINE_NOALLOC_MAX_ACTIVE int32 slots (1 MiB) per device, in the
+// library's static device memory.  One copy per device, shared by every call
+// on that device: calls that overlap in time race on it.
+static __device__ __align__(256) int32_t g_combine_inv[EXQ_COMBINE_NOALLOC_MAX_ACTIVE];
+
+// Address of g_combine_inv on the current device, looked up once per device.
+// The first call on a device may load the module, so make it before any
+// stream capture begins.
+static int32_t* combine_scratch_ptr() {
+  static std::atomic<int32_t*> ptrs[64];
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess || dev < 0 || dev >= 64) {
+    set_error("combine_noalloc: cudaGetDevice failed");
+    return nullptr;
+  }
+  int32_t* p = ptrs[dev].load(std::memory_order_acquire);
+  if (!p) {
+    void* a = nullptr;
+    e = cudaGetSymbolAddress(&a, g_combine_inv);
+    if (e != cudaSuccess) {
+      set_error("combine_noalloc: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
+      return nullptr;
+    }
+    p = static_cast<int32_t*>(a);
+    ptrs[dev].store(p, std::memory_order_release);
+  }
+  return p;
+}
+
+extern "C" int exq_combine_noalloc(const void* down_out, int dtype, int64_t n_active,
+                                   int64_t hidden_size, const int64_t* sort_order,
+                                   const void* router_weights, int w_dtype, int64_t n_tokens,
+                                   int32_t top_k, void* result, int out_dtype, void* stream) {
+  EXQ_CHECK_ARG(n_active >= 0 && n_active <= EXQ_COMBINE_NOALLOC_MAX_ACTIVE,
+                "combine_noalloc: n_active %lld is outside the static scratch of %d slots "
+                "(call exq_combine with a workspace instead)",
+                (long long)n_active, EXQ_COMBINE_NOALLOC_MAX_ACTIVE);
+  int32_t* inv = combine_scratch_ptr();
+  if (!inv) return EXQ_ERR_CUDA;
+  // exq_combine fills the first n_active slots with -1 on `stream` before use,
+  // so nothing in the scratch has to start zeroed.
+  return exq_combine(down_out, dtype, n_active, hidden_size, sort_order, router_weights, w_dtype,
+                     n_tokens, top_k, result, out_dtype, inv,
+                     sizeof(int32_t) * static_cast<size_t>(EXQ_COMBINE_NOALLOC_MAX_ACTIVE), stream);
 }
 
 extern "C" int exq_silu_and_mul(const void* input, void* out, int dtype, int64_t m,

@@ -128,6 +128,25 @@ EXQ_API int exq_combine(const void* down_out, int dtype, int64_t n_active, int64
                 int64_t n_tokens, int32_t top_k, void* result, int out_dtype,
                 void* workspace, size_t workspace_bytes, void* stream);
 
+/* No counterpart in the reference.  exq_combine without a workspace argument:
+ * the inverse-permutation scratch is a static device array of
+ * EXQ_COMBINE_NOALLOC_MAX_ACTIVE int32 slots (1 MiB per device) inside this
+ * library, so the call allocates no memory (no cudaMalloc, no allocating
+ * library).  For callers that hold only the input and output pointers and no
+ * device allocator, e.g. a plain C binding of the reference's combine.
+ * - n_active above the maximum returns EXQ_ERR_INVALID with a message.
+ * - The scratch is one per device and shared: calls on the same device that
+ *   overlap in time (different streams or host threads) race on it.
+ * - The first call on each device looks the scratch address up (and may load
+ *   the module); make it before any stream capture begins.
+ * - Nothing has to start zeroed: each call fills what it uses on `stream`.
+ * Results are identical to exq_combine. */
+#define EXQ_COMBINE_NOALLOC_MAX_ACTIVE 262144
+EXQ_API int exq_combine_noalloc(const void* down_out, int dtype, int64_t n_active,
+                                int64_t hidden_size, const int64_t* sort_order,
+                                const void* router_weights, int w_dtype, int64_t n_tokens,
+                                int32_t top_k, void* result, int out_dtype, void* stream);
+
 /* sgl_kernel.silu_and_mul (exq/runtime/sglang_backend.py:138-140):
  * out[m, i] = silu(x[m, i]) * x[m, I + i], fp32 math. */
 EXQ_API int exq_silu_and_mul(const void* input, void* out, int dtype, int64_t m, int64_t inter,
