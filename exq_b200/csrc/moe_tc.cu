@@ -212,6 +212,40 @@ struct MmaItem {
 template <int SPS>
 __device__ __forceinline__ bool mma_slot(const MmaItem& mi, uint32_t abuf, int kc0, Ring& rb,
                                          int& sidx) {
+  if (SPS > 1 && sidx + SPS <= mi.per_slot && kc0 + SPS <= mi.nk) {
+    // Fast path (N <= 32 for INT4): all SPS stages lie in the current B slot,
+    // so one wait at most and all 4*SPS MMAs from one elected block, with the
+    // descriptors computed by the whole warp beforehand.
+    if (sidx == 0) {
+      if (!__all_sync(0xffffffffu, mbar_wait(mi.bar_bfull + 8u * rb.idx, rb.phase, mi.status)))
+        return false;
+      tc_fence_after();
+    }
+    uint64_t bd[SPS];
+    bd[0] = mi.bdesc0 + rb.idx * (kBSlot >> 4) + sidx * mi.stage_desc;
+#pragma unroll
+    for (int sub = 1; sub < SPS; ++sub) bd[sub] = bd[sub - 1] + mi.stage_desc;
+    const bool release_b = (sidx + SPS == mi.per_slot) || (kc0 + SPS == mi.nk);
+    const uint32_t first = kc0 != 0;
+    if (elect_one()) {
+#pragma unroll
+      for (int sub = 0; sub < SPS; ++sub) {
+        const uint32_t a = abuf + 32 * sub;
+        tc_mma_f16_ts(mi.d, a, bd[sub], mi.idesc, sub == 0 ? first : 1u);
+        tc_mma_f16_ts(mi.d, a + 8, bd[sub] + 2, mi.idesc, 1u);
+        tc_mma_f16_ts(mi.d, a + 16, bd[sub] + 4, mi.idesc, 1u);
+        tc_mma_f16_ts(mi.d, a + 24, bd[sub] + 6, mi.idesc, 1u);
+      }
+      if (release_b) tc_commit(mi.bar_bempty + 8u * rb.idx);
+    }
+    __syncwarp();
+    sidx += SPS;
+    if (release_b) {
+      rb.next(kBStages);
+      sidx = 0;
+    }
+    return true;
+  }
 #pragma unroll
   for (int sub = 0; sub < SPS; ++sub) {
     const int kc = kc0 + sub;
