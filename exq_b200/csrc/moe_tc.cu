@@ -23,12 +23,14 @@
 //                applied) in registers and writes them to its tensor-memory
 //                lanes with one tcgen05.st; a slot is one "super-stage"
 //                (INT4 256 k, INT8 128 k, 16-bit 64 k) of the A operand
-// A work item is (expert, 128-row block of the projection, up to 128 tokens
+// A work item is (expert, 128-row block of the projection, up to 64 tokens
 // of that expert): every weight byte is dequantised once per item and all the
 // expert's tokens ride in the MMA's N dimension.
 //
-// Tensor memory (512 columns): accumulators at [0,128) and [128,256); two A
-// buffers of 128 columns (128 rows x 256 fp16) at [256,512).
+// Tensor memory (512 columns): accumulators at [0,64) and [64,128); three A
+// buffers of 128 columns (128 rows x 256 fp16) at [128,512).  Tiles hold at
+// most 64 tokens so that the third A buffer fits: it lets the dequantisers
+// run one weight slot further ahead of the MMA.
 //
 // K order.  Inside every 8-element octet the k order is permuted to
 // [0,4,1,5,2,6,3,7] identically for weights and activations (a dot product
@@ -50,12 +52,13 @@ constexpr int kThreads = kWarps * 32;
 constexpr int kWarpW = 0, kWarpB = 1, kWarpMma = 2;
 constexpr int kEpiWarp0 = 3, kNumEpiWarps = 4;
 constexpr int kDqWarp0 = 7, kNumDqWarps = 16;  // 4 lane quarters x 4 k-slices of 64
-constexpr int kWStages = 6, kABufs = 2, kBStages = 4;  // weight slots, TMEM A buffers, B slots
+constexpr int kWStages = 6, kABufs = 3, kBStages = 4;  // weight slots, TMEM A buffers, B slots
 constexpr int kWSlot = 16384, kSSlot = 512, kBSlot = 16384;
 constexpr int kACols = 128;  // tensor-memory columns per A buffer (128 rows x 256 fp16)
-constexpr int kMaxN = 128;       // tokens per item (the MMA's N)
+constexpr int kMaxN = 64;        // tokens per item (the MMA's N)
+constexpr int kBRows = 128;      // activation rows one B slot holds (128 rows x 128 B)
 constexpr int kTmemCols = 512;
-constexpr int kTmemA = 256;      // first tensor-memory column of the A buffers
+constexpr int kTmemA = 2 * kMaxN;  // first tensor-memory column of the A buffers
 constexpr int kKS = 64;          // k per pipeline stage
 
 constexpr int kOffB = 0;
@@ -400,7 +403,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
       Item it;
       if (!decode_item(p, item, n_tiles, it)) continue;
       const int nk = p.k / kKS;
-      const int per_slot = kMaxN / it.n;
+      const int per_slot = kBRows / it.n;
       const uint32_t stage_bytes = static_cast<uint32_t>(it.n) * 128u;
       bool ok = true;
       for (int kc0 = 0; kc0 < nk; kc0 += per_slot) {
@@ -463,7 +466,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
       mi.d = tmem + ab * kMaxN;
       mi.idesc = idesc_f16_m128(it.n);
       mi.nk = p.k / kKS;
-      mi.per_slot = kMaxN / it.n;
+      mi.per_slot = kBRows / it.n;
       mi.stage_desc = static_cast<uint32_t>(it.n) * 8u;  // n rows x 128 B, in 16 B units
       mi.bdesc0 = bdesc0;
       mi.bar_bfull = B_full(0);
