@@ -86,6 +86,7 @@ struct TcParams {
   int inter;
   int k;
   int nblocks;
+  int weights_early;      // 1: the predecessor kernel writes only the activations (see below)
   void* out;
   int64_t out_stride;
   uint32_t* status;
@@ -327,8 +328,11 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = misc[0];
-  // everything above overlaps the tail of the previous kernel in the stream
-  pdl_wait();
+  // everything above overlaps the tail of the previous kernel in the stream.
+  // With p.weights_early the tile list was written two launches back, so only
+  // the activation producer (which reads the predecessor's output) waits: the
+  // weight producer and the dequantisers start on the first slots right away.
+  if (!p.weights_early) pdl_wait();
   pdl_trigger();
   const int n_tiles = min(*p.n_tiles_ptr, p.max_tiles);
   const int n_items = n_tiles * p.nblocks;
@@ -397,6 +401,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
     }
   } else if (warp == kWarpB) {
     // ---------------------------------------------------------- activations
+    if (p.weights_early) pdl_wait();
     Ring r;
     int issued = 0;
     for (int item = blockIdx.x; item < n_items && !aborted(); item += gridDim.x) {
@@ -1082,6 +1087,8 @@ extern "C" int exq_moe_layer_forward_range(const exq_moe_weights* w, const void*
     p.out = proj == 0 ? static_cast<void*>(ws.mid) : static_cast<void*>(ws.partial);
     p.out_stride = proj == 0 ? I : H;
     p.status = status;
+    // down right after gate_up in this call: its tile list predates gate_up
+    p.weights_early = proj == 1 && first_stage <= 2;
     const int64_t max_items = ws.max_tiles * p.nblocks;
     st = tc::launch_tc(p, static_cast<int>(max_items < INT32_MAX ? max_items : INT32_MAX), s);
     if (st != EXQ_OK) return st;
