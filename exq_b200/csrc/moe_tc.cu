@@ -6,23 +6,27 @@
 // exq/runtime/sglang_backend.py:117-156) for experts that mix BF16, INT8 and
 // INT4 weight tiers.
 //
-// One persistent CTA per SM (736 threads, 23 warps):
+// One persistent CTA per SM (608 threads, 19 warps):
 //   warp 0       weight producer: one TMA per 16 KB slot brings 128 weight rows
 //                x 256 k (INT4; INT8 128 k, 16-bit 64 k) into a 6-slot smem
 //                ring, plus one TMA for the INT4 group scales of the slot
 //   warp 1       activation producer: TMA 2D loads (128B swizzle) of the
-//                item's token rows into a 4-slot ring of 16 KB slots; a slot
-//                holds 128/N k-stages of N rows, so small items prefetch deep
+//                item's token rows into a 3-slot ring of 32 KB slots; a slot
+//                holds 256/N k-stages of N rows (a whole number of weight
+//                slots), so small items prefetch deep
 //   warp 2       MMA issuer: one thread issues tcgen05.mma with A (weights) in
 //                tensor memory and B (tokens) in shared memory, M=128 rows,
 //                N=tokens, K=16, into a double-buffered accumulator
 //   warps 3-6    epilogue: tcgen05.ld of the accumulator, fused SiLU*mul
 //                (gate_up) or router-weighted fp32 partials (down)
-//   warps 7-22   dequantisers: warp (lane quarter q, k-slice j) turns, for every
-//                weight slot, 64 k of the 32 rows of quarter q into fp16 (scale
-//                applied) in registers and writes them to its tensor-memory
-//                lanes with one tcgen05.st; a slot is one "super-stage"
-//                (INT4 256 k, INT8 128 k, 16-bit 64 k) of the A operand
+//   warps 7-18   dequantisers, three groups of four warps (one per lane
+//                quarter).  Group g takes every third weight slot (weight-ring
+//                positions g and g+3, tensor-memory A buffer g), so each ring
+//                position and A buffer has one consumer group and the groups
+//                run staggered.  A warp turns its 32 rows x the slot's k (INT4
+//                256 k, INT8 128 k, 16-bit 64 k) into fp16 (scale applied) in
+//                registers, 64 k at a time, and writes them to its lanes of the
+//                A buffer with tcgen05.st
 // A work item is (expert, 128-row block of the projection, up to 64 tokens
 // of that expert): every weight byte is dequantised once per item and all the
 // expert's tokens ride in the MMA's N dimension.
@@ -47,16 +51,17 @@
 namespace exq {
 namespace tc {
 
-constexpr int kWarps = 23;
+constexpr int kWarps = 19;
 constexpr int kThreads = kWarps * 32;
 constexpr int kWarpW = 0, kWarpB = 1, kWarpMma = 2;
 constexpr int kEpiWarp0 = 3, kNumEpiWarps = 4;
-constexpr int kDqWarp0 = 7, kNumDqWarps = 16;  // 4 lane quarters x 4 k-slices of 64
-constexpr int kWStages = 6, kABufs = 3, kBStages = 4;  // weight slots, TMEM A buffers, B slots
-constexpr int kWSlot = 16384, kSSlot = 512, kBSlot = 16384;
+constexpr int kDqWarp0 = 7, kDqGroups = 3, kDqGroupWarps = 4;  // 3 groups x 4 lane quarters
+constexpr int kWStages = 6, kABufs = 3, kBStages = 3;  // weight slots, TMEM A buffers, B slots
+constexpr int kWSlot = 16384, kSSlot = 512, kBSlot = 32768;
 constexpr int kACols = 128;  // tensor-memory columns per A buffer (128 rows x 256 fp16)
 constexpr int kMaxN = 64;        // tokens per item (the MMA's N)
-constexpr int kBRows = 128;      // activation rows one B slot holds (128 rows x 128 B)
+static_assert(kMaxN <= 64, "the down epilogue holds the router weights of 64 tokens per warp");
+constexpr int kBRows = 256;      // activation rows one B slot holds (256 rows x 128 B)
 constexpr int kTmemCols = 512;
 constexpr int kTmemA = 2 * kMaxN;  // first tensor-memory column of the A buffers
 constexpr int kKS = 64;          // k per pipeline stage
@@ -67,7 +72,9 @@ constexpr int kOffS = kOffW + kWStages * kWSlot;
 constexpr int kOffBar = kOffS + kWStages * kSSlot;
 constexpr int kNumBars = 2 * kWStages + 2 * kABufs + 2 * kBStages + 4;
 constexpr int kOffMisc = kOffBar + kNumBars * 8;
-constexpr int kSmemBytes = kOffMisc + 64 + 1024;  // + slack to align the base to 1024 B
+constexpr int kItemTab = 128;  // work items of this CTA decoded into shared memory up front
+constexpr int kOffItems = kOffMisc + 64;
+constexpr int kSmemBytes = kOffItems + kItemTab * 16 + 1024;  // + slack to align the base to 1024 B
 
 enum : int { kTierBF16 = EXQ_TIER_BF16, kTierINT8 = EXQ_TIER_INT8, kTierINT4 = EXQ_TIER_INT4 };
 
@@ -96,13 +103,25 @@ struct Item {
   int e, m0, mc, nb, tier, idx, n, r0;
 };
 
-__device__ __forceinline__ bool decode_item(const TcParams& p, int item, int n_tiles, Item& it) {
+// (expert, first row, rows, expert_slot code) of a work item, from global memory.
+__device__ __forceinline__ int4 load_item(const TcParams& p, int item, int n_tiles) {
+  const int tile = item - (item / n_tiles) * n_tiles;
+  const int e = __ldg(p.tile_info + 3 * tile);
+  return make_int4(e, __ldg(p.tile_info + 3 * tile + 1), __ldg(p.tile_info + 3 * tile + 2),
+                   __ldg(p.expert_slot + e));
+}
+
+// Work items of a CTA are blockIdx.x, blockIdx.x + gridDim.x, ...; the first
+// kItemTab of them are read from the shared-memory table `tab`.
+__device__ __forceinline__ bool decode_item(const TcParams& p, const int4* tab, int item,
+                                            int n_tiles, Item& it) {
+  const int li = (item - static_cast<int>(blockIdx.x)) / static_cast<int>(gridDim.x);
+  const int4 v = li < kItemTab ? tab[li] : load_item(p, item, n_tiles);
   it.nb = item / n_tiles;
-  const int tile = item - it.nb * n_tiles;
-  it.e = __ldg(p.tile_info + 3 * tile);
-  it.m0 = __ldg(p.tile_info + 3 * tile + 1);
-  it.mc = __ldg(p.tile_info + 3 * tile + 2);
-  const int code = __ldg(p.expert_slot + it.e);
+  it.e = v.x;
+  it.m0 = v.y;
+  it.mc = v.z;
+  const int code = v.w;
   it.tier = code >> 24;
   it.idx = code & 0xFFFFFF;
   it.n = max(16, (it.mc + 15) & ~15);
@@ -113,6 +132,12 @@ __device__ __forceinline__ bool decode_item(const TcParams& p, int item, int n_t
 // k-stages (64 k each) carried by one 16 KB weight slot: 128 rows x 128 bytes.
 __device__ __forceinline__ int stages_per_slot(int tier) {
   return tier == kTierINT4 ? 4 : (tier == kTierINT8 ? 2 : 1);
+}
+
+// k-stages of n activation rows one B slot carries: a multiple of the weight
+// slot's stages, so the stages of a weight slot never straddle two B slots.
+__device__ __forceinline__ int b_stages_per_slot(int n, int sps) {
+  return (kBRows / n) / sps * sps;
 }
 
 struct Ring {
@@ -303,10 +328,10 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
   if (threadIdx.x == 0) {
     for (int i = 0; i < kWStages; ++i) {
       mbar_init(W_full(i), 1);
-      mbar_init(W_empty(i), kNumDqWarps);
+      mbar_init(W_empty(i), kDqGroupWarps);
     }
     for (int i = 0; i < kABufs; ++i) {
-      mbar_init(A_full(i), kNumDqWarps);
+      mbar_init(A_full(i), kDqGroupWarps);
       mbar_init(A_empty(i), 1);
     }
     for (int i = 0; i < kBStages; ++i) {
@@ -336,6 +361,13 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
   pdl_trigger();
   const int n_tiles = min(*p.n_tiles_ptr, p.max_tiles);
   const int n_items = n_tiles * p.nblocks;
+  // decode this CTA's items once, so no role waits on global loads at an item boundary
+  int4* items_tab = reinterpret_cast<int4*>(gbase + kOffItems);
+  for (int t = threadIdx.x; t < kItemTab; t += kThreads) {
+    const int item = static_cast<int>(blockIdx.x) + t * static_cast<int>(gridDim.x);
+    if (item < n_items) items_tab[t] = load_item(p, item, n_tiles);
+  }
+  __syncthreads();
   auto aborted = [&]() { return misc[1] != 0; };
   auto do_abort = [&]() { misc[1] = 1; };
 
@@ -348,7 +380,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
     const int G = p.k >> 7;
     for (int item = blockIdx.x; item < n_items && !aborted(); item += gridDim.x) {
       Item it;
-      if (!decode_item(p, item, n_tiles, it)) {
+      if (!decode_item(p, items_tab, item, n_tiles, it)) {
         if (lane == 0) atomicOr(p.status, EXQ_DEV_BAD_TIER);
         continue;
       }
@@ -406,9 +438,9 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
     int issued = 0;
     for (int item = blockIdx.x; item < n_items && !aborted(); item += gridDim.x) {
       Item it;
-      if (!decode_item(p, item, n_tiles, it)) continue;
+      if (!decode_item(p, items_tab, item, n_tiles, it)) continue;
       const int nk = p.k / kKS;
-      const int per_slot = kBRows / it.n;
+      const int per_slot = b_stages_per_slot(it.n, stages_per_slot(it.tier));
       const uint32_t stage_bytes = static_cast<uint32_t>(it.n) * 128u;
       bool ok = true;
       for (int kc0 = 0; kc0 < nk; kc0 += per_slot) {
@@ -458,7 +490,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
     const uint64_t bdesc0 = smem_desc_sw128(sB);
     for (int item = blockIdx.x; item < n_items && !aborted(); item += gridDim.x) {
       Item it;
-      if (!decode_item(p, item, n_tiles, it)) continue;
+      if (!decode_item(p, items_tab, item, n_tiles, it)) continue;
       const int ab = count & 1;
       const uint32_t acc_phase = (count >> 1) & 1;
       ++count;
@@ -471,7 +503,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
       mi.d = tmem + ab * kMaxN;
       mi.idesc = idesc_f16_m128(it.n);
       mi.nk = p.k / kKS;
-      mi.per_slot = kBRows / it.n;
+      mi.per_slot = b_stages_per_slot(it.n, stages_per_slot(it.tier));
       mi.stage_desc = static_cast<uint32_t>(it.n) * 8u;  // n rows x 128 B, in 16 B units
       mi.bdesc0 = bdesc0;
       mi.bar_bfull = B_full(0);
@@ -509,7 +541,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
     int count = 0;
     for (int item = blockIdx.x; item < n_items && !aborted(); item += gridDim.x, ++count) {
       Item it;
-      if (!decode_item(p, item, n_tiles, it)) {
+      if (!decode_item(p, items_tab, item, n_tiles, it)) {
         --count;
         continue;
       }
@@ -557,18 +589,22 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
         const int h = it.r0 + row;
         float s = 1.f;
         if (it.tier == kTierINT8) s = __half2float(p.s8[static_cast<int64_t>(it.idx) * p.n_rows + h]);
-        float* part = static_cast<float*>(p.out);
+        // router weights of the item's tokens, loaded once: lane l holds tokens
+        // l and 32 + l, every token's weight is then a shuffle away
+        const float w_lo = lane < it.mc ? __ldg(p.sorted_w + it.m0 + lane) : 0.f;
+        const float w_hi = 32 + lane < it.mc ? __ldg(p.sorted_w + it.m0 + 32 + lane) : 0.f;
+        float* prow = static_cast<float*>(p.out) + static_cast<int64_t>(it.m0) * p.out_stride + h;
         for (int c = 0; c < it.n; c += 16) {
           uint32_t v[16];
           tmem_ld16(taddr + c, v);
           tmem_wait_ld();
+          const float wsrc = c < 32 ? w_lo : w_hi;
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
             const int tok = c + i;
-            if (tok < it.mc) {
-              const int64_t pos = it.m0 + tok;
-              part[pos * p.out_stride + h] = __uint_as_float(v[i]) * s * __ldg(p.sorted_w + pos);
-            }
+            const float wt = __shfl_sync(0xffffffffu, wsrc, tok & 31);
+            if (tok < it.mc)
+              prow[static_cast<int64_t>(tok) * p.out_stride] = __uint_as_float(v[i]) * s * wt;
           }
         }
       }
@@ -578,38 +614,42 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
     }
   } else {
     // ---------------------------------------------------------- dequant
-    // Warp (quarter q = warp & 3, slice j) converts, for every weight slot, the
-    // j-th 64 k of its 32 rows (tensor-memory lanes 32q..32q+31).  Every warp
-    // consumes every slot in order, so each slot has one consumer set.
-    const int dw = warp - kDqWarp0;
-    const int j = dw >> 2;
+    // Group g = (warp - kDqWarp0) / 4 converts weight slots gs = g, g+3, ...
+    // (gs counts slots over all items): ring position gs % 6 and A buffer
+    // gs % 3 == g.  The warp's lane quarter is warp % 4 (tensor-memory rule).
+    const int grp = (warp - kDqWarp0) >> 2;
     const int m = 32 * (warp & 3) + lane;
     const uint32_t tlane = static_cast<uint32_t>(32 * (warp & 3)) << 16;
-    Ring rw, ra;
+    const uint32_t abuf = tmem + tlane + kTmemA + grp * kACols;
+    const uint32_t a_empty = A_empty(grp), a_full = A_full(grp);
+    uint32_t gs = 0;  // global slot counter of this CTA
     for (int item = blockIdx.x; item < n_items && !aborted(); item += gridDim.x) {
       Item it;
-      if (!decode_item(p, item, n_tiles, it)) continue;
+      if (!decode_item(p, items_tab, item, n_tiles, it)) continue;
       const int nk = p.k / kKS;
       const int sps = stages_per_slot(it.tier);
       // gate_up interleaves gate/up rows in blocks of 8 (the epilogue pairs lanes m, m^8)
       const int lw = p.gate_up ? (((m >> 4) << 3) + (m & 7) + ((m & 8) ? 64 : 0)) : m;
       const int swz = lw & 7;
       bool ok = true;
-      for (int kc0 = 0; kc0 < nk; kc0 += sps) {
+      for (int kc0 = 0; kc0 < nk; kc0 += sps, ++gs) {
+        if (static_cast<int>(gs % kDqGroups) != grp) continue;
         const int ns = min(sps, nk - kc0);
-        bool got = mbar_wait(A_empty(ra.idx), ra.phase ^ 1, p.status);
-        if (got) got = mbar_wait(W_full(rw.idx), rw.phase, p.status);
+        const uint32_t wi = gs % kWStages, wph = (gs / kWStages) & 1;
+        const uint32_t aph = (gs / kABufs) & 1;
+        bool got = mbar_wait(a_empty, aph ^ 1, p.status);
+        if (got) got = mbar_wait(W_full(wi), wph, p.status);
         if (!__all_sync(0xffffffffu, got)) {
           ok = false;
           break;
         }
-        if (j < ns) {
-          const uint32_t src = sW + rw.idx * kWSlot + lw * 128;  // 128B-swizzled row
+        const uint32_t src = sW + wi * kWSlot + lw * 128;  // 128B-swizzled row
+        for (int j = 0; j < ns; ++j) {
           uint32_t v[32];
           if (it.tier == kTierINT4) {
             const uint4 w0 = lds128(src + (((2 * j) ^ swz) << 4));
             const uint4 w1 = lds128(src + (((2 * j + 1) ^ swz) << 4));
-            const uint16_t sraw = lds16(sS + rw.idx * kSSlot + (j >> 1) * 256 + lw * 2);
+            const uint16_t sraw = lds16(sS + wi * kSSlot + (j >> 1) * 256 + lw * 2);
             const __half2 s2 = __halves2half2(__ushort_as_half(sraw), __ushort_as_half(sraw));
             dq_int4_word(w0.x, s2, v + 0);
             dq_int4_word(w0.y, s2, v + 4);
@@ -638,17 +678,15 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
               v[4 * c + 3] = wv.w;
             }
           }
-          tmem_st32(tmem + tlane + kTmemA + ra.idx * kACols + 32 * j, v);
+          tmem_st32(abuf + 32 * j, v);
           tmem_wait_st();
         }
         tc_fence_before();
         __syncwarp();
         if (lane == 0) {
-          mbar_arrive(W_empty(rw.idx));
-          mbar_arrive(A_full(ra.idx));
+          mbar_arrive(W_empty(wi));
+          mbar_arrive(a_full);
         }
-        rw.next(kWStages);
-        ra.next(kABufs);
       }
       if (!ok) {
         do_abort();
