@@ -74,7 +74,8 @@ constexpr int kNumBars = 2 * kWStages + 2 * kABufs + 2 * kBStages + 4;
 constexpr int kOffMisc = kOffBar + kNumBars * 8;
 constexpr int kItemTab = 128;  // work items of this CTA decoded into shared memory up front
 constexpr int kOffItems = kOffMisc + 64;
-constexpr int kSmemBytes = kOffItems + kItemTab * 16 + 1024;  // + slack to align the base to 1024 B
+constexpr int kItemBytes = 48;  // sizeof(Item)
+constexpr int kSmemBytes = kOffItems + kItemTab * kItemBytes + 1024;  // + slack to align the base to 1024 B
 
 enum : int { kTierBF16 = EXQ_TIER_BF16, kTierINT8 = EXQ_TIER_INT8, kTierINT4 = EXQ_TIER_INT4 };
 
@@ -99,36 +100,6 @@ struct TcParams {
   uint32_t* status;
 };
 
-struct Item {
-  int e, m0, mc, nb, tier, idx, n, r0;
-};
-
-// (expert, first row, rows, expert_slot code) of a work item, from global memory.
-__device__ __forceinline__ int4 load_item(const TcParams& p, int item, int n_tiles) {
-  const int tile = item - (item / n_tiles) * n_tiles;
-  const int e = __ldg(p.tile_info + 3 * tile);
-  return make_int4(e, __ldg(p.tile_info + 3 * tile + 1), __ldg(p.tile_info + 3 * tile + 2),
-                   __ldg(p.expert_slot + e));
-}
-
-// Work items of a CTA are blockIdx.x, blockIdx.x + gridDim.x, ...; the first
-// kItemTab of them are read from the shared-memory table `tab`.
-__device__ __forceinline__ bool decode_item(const TcParams& p, const int4* tab, int item,
-                                            int n_tiles, Item& it) {
-  const int li = (item - static_cast<int>(blockIdx.x)) / static_cast<int>(gridDim.x);
-  const int4 v = li < kItemTab ? tab[li] : load_item(p, item, n_tiles);
-  it.nb = item / n_tiles;
-  it.e = v.x;
-  it.m0 = v.y;
-  it.mc = v.z;
-  const int code = v.w;
-  it.tier = code >> 24;
-  it.idx = code & 0xFFFFFF;
-  it.n = max(16, (it.mc + 15) & ~15);
-  it.r0 = p.gate_up ? it.nb * 64 : it.nb * 128;
-  return it.tier == kTierINT4 || it.tier == kTierINT8 || it.tier == kTierBF16;
-}
-
 // k-stages (64 k each) carried by one 16 KB weight slot: 128 rows x 128 bytes.
 __device__ __forceinline__ int stages_per_slot(int tier) {
   return tier == kTierINT4 ? 4 : (tier == kTierINT8 ? 2 : 1);
@@ -138,6 +109,41 @@ __device__ __forceinline__ int stages_per_slot(int tier) {
 // slot's stages, so the stages of a weight slot never straddle two B slots.
 __device__ __forceinline__ int b_stages_per_slot(int n, int sps) {
   return (kBRows / n) / sps * sps;
+}
+
+// Everything a warp needs about a work item, computed once per CTA.
+struct Item {
+  int e, m0, mc, nb;      // expert, first sorted row, rows, 128-row block of the projection
+  int tier, idx, n, r0;   // tier, index in the tier storage, MMA N (mc rounded up to 16), first row
+  int sps, per_slot, pad0, pad1;  // k-stages per weight slot, per activation slot
+};
+
+static_assert(sizeof(Item) == kItemBytes, "item table entry size");
+
+__device__ __forceinline__ Item make_item(const TcParams& p, int item, int n_tiles) {
+  Item it;
+  it.nb = item / n_tiles;
+  const int tile = item - it.nb * n_tiles;
+  it.e = __ldg(p.tile_info + 3 * tile);
+  it.m0 = __ldg(p.tile_info + 3 * tile + 1);
+  it.mc = __ldg(p.tile_info + 3 * tile + 2);
+  const int code = __ldg(p.expert_slot + it.e);
+  it.tier = code >> 24;
+  it.idx = code & 0xFFFFFF;
+  it.n = max(16, (it.mc + 15) & ~15);
+  it.r0 = p.gate_up ? it.nb * 64 : it.nb * 128;
+  it.sps = stages_per_slot(it.tier);
+  it.per_slot = b_stages_per_slot(it.n, it.sps);
+  it.pad0 = it.pad1 = 0;
+  return it;
+}
+
+// The CTA's li-th work item (global index `item`): from the shared table for
+// the first kItemTab, else from global memory.  False for an unknown tier.
+__device__ __forceinline__ bool decode_item(const TcParams& p, const Item* tab, int li, int item,
+                                            int n_tiles, Item& it) {
+  it = li < kItemTab ? tab[li] : make_item(p, item, n_tiles);
+  return it.tier == kTierINT4 || it.tier == kTierINT8 || it.tier == kTierBF16;
 }
 
 struct Ring {
@@ -362,10 +368,10 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
   const int n_tiles = min(*p.n_tiles_ptr, p.max_tiles);
   const int n_items = n_tiles * p.nblocks;
   // decode this CTA's items once, so no role waits on global loads at an item boundary
-  int4* items_tab = reinterpret_cast<int4*>(gbase + kOffItems);
+  Item* items_tab = reinterpret_cast<Item*>(gbase + kOffItems);
   for (int t = threadIdx.x; t < kItemTab; t += kThreads) {
     const int item = static_cast<int>(blockIdx.x) + t * static_cast<int>(gridDim.x);
-    if (item < n_items) items_tab[t] = load_item(p, item, n_tiles);
+    if (item < n_items) items_tab[t] = make_item(p, item, n_tiles);
   }
   __syncthreads();
   auto aborted = [&]() { return misc[1] != 0; };
@@ -378,14 +384,14 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
     Ring r;
     int issued = 0;
     const int G = p.k >> 7;
-    for (int item = blockIdx.x; item < n_items && !aborted(); item += gridDim.x) {
+    for (int item = blockIdx.x, li = 0; item < n_items && !aborted(); item += gridDim.x, ++li) {
       Item it;
-      if (!decode_item(p, items_tab, item, n_tiles, it)) {
+      if (!decode_item(p, items_tab, li, item, n_tiles, it)) {
         if (lane == 0) atomicOr(p.status, EXQ_DEV_BAD_TIER);
         continue;
       }
       const int nk = p.k / kKS;
-      const int sps = stages_per_slot(it.tier);
+      const int sps = it.sps;
       bool ok = true;
       for (int kc0 = 0; kc0 < nk; kc0 += sps) {
         if (!__all_sync(0xffffffffu, mbar_wait(W_empty(r.idx), r.phase ^ 1, p.status))) {
@@ -436,11 +442,11 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
     if (p.weights_early) pdl_wait();
     Ring r;
     int issued = 0;
-    for (int item = blockIdx.x; item < n_items && !aborted(); item += gridDim.x) {
+    for (int item = blockIdx.x, li = 0; item < n_items && !aborted(); item += gridDim.x, ++li) {
       Item it;
-      if (!decode_item(p, items_tab, item, n_tiles, it)) continue;
+      if (!decode_item(p, items_tab, li, item, n_tiles, it)) continue;
       const int nk = p.k / kKS;
-      const int per_slot = b_stages_per_slot(it.n, stages_per_slot(it.tier));
+      const int per_slot = it.per_slot;
       const uint32_t stage_bytes = static_cast<uint32_t>(it.n) * 128u;
       bool ok = true;
       for (int kc0 = 0; kc0 < nk; kc0 += per_slot) {
@@ -488,9 +494,9 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
     Ring ra, rb;
     int count = 0;
     const uint64_t bdesc0 = smem_desc_sw128(sB);
-    for (int item = blockIdx.x; item < n_items && !aborted(); item += gridDim.x) {
+    for (int item = blockIdx.x, li = 0; item < n_items && !aborted(); item += gridDim.x, ++li) {
       Item it;
-      if (!decode_item(p, items_tab, item, n_tiles, it)) continue;
+      if (!decode_item(p, items_tab, li, item, n_tiles, it)) continue;
       const int ab = count & 1;
       const uint32_t acc_phase = (count >> 1) & 1;
       ++count;
@@ -503,7 +509,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
       mi.d = tmem + ab * kMaxN;
       mi.idesc = idesc_f16_m128(it.n);
       mi.nk = p.k / kKS;
-      mi.per_slot = b_stages_per_slot(it.n, stages_per_slot(it.tier));
+      mi.per_slot = it.per_slot;
       mi.stage_desc = static_cast<uint32_t>(it.n) * 8u;  // n rows x 128 B, in 16 B units
       mi.bdesc0 = bdesc0;
       mi.bar_bfull = B_full(0);
@@ -511,7 +517,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
       mi.status = p.status;
       bool ok = true;
       int sidx = 0;
-      const int sps = stages_per_slot(it.tier);
+      const int sps = it.sps;
       for (int kc0 = 0; kc0 < mi.nk; kc0 += sps) {
         if (!__all_sync(0xffffffffu, mbar_wait(A_full(ra.idx), ra.phase, p.status))) {
           ok = false;
@@ -539,9 +545,9 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
     const int quarter = warp & 3;  // TMEM lanes 32*quarter .. +31
     const int row = 32 * quarter + lane;
     int count = 0;
-    for (int item = blockIdx.x; item < n_items && !aborted(); item += gridDim.x, ++count) {
+    for (int item = blockIdx.x, li = 0; item < n_items && !aborted(); item += gridDim.x, ++li, ++count) {
       Item it;
-      if (!decode_item(p, items_tab, item, n_tiles, it)) {
+      if (!decode_item(p, items_tab, li, item, n_tiles, it)) {
         --count;
         continue;
       }
@@ -623,11 +629,11 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
     const uint32_t abuf = tmem + tlane + kTmemA + grp * kACols;
     const uint32_t a_empty = A_empty(grp), a_full = A_full(grp);
     uint32_t gs = 0;  // global slot counter of this CTA
-    for (int item = blockIdx.x; item < n_items && !aborted(); item += gridDim.x) {
+    for (int item = blockIdx.x, li = 0; item < n_items && !aborted(); item += gridDim.x, ++li) {
       Item it;
-      if (!decode_item(p, items_tab, item, n_tiles, it)) continue;
+      if (!decode_item(p, items_tab, li, item, n_tiles, it)) continue;
       const int nk = p.k / kKS;
-      const int sps = stages_per_slot(it.tier);
+      const int sps = it.sps;
       // gate_up interleaves gate/up rows in blocks of 8 (the epilogue pairs lanes m, m^8)
       const int lw = p.gate_up ? (((m >> 4) << 3) + (m & 7) + ((m & 8) ? 64 : 0)) : m;
       const int swz = lw & 7;
