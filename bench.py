@@ -49,6 +49,8 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--profile", action="store_true",
+                    help="small case for ncu: one layer of the bench workload, 3 eager calls")
     return ap.parse_args()
 
 
@@ -368,10 +370,27 @@ def e2e_timing(banks, inputs, dev, steps, warmup):
     return e0.elapsed_time(e1) / 1e3, h2d, d2h
 
 
+def profile_case():
+    """One layer of the bench workload (311 MB of INT4 weights, > L2) called
+    three times eagerly: the capture target for ``ncu --set full`` on the GEMM
+    (route_gather, gate_up, down, combine: 4 launches per call)."""
+    import torch
+    dev = torch.device("cuda", 0)
+    bank = build_layers(dev, 1)[0]
+    x, ids, w, _ = layer_inputs(dev, CFG["tokens"], 1)[0]
+    for _ in range(3):
+        y = bank(x, ids, w)
+    torch.cuda.synchronize(dev)
+    print(f"profile case ok: T={CFG['tokens']} |y|={y.float().norm().item():.4f}")
+    return 0
+
+
 def main():
     args = parse()
     if args.impl == "reference":
         return reference_arm(args)
+    if args.profile:
+        return profile_case()
     import torch
     import torch.distributed as dist
     world = int(os.environ.get("WORLD_SIZE", "1"))
