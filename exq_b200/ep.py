@@ -1,0 +1,146 @@
+"""Expert parallelism for the MoE expert layer (one process per GPU, NCCL).
+
+The reference has no expert-parallel path of its own: its layer runs whole on
+one GPU (exq/runtime/sglang_backend.py:65-158).  This module shards the
+routed experts of one layer across the ranks of a process group and moves
+tokens to their experts with one all-to-all each way:
+
+1. every rank counts, per destination rank, the (token, expert) slots of its
+   own tokens; an all-to-all of the counts tells every rank what it receives;
+2. the hidden rows of the slots, grouped by destination, and their expert
+   index local to the destination, go out in one all-to-all;
+3. each rank runs its experts on the rows it received with the fused layer
+   kernel (every received row is a token with one expert of weight 1);
+4. the expert outputs return by the reverse all-to-all, in send order;
+5. the owner of each token applies the router weights and sums its slots with
+   the combine kernel (``exq_combine``), and adds the shared experts, which
+   every rank holds and runs on its own tokens.
+
+Rank r owns routed experts [r*E/P, (r+1)*E/P).  Counts travel to the host
+once per call to size the exchange, so a call is not CUDA-graph capturable.
+
+The local expert compute and the weighted combine are functions of the layer
+(``local_fn``, ``combine_fn``).  By default they are this package's CUDA
+kernels; the multi-process CPU tests substitute the CPU oracle to check the
+exchange logic on ``gloo`` ranks.
+"""
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+
+from . import _lib as L
+
+
+def shard_range(n_routed: int, world: int, rank: int) -> tuple[int, int]:
+    """[lo, hi) of the routed experts rank ``rank`` owns."""
+    if n_routed % world:
+        raise ValueError(f"{n_routed} routed experts do not split evenly over {world} ranks")
+    per = n_routed // world
+    return rank * per, (rank + 1) * per
+
+
+def _cuda_combine(rows: torch.Tensor, order: torch.Tensor, weights: torch.Tensor,
+                  out_dtype: torch.dtype) -> torch.Tensor:
+    """y[t] = sum_j w[t, j] * rows[pos(t*k + j)] with pos the inverse of ``order``."""
+    from . import exq_dispatch_cuda as D
+    t = weights.shape[0]
+    y = torch.empty(t, rows.shape[1], dtype=out_dtype, device=rows.device)
+    D.combine(rows, order, weights, y)
+    return y
+
+
+class ExpertParallelLayer:
+    """One MoE layer whose routed experts are sharded over a process group.
+
+    ``local_bank`` holds this rank's routed experts (``n_routed / world`` of
+    them, as an :class:`exq_b200.ExpertBank`); ``shared_bank`` optionally holds
+    the always-on shared experts (replicated on every rank).
+    """
+
+    def __init__(self, local_bank, n_routed: int, group=None, shared_bank=None,
+                 local_fn=None, combine_fn=None, shared_fn=None):
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.n_routed = n_routed
+        self.lo, self.hi = shard_range(n_routed, self.world, self.rank)
+        self.per_rank = self.hi - self.lo
+        self.local_bank = local_bank
+        self.shared_bank = shared_bank
+        if local_bank is not None and getattr(local_bank, "n_routed", self.per_rank) != self.per_rank:
+            raise ValueError(f"local bank holds {local_bank.n_routed} experts, rank {self.rank} "
+                             f"owns {self.per_rank}")
+        self.local_fn = local_fn or self._bank_rows
+        self.combine_fn = combine_fn or _cuda_combine
+        self.shared_fn = shared_fn or self._shared_rows
+
+    # default compute: the fused layer kernel, one expert of weight 1 per row
+    def _bank_rows(self, rows: torch.Tensor, local_ids: torch.Tensor) -> torch.Tensor:
+        if rows.shape[0] == 0:
+            return rows.new_empty(0, rows.shape[1])
+        ones = torch.ones(rows.shape[0], 1, dtype=torch.float32, device=rows.device)
+        return self.local_bank(rows, local_ids.view(-1, 1), ones)
+
+    def _shared_rows(self, hidden: torch.Tensor) -> torch.Tensor | None:
+        if self.shared_bank is None:
+            return None
+        s = self.shared_bank.n_routed
+        ids = torch.arange(s, dtype=torch.int32, device=hidden.device).expand(hidden.shape[0], s)
+        w = torch.ones(hidden.shape[0], s, dtype=torch.float32, device=hidden.device)
+        return self.shared_bank(hidden, ids.contiguous(), w)
+
+    def forward(self, hidden: torch.Tensor, topk_ids: torch.Tensor,
+                topk_weights: torch.Tensor) -> torch.Tensor:
+        """[T, H] output for this rank's T tokens (same dtype as ``hidden``)."""
+        if topk_ids.shape != topk_weights.shape or topk_ids.shape[0] != hidden.shape[0]:
+            raise ValueError("topk_ids / topk_weights must be [T, k] for hidden [T, H]")
+        t, k = topk_ids.shape
+        h = hidden.shape[1]
+        flat = topk_ids.reshape(-1).to(torch.int64)
+        if flat.numel() and (int(flat.min()) < 0 or int(flat.max()) >= self.n_routed):
+            raise ValueError("expert id out of range")
+        dest = torch.div(flat, self.per_rank, rounding_mode="floor")
+        # slots grouped by destination rank; stable keeps slot order inside a group
+        order = torch.sort(dest, stable=True).indices
+        send_counts = torch.bincount(dest, minlength=self.world)
+        recv_counts = torch.empty_like(send_counts)
+        dist.all_to_all_single(recv_counts, send_counts, group=self.group)
+        sc, rc = send_counts.tolist(), recv_counts.tolist()
+
+        send_rows = hidden.index_select(0, torch.div(order, k, rounding_mode="floor")).contiguous()
+        send_ids = (flat[order] - dest[order] * self.per_rank).to(torch.int32).contiguous()
+        recv_rows = hidden.new_empty(sum(rc), h)
+        recv_ids = torch.empty(sum(rc), dtype=torch.int32, device=hidden.device)
+        dist.all_to_all_single(recv_rows, send_rows, rc, sc, group=self.group)
+        dist.all_to_all_single(recv_ids, send_ids, rc, sc, group=self.group)
+
+        out_rows = self.local_fn(recv_rows, recv_ids).contiguous()
+        back = hidden.new_empty(t * k, h)
+        dist.all_to_all_single(back, out_rows, sc, rc, group=self.group)
+
+        y = self.combine_fn(back, order, topk_weights, hidden.dtype)
+        shared = self.shared_fn(hidden)
+        if shared is not None:
+            y = y + shared
+        return y
+
+    __call__ = forward
+
+
+def build_rank_banks(w13: torch.Tensor, w2: torch.Tensor, world: int, rank: int, tiers=None,
+                     act_dtype: torch.dtype = torch.float16, shared_w13=None, shared_w2=None,
+                     shared_tier: str = "BF16"):
+    """This rank's ExpertBank (its slice of the routed experts) and, when given,
+    the shared-expert bank.  ``w13`` [E, 2I, H] / ``w2`` [E, H, I] on the GPU."""
+    from .experts import ExpertBank
+    L.require_cuda(w13, w2)
+    lo, hi = shard_range(w13.shape[0], world, rank)
+    local = ExpertBank.from_dense(w13[lo:hi], w2[lo:hi],
+                                  None if tiers is None else list(tiers)[lo:hi],
+                                  act_dtype=act_dtype)
+    shared = None
+    if shared_w13 is not None:
+        shared = ExpertBank.from_dense(shared_w13, shared_w2, [shared_tier] * shared_w13.shape[0],
+                                       act_dtype=act_dtype)
+    return local, shared

@@ -1,0 +1,104 @@
+"""Workers for the expert-parallel tests (spawned as separate processes).
+
+The CPU workers run the exchange of exq_b200.ep.ExpertParallelLayer on gloo
+ranks with the CPU oracle as the local expert compute and the combine; the
+GPU worker runs the real kernels over NCCL and compares with the full layer
+on one GPU."""
+import os
+
+import torch
+import torch.distributed as dist
+
+from oracle import moe as OM
+
+H, I, E, K = 64, 32, 8, 2
+
+
+def _init(rank, world, port, backend):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    from datetime import timedelta
+    dist.init_process_group(backend, rank=rank, world_size=world, timeout=timedelta(seconds=60))
+
+
+def _weights(seed=0):
+    g = torch.Generator().manual_seed(seed)
+    w13 = [torch.randn(2 * I, H, generator=g) * 0.05 for _ in range(E)]
+    w2 = [torch.randn(H, I, generator=g) * 0.05 for _ in range(E)]
+    return w13, w2
+
+
+def _tokens(rank, t, case):
+    g = torch.Generator().manual_seed(100 + rank)
+    x = torch.randn(t, H, generator=g).to(torch.float16)
+    if case == "one_rank":   # every slot to the experts of rank 0
+        ids = torch.stack([torch.randperm(E // 2, generator=g)[:K] for _ in range(t)]) if t else \
+            torch.zeros(0, K, dtype=torch.int64)
+    else:
+        ids = torch.stack([torch.randperm(E, generator=g)[:K] for _ in range(t)]) if t else \
+            torch.zeros(0, K, dtype=torch.int64)
+    w = torch.rand(t, K, generator=g)
+    return x, ids, w / w.sum(-1, keepdim=True).clamp_min(1e-6)
+
+
+def cpu_worker(rank, world, port, case, t_per_rank):
+    from exq_b200.ep import ExpertParallelLayer
+    _init(rank, world, port, "gloo")
+    try:
+        w13, w2 = _weights()
+        t = t_per_rank[rank]
+        x, ids, w = _tokens(rank, t, case)
+
+        def local_fn(rows, local_ids):
+            lo = rank * (E // world)
+            if rows.shape[0] == 0:
+                return rows.new_empty(0, H)
+            gids = (local_ids.long() + lo).view(-1, 1)
+            ones = torch.ones(rows.shape[0], 1)
+            return OM.moe_layer(rows, gids, ones, w13, w2).to(rows.dtype)
+
+        def combine_fn(back, order, weights, dtype):
+            t_, k_ = weights.shape
+            pos = torch.empty_like(order)
+            pos[order] = torch.arange(order.numel())
+            y = torch.zeros(t_, back.shape[1])
+            for j in range(k_):
+                y += weights[:, j:j + 1].float() * back[pos.view(t_, k_)[:, j]].float()
+            return y.to(dtype)
+
+        layer = ExpertParallelLayer(None, E, local_fn=local_fn, combine_fn=combine_fn,
+                                    shared_fn=lambda h: None)
+        y = layer(x, ids, w)
+        ref = OM.moe_layer(x, ids, w, w13, w2).to(torch.float16)
+        assert y.shape == (t, H) and y.dtype == torch.float16
+        if t:
+            err = OM.rel_l2(y, ref)
+            assert err < 1e-3, f"rank {rank}: rel-L2 {err:.2e}"
+    finally:
+        dist.destroy_process_group()
+
+
+def gpu_worker(rank, world, port):
+    """EP over NCCL on `world` GPUs vs the whole layer on one GPU (Mixtral-like, bf16)."""
+    from exq_b200 import ExpertBank
+    from exq_b200.ep import ExpertParallelLayer, build_rank_banks
+    from exq_b200.synth import expert_weights, hidden_states, zipf_router
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    _init(rank, world, port, "nccl")
+    try:
+        e, h, inter, k, t = 8, 512, 256, 2, 48
+        w13, w2 = expert_weights(e, inter, h, seed=0, device=dev)
+        local, _ = build_rank_banks(w13, w2, world, rank, act_dtype=torch.bfloat16)
+        layer = ExpertParallelLayer(local, e)
+        ids, w = zipf_router(t, e, k, seed=rank)
+        x = hidden_states(t, h, seed=rank).to(dev, torch.bfloat16)
+        y = layer(x, ids.to(dev), w.to(dev))
+        full = ExpertBank.from_dense(w13, w2, None, act_dtype=torch.bfloat16)
+        ref = full(x, ids.to(dev), w.to(dev))
+        torch.cuda.synchronize(dev)
+        err = OM.rel_l2(y.float().cpu(), ref.float().cpu())
+        assert err < 5e-3, f"rank {rank}: rel-L2 {err:.2e} vs the single-GPU layer"
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()

@@ -1,0 +1,38 @@
+"""Expert parallelism: the exchange logic on gloo ranks (CPU) and the CUDA path
+over NCCL (needs two GPUs)."""
+import socket
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+import _ep_helpers as EH
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+@pytest.mark.parametrize("case,t_per_rank", [("spread", (5, 7)), ("one_rank", (6, 3)),
+                                             ("spread", (4, 0))])
+def test_ep_exchange_matches_single_process_oracle(case, t_per_rank):
+    """Two gloo ranks: routing to both ranks, every slot to rank 0's experts
+    (rank 1 receives nothing), and a rank with no tokens."""
+    mp.spawn(EH.cpu_worker, args=(2, _free_port(), case, t_per_rank), nprocs=2, join=True)
+
+
+def test_shard_range():
+    from exq_b200.ep import shard_range
+    assert shard_range(8, 2, 1) == (4, 8)
+    assert shard_range(64, 8, 0) == (0, 8)
+    with pytest.raises(ValueError):
+        shard_range(6, 4, 0)
+
+
+@pytest.mark.gpu
+def test_ep_nccl_two_gpus_matches_single_gpu():
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    mp.spawn(EH.gpu_worker, args=(2, _free_port()), nprocs=2, join=True)
