@@ -49,6 +49,8 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-ep", action="store_true",
+                    help="skip the expert-parallel configs (C4, C5; one GPU = whole layer)")
     ap.add_argument("--profile", action="store_true",
                     help="small case for ncu: one layer of the bench workload, 3 eager calls")
     return ap.parse_args()
@@ -370,6 +372,75 @@ def e2e_timing(banks, inputs, dev, steps, warmup):
     return e0.elapsed_time(e1) / 1e3, h2d, d2h
 
 
+EP_CASES = ("mixtral", "dsv2_lite")   # the expert-sharded configs (C4, C5), decode T=256 per rank
+
+
+def ep_measure(dev, world, rank, name, steps=50, warmup=5):
+    """Expert-parallel layer over NCCL: rank r owns E/world routed experts and
+    its own T=256 tokens; one step = all-to-all out, local fused layer,
+    all-to-all back, weighted combine (+ shared experts).  On one GPU the step
+    is the whole layer (no exchange), the baseline of the scaling.  Device time
+    of `steps` steps, max over ranks.  Reports per-step latency and the weight
+    bytes of the locally owned experts that received tokens, per rank."""
+    import torch
+    import torch.distributed as dist
+    from exq_b200.ep import ExpertParallelLayer, build_rank_banks
+    from exq_b200.synth import CONFIGS, expert_weights, hidden_states, zipf_router
+    c = CONFIGS[name]
+    t = 256
+    w13, w2 = expert_weights(c.n_experts, c.inter, c.hidden, seed=0, device=dev)
+    sw13 = sw2 = None
+    if c.n_shared:
+        sw13, sw2 = expert_weights(c.n_shared, c.inter, c.hidden, seed=1, device=dev)
+    if world == 1:   # the whole layer on one GPU: the baseline of the EP scaling
+        from exq_b200 import ExpertBank
+        local = ExpertBank.from_dense(w13, w2, None, act_dtype=c.act_dtype, shared_w13=sw13,
+                                      shared_w2=sw2)
+        shared = None
+        layer = local
+    else:
+        local, shared = build_rank_banks(w13, w2, world, rank, act_dtype=c.act_dtype,
+                                         shared_w13=sw13, shared_w2=sw2)
+        layer = ExpertParallelLayer(local, c.n_experts, shared_bank=shared)
+    del w13, w2, sw13, sw2
+    torch.cuda.empty_cache()
+    ids, w = zipf_router(t, c.n_experts, c.top_k, seed=11 + rank)
+    x = hidden_states(t, c.hidden, seed=11 + rank).to(dev, c.act_dtype)
+    ids, w = ids.to(dev), w.to(dev)
+    for _ in range(warmup):
+        layer(x, ids, w)
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        layer(x, ids, w)
+    e1.record()
+    torch.cuda.synchronize(dev)
+    sec = torch.tensor([e0.elapsed_time(e1) / 1e3 / steps], device=dev)
+    all_ids = [ids]
+    if world > 1:
+        dist.all_reduce(sec, op=dist.ReduceOp.MAX)
+        # weight bytes per rank: owned experts that received a slot from any rank
+        all_ids = [torch.empty_like(ids) for _ in range(world)]
+        dist.all_gather(all_ids, ids)
+    per = c.n_experts // world
+    used = torch.unique(torch.cat(all_ids).reshape(-1))
+    mine = int(((used >= rank * per) & (used < (rank + 1) * per)).sum())
+    wbytes = torch.tensor([float(mine * local.weight_bytes(0))], device=dev)
+    if world > 1:
+        dist.all_reduce(wbytes, op=dist.ReduceOp.MAX)
+    us = float(sec.item()) * 1e6
+    del layer, local, shared
+    torch.cuda.empty_cache()
+    return {"model": c.name, "experts": c.n_experts, "top_k": c.top_k, "hidden": c.hidden,
+            "inter": c.inter, "shared": c.n_shared, "tokens_per_rank": t,
+            "experts_per_rank": per, "us_per_step": round(us, 1),
+            "weight_GBps_per_rank": round(float(wbytes.item()) / (us * 1e-6) / 1e9, 1),
+            "tokens_per_s_total": round(world * t / (us * 1e-6), 1)}
+
+
 def profile_case():
     """One layer of the bench workload (311 MB of INT4 weights, > L2) called
     three times eagerly: the capture target for ``ncu --set full`` on the GEMM
@@ -479,6 +550,11 @@ def main():
     if rank == 0 and world == 1 and not args.no_cpu:
         cpu = cpu_baseline()
 
+    ep = {}
+    if not args.no_ep:
+        for name in EP_CASES:
+            ep[name] = ep_measure(dev, world, rank, name)
+
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -507,10 +583,14 @@ def main():
         "e2e": {"value": round(e2e_val, 1), "unit": UNIT, "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "steps": e2e_steps,
                 "us_per_layer": round(1e6 * t_e2e / e2e_steps, 2)},
-        "gpu_launches": len(STAGES) * args.steps,
+        # route+gather, gate_up, down, combine per layer call (the separate
+        # activation-prep launch only runs above 4096 slots)
+        "gpu_launches": (4 if c["tokens"] * c["top_k"] <= 4096 else 5) * args.steps,
         "clocks": clk.summary(),
         "sweep": sweep,
     }
+    if ep:
+        line["ep"] = ep
     print(json.dumps(line), flush=True)
     return 0
 

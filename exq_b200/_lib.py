@@ -47,6 +47,9 @@ SIGNATURES = {
     "exq_combine_workspace_bytes": (sz, [i64]),
     "exq_combine": (C.c_int, [vp, C.c_int, i64, i64, vp, vp, C.c_int, i64, i32, vp, C.c_int, vp,
                               sz, vp]),
+    "exq_ep_pack": (C.c_int, [vp, C.c_int, i64, i32, i32, i32, vp, C.c_int, i64, vp, vp, vp, vp,
+                              vp]),
+    "exq_ep_combine": (C.c_int, [vp, C.c_int, vp, vp, C.c_int, i64, i32, i64, vp, vp, vp]),
     "exq_combine_noalloc": (C.c_int, [vp, C.c_int, i64, i64, vp, vp, C.c_int, i64, i32, vp,
                                       C.c_int, vp]),
     "exq_silu_and_mul": (C.c_int, [vp, vp, C.c_int, i64, i64, vp]),

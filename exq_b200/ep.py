@@ -5,24 +5,26 @@ one GPU (exq/runtime/sglang_backend.py:65-158).  This module shards the
 routed experts of one layer across the ranks of a process group and moves
 tokens to their experts with one all-to-all each way:
 
-1. every rank counts, per destination rank, the (token, expert) slots of its
-   own tokens; an all-to-all of the counts tells every rank what it receives;
-2. the hidden rows of the slots, grouped by destination, and their expert
-   index local to the destination, go out in one all-to-all;
+1. one kernel (``exq_ep_pack``) groups the (token, expert) slots of this
+   rank's tokens by destination rank, copies their hidden rows into a send
+   buffer and counts them; an all-to-all of the counts tells every rank what
+   it receives (the step's one host synchronisation, for NCCL's split sizes);
+2. the rows and their expert index local to the destination go out in
+   all-to-alls;
 3. each rank runs its experts on the rows it received with the fused layer
    kernel (every received row is a token with one expert of weight 1);
 4. the expert outputs return by the reverse all-to-all, in send order;
-5. the owner of each token applies the router weights and sums its slots with
-   the combine kernel (``exq_combine``), and adds the shared experts, which
-   every rank holds and runs on its own tokens.
+5. the owner of each token applies the router weights and sums its slots,
+   plus the shared experts (every rank holds them and runs them on its own
+   tokens), in one kernel (``exq_ep_combine``).
 
 Rank r owns routed experts [r*E/P, (r+1)*E/P).  Counts travel to the host
 once per call to size the exchange, so a call is not CUDA-graph capturable.
 
-The local expert compute and the weighted combine are functions of the layer
-(``local_fn``, ``combine_fn``).  By default they are this package's CUDA
-kernels; the multi-process CPU tests substitute the CPU oracle to check the
-exchange logic on ``gloo`` ranks.
+The packing, the local expert compute and the combine are functions of the
+layer (``pack_fn``, ``local_fn``, ``combine_fn``).  By default they are this
+package's CUDA kernels; the multi-process CPU tests substitute the CPU oracle
+to check the exchange logic on ``gloo`` ranks.
 """
 from __future__ import annotations
 
@@ -40,13 +42,33 @@ def shard_range(n_routed: int, world: int, rank: int) -> tuple[int, int]:
     return rank * per, (rank + 1) * per
 
 
-def _cuda_combine(rows: torch.Tensor, order: torch.Tensor, weights: torch.Tensor,
-                  out_dtype: torch.dtype) -> torch.Tensor:
-    """y[t] = sum_j w[t, j] * rows[pos(t*k + j)] with pos the inverse of ``order``."""
-    from . import exq_dispatch_cuda as D
-    t = weights.shape[0]
-    y = torch.empty(t, rows.shape[1], dtype=out_dtype, device=rows.device)
-    D.combine(rows, order, weights, y)
+def _cuda_pack(hidden: torch.Tensor, topk_ids: torch.Tensor, per_rank: int, world: int):
+    """(send_rows [T*k, H], send_ids [T*k] i32, slot_row [T*k] i32, counts [world] i32)
+    with the slots grouped by destination rank (``exq_ep_pack``, one launch)."""
+    t, k = topk_ids.shape
+    dev = hidden.device
+    ids = topk_ids.contiguous()
+    send_rows = torch.empty(t * k, hidden.shape[1], dtype=hidden.dtype, device=dev)
+    send_ids = torch.empty(t * k, dtype=torch.int32, device=dev)
+    slot_row = torch.empty(t * k, dtype=torch.int32, device=dev)
+    counts = torch.empty(world, dtype=torch.int32, device=dev)
+    L.check(L.lib().exq_ep_pack(L.ptr(ids), L.tag(ids), t, k, per_rank, world,
+                                L.ptr(hidden), L.tag(hidden), hidden.shape[1], L.ptr(send_rows),
+                                L.ptr(send_ids), L.ptr(slot_row), L.ptr(counts),
+                                L.stream_of(dev)), "ep_pack")
+    return send_rows, send_ids, slot_row, counts
+
+
+def _cuda_combine(back: torch.Tensor, slot_row: torch.Tensor, weights: torch.Tensor,
+                  base: torch.Tensor | None) -> torch.Tensor:
+    """y[t] = base[t] + sum_j w[t, j] * back[slot_row[t*k + j]] (``exq_ep_combine``)."""
+    t, k = weights.shape
+    w = weights.contiguous()
+    y = torch.empty(t, back.shape[1], dtype=back.dtype, device=back.device)
+    L.check(L.lib().exq_ep_combine(L.ptr(back), L.tag(back), L.ptr(slot_row), L.ptr(w),
+                                   L.tag(w), t, k, back.shape[1],
+                                   None if base is None else L.ptr(base), L.ptr(y),
+                                   L.stream_of(back.device)), "ep_combine")
     return y
 
 
@@ -59,7 +81,7 @@ class ExpertParallelLayer:
     """
 
     def __init__(self, local_bank, n_routed: int, group=None, shared_bank=None,
-                 local_fn=None, combine_fn=None, shared_fn=None):
+                 local_fn=None, combine_fn=None, shared_fn=None, pack_fn=None):
         self.group = group
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
@@ -74,6 +96,7 @@ class ExpertParallelLayer:
         self.local_fn = local_fn or self._bank_rows
         self.combine_fn = combine_fn or _cuda_combine
         self.shared_fn = shared_fn or self._shared_rows
+        self.pack_fn = pack_fn or _cuda_pack
 
     # default compute: the fused layer kernel, one expert of weight 1 per row
     def _bank_rows(self, rows: torch.Tensor, local_ids: torch.Tensor) -> torch.Tensor:
@@ -92,38 +115,32 @@ class ExpertParallelLayer:
 
     def forward(self, hidden: torch.Tensor, topk_ids: torch.Tensor,
                 topk_weights: torch.Tensor) -> torch.Tensor:
-        """[T, H] output for this rank's T tokens (same dtype as ``hidden``)."""
+        """[T, H] output for this rank's T tokens (same dtype as ``hidden``).
+
+        Expert ids out of range are dropped and flagged in the device status,
+        as in the single-GPU layer."""
         if topk_ids.shape != topk_weights.shape or topk_ids.shape[0] != hidden.shape[0]:
             raise ValueError("topk_ids / topk_weights must be [T, k] for hidden [T, H]")
         t, k = topk_ids.shape
         h = hidden.shape[1]
-        flat = topk_ids.reshape(-1).to(torch.int64)
-        if flat.numel() and (int(flat.min()) < 0 or int(flat.max()) >= self.n_routed):
-            raise ValueError("expert id out of range")
-        dest = torch.div(flat, self.per_rank, rounding_mode="floor")
-        # slots grouped by destination rank; stable keeps slot order inside a group
-        order = torch.sort(dest, stable=True).indices
-        send_counts = torch.bincount(dest, minlength=self.world)
+        send_rows, send_ids, slot_row, send_counts = self.pack_fn(hidden.contiguous(), topk_ids,
+                                                                  self.per_rank, self.world)
+        send_counts = send_counts.to(torch.int64)
         recv_counts = torch.empty_like(send_counts)
         dist.all_to_all_single(recv_counts, send_counts, group=self.group)
-        sc, rc = send_counts.tolist(), recv_counts.tolist()
-
-        send_rows = hidden.index_select(0, torch.div(order, k, rounding_mode="floor")).contiguous()
-        send_ids = (flat[order] - dest[order] * self.per_rank).to(torch.int32).contiguous()
+        sc, rc = send_counts.tolist(), recv_counts.tolist()   # the one host sync of a step
+        n_send = sum(sc)
         recv_rows = hidden.new_empty(sum(rc), h)
         recv_ids = torch.empty(sum(rc), dtype=torch.int32, device=hidden.device)
-        dist.all_to_all_single(recv_rows, send_rows, rc, sc, group=self.group)
-        dist.all_to_all_single(recv_ids, send_ids, rc, sc, group=self.group)
+        dist.all_to_all_single(recv_rows, send_rows[:n_send], rc, sc, group=self.group)
+        dist.all_to_all_single(recv_ids, send_ids[:n_send], rc, sc, group=self.group)
 
         out_rows = self.local_fn(recv_rows, recv_ids).contiguous()
-        back = hidden.new_empty(t * k, h)
-        dist.all_to_all_single(back, out_rows, sc, rc, group=self.group)
+        back = hidden.new_empty(max(n_send, 1), h)
+        dist.all_to_all_single(back[:n_send], out_rows, sc, rc, group=self.group)
 
-        y = self.combine_fn(back, order, topk_weights, hidden.dtype)
         shared = self.shared_fn(hidden)
-        if shared is not None:
-            y = y + shared
-        return y
+        return self.combine_fn(back, slot_row, topk_weights, shared)
 
     __call__ = forward
 

@@ -128,6 +128,30 @@ EXQ_API int exq_combine(const void* down_out, int dtype, int64_t n_active, int64
                 int64_t n_tokens, int32_t top_k, void* result, int out_dtype,
                 void* workspace, size_t workspace_bytes, void* stream);
 
+/* ---------------------------------------------------------------- expert parallelism */
+
+/* No counterpart in the reference (its layer runs whole on one GPU,
+ * exq/runtime/sglang_backend.py:65-158).  The send side of the expert-parallel
+ * exchange of exq_b200/ep.py: the T*k slots of topk_ids [T, k], grouped by
+ * destination rank d = expert / experts_per_rank in ascending slot order,
+ * become send_rows [T*k, hidden_size] (the hidden row of each slot, same
+ * dtype), send_ids[r] (the expert index local to the destination),
+ * slot_row[slot] (send row of the slot, -1 if its expert id is out of range:
+ * dropped and flagged in the device status) and counts[n_ranks] (rows per
+ * destination).  At most 4096 slots and 64 ranks; hidden_size % 8 == 0. */
+EXQ_API int exq_ep_pack(const void* topk_ids, int ids_dtype, int64_t n_tokens, int32_t top_k,
+                        int32_t experts_per_rank, int32_t n_ranks, const void* hidden, int dtype,
+                        int64_t hidden_size, void* send_rows, int32_t* send_ids,
+                        int32_t* slot_row, int32_t* counts, void* stream);
+
+/* No counterpart in the reference.  The receive side of the exchange:
+ * out[t, :] = base[t, :] + sum_j weights[t, j] * rows[slot_row[t*k + j], :]
+ * (fp32 in slot order, one rounding; base may be NULL; slot_row < 0 skipped).
+ * rows, base and out share dtype (fp16/bf16); weights fp32/fp16/bf16. */
+EXQ_API int exq_ep_combine(const void* rows, int dtype, const int32_t* slot_row,
+                           const void* weights, int w_dtype, int64_t n_tokens, int32_t top_k,
+                           int64_t hidden_size, const void* base, void* out, void* stream);
+
 /* No counterpart in the reference.  exq_combine without a workspace argument:
  * the inverse-permutation scratch is a static device array of
  * EXQ_COMBINE_NOALLOC_MAX_ACTIVE int32 slots (1 MiB per device) inside this

@@ -57,17 +57,29 @@ def cpu_worker(rank, world, port, case, t_per_rank):
             ones = torch.ones(rows.shape[0], 1)
             return OM.moe_layer(rows, gids, ones, w13, w2).to(rows.dtype)
 
-        def combine_fn(back, order, weights, dtype):
+        def pack_fn(hidden, topk_ids, per_rank, world_):
+            # slots grouped by destination rank in ascending slot order
+            t_, k_ = topk_ids.shape
+            flat = topk_ids.reshape(-1).long()
+            dest = flat // per_rank
+            order = torch.sort(dest, stable=True).indices
+            slot_row = torch.empty_like(order)
+            slot_row[order] = torch.arange(order.numel())
+            counts = torch.bincount(dest, minlength=world_).to(torch.int32)
+            return (hidden[order // k_].contiguous(), (flat[order] % per_rank).to(torch.int32),
+                    slot_row.to(torch.int32), counts)
+
+        def combine_fn(back, slot_row, weights, base):
             t_, k_ = weights.shape
-            pos = torch.empty_like(order)
-            pos[order] = torch.arange(order.numel())
             y = torch.zeros(t_, back.shape[1])
             for j in range(k_):
-                y += weights[:, j:j + 1].float() * back[pos.view(t_, k_)[:, j]].float()
-            return y.to(dtype)
+                y += weights[:, j:j + 1].float() * back[slot_row.view(t_, k_)[:, j].long()].float()
+            if base is not None:
+                y += base.float()
+            return y.to(back.dtype)
 
         layer = ExpertParallelLayer(None, E, local_fn=local_fn, combine_fn=combine_fn,
-                                    shared_fn=lambda h: None)
+                                    shared_fn=lambda h: None, pack_fn=pack_fn)
         y = layer(x, ids, w)
         ref = OM.moe_layer(x, ids, w, w13, w2).to(torch.float16)
         assert y.shape == (t, H) and y.dtype == torch.float16
