@@ -82,7 +82,8 @@ enum : int { kTierBF16 = EXQ_TIER_BF16, kTierINT8 = EXQ_TIER_INT8, kTierINT4 = E
 struct TcParams {
   CUtensorMap tm_w[3];  // weights of this projection per tier storage
   CUtensorMap tm_s;     // INT4 group scales (group-major) of this projection
-  CUtensorMap tm_b[4];  // activations [n_pos, k] fp16, octet-permuted; box rows 16/32/64/128
+  CUtensorMap tm_b[4];  // activations, stage-major [k/64][n_pos][64] fp16 (octet-permuted);
+                        // map b: box of N = 16(b+1) rows x the stages of one B slot
   const int32_t* expert_slot;  // tier << 24 | index inside the tier storage
   const int32_t* tile_info;
   const int32_t* n_tiles_ptr;
@@ -95,6 +96,7 @@ struct TcParams {
   int k;
   int nblocks;
   int weights_early;      // 1: the predecessor kernel writes only the activations (see below)
+  int64_t n_pos;          // rows of the activation / mid buffers
   void* out;
   int64_t out_stride;
   uint32_t* status;
@@ -105,10 +107,11 @@ __device__ __forceinline__ int stages_per_slot(int tier) {
   return tier == kTierINT4 ? 4 : (tier == kTierINT8 ? 2 : 1);
 }
 
-// k-stages of n activation rows one B slot carries: a multiple of the weight
-// slot's stages, so the stages of a weight slot never straddle two B slots.
-__device__ __forceinline__ int b_stages_per_slot(int n, int sps) {
-  return (kBRows / n) / sps * sps;
+// k-stages of n activation rows one B slot carries: a multiple of 4 (the
+// stages of an INT4 weight slot), so a weight slot never straddles two B
+// slots; one 3D TMA box (n rows x these stages) fills the slot.
+__host__ __device__ __forceinline__ int b_stages_per_slot(int n) {
+  return (kBRows / n) & ~3;
 }
 
 // Everything a warp needs about a work item, computed once per CTA.
@@ -133,7 +136,7 @@ __device__ __forceinline__ Item make_item(const TcParams& p, int item, int n_til
   it.n = max(16, (it.mc + 15) & ~15);
   it.r0 = p.gate_up ? it.nb * 64 : it.nb * 128;
   it.sps = stages_per_slot(it.tier);
-  it.per_slot = b_stages_per_slot(it.n, it.sps);
+  it.per_slot = b_stages_per_slot(it.n);
   it.pad0 = it.pad1 = 0;
   return it;
 }
@@ -351,6 +354,12 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
     misc[1] = 0;
     mbar_fence_init();
   }
+  if (threadIdx.x == 32 * kWarpW) {  // tensor-map descriptors into the TMA unit's cache
+    for (int i = 0; i < 3; ++i) tma_prefetch_desc(&p.tm_w[i]);
+    tma_prefetch_desc(&p.tm_s);
+  } else if (threadIdx.x == 32 * kWarpB) {
+    for (int i = 0; i < 4; ++i) tma_prefetch_desc(&p.tm_b[i]);
+  }
   if (warp == kWarpMma) {
     tmem_alloc(base + kOffMisc, kTmemCols);
     tmem_relinquish();
@@ -454,21 +463,11 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
           ok = false;
           break;
         }
-        const int ns = min(per_slot, nk - kc0);
         const uint32_t bar = B_full(r.idx);
         if (elect_one()) {
-          mbar_arrive_tx(bar, ns * stage_bytes);
-          for (int sidx = 0; sidx < ns; ++sidx) {
-            const uint32_t dst = sB + r.idx * kBSlot + sidx * stage_bytes;
-            int row = 0;
-            for (int b = 3; b >= 0; --b) {  // rows in boxes of 128, 64, 32, 16
-              const int h = 16 << b;
-              while (it.n - row >= h) {
-                tma_load_2d(dst + row * 128, &p.tm_b[b], bar, (kc0 + sidx) * kKS, it.m0 + row);
-                row += h;
-              }
-            }
-          }
+          // the whole slot in one box: n rows x per_slot stages (stages past k read as zeros)
+          mbar_arrive_tx(bar, static_cast<uint32_t>(per_slot) * stage_bytes);
+          tma_load_3d(sB + r.idx * kBSlot, &p.tm_b[(it.n >> 4) - 1], bar, 0, it.m0, kc0);
         }
         __syncwarp();
         r.next(kBStages);
@@ -572,7 +571,9 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
         }
         __half* mid = static_cast<__half*>(p.out);
         const int col = perm_pos(g);
-        __half* mrow = mid + static_cast<int64_t>(it.m0) * p.out_stride + col;
+        // mid is stage-major [I/64][n_pos][64]: column col of row m0 + tok
+        __half* mrow = mid + static_cast<int64_t>(col >> 6) * p.n_pos * 64 + (col & 63) +
+                       static_cast<int64_t>(it.m0) * 64;
         for (int c = 0; c < it.n; c += 16) {
           uint32_t v[16];
           tmem_ld16(taddr + c, v);
@@ -587,7 +588,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
             const float up = (is_up ? hi : recv) * su;
             const int tok = c + i + (is_up ? 8 : 0);
             if (tok < it.mc)
-              mrow[static_cast<int64_t>(tok) * p.out_stride] =
+              mrow[static_cast<int64_t>(tok) * 64] =
                   __float2half_rn(__fdividef(gate, 1.0f + __expf(-gate)) * up);
           }
         }
@@ -725,7 +726,7 @@ __global__ void prep_act_kernel(const T* __restrict__ hidden, int64_t hid, int64
     const int32_t slot = sorted_slot[pos];
     const int64_t tok = slot / spt;
     if (slot < 0 || tok >= n_tokens) {  // unused position (dropped slot): zero row
-      reinterpret_cast<uint4*>(out + pos * hid)[o] = make_uint4(0, 0, 0, 0);
+      reinterpret_cast<uint4*>(out)[((o >> 3) * n_pos + pos) * 8 + (o & 7)] = make_uint4(0, 0, 0, 0);
       continue;
     }
     const uint4 v = reinterpret_cast<const uint4*>(hidden + tok * hid)[o];
@@ -744,7 +745,7 @@ __global__ void prep_act_kernel(const T* __restrict__ hidden, int64_t hid, int64
     r.y = prmt(w[0], w[2], 0x7632u);  // (k1, k5)
     r.z = prmt(w[1], w[3], 0x5410u);  // (k2, k6)
     r.w = prmt(w[1], w[3], 0x7632u);  // (k3, k7)
-    reinterpret_cast<uint4*>(out + pos * hid)[o] = r;
+    reinterpret_cast<uint4*>(out)[((o >> 3) * n_pos + pos) * 8 + (o & 7)] = r;  // stage-major
   }
 }
 
@@ -877,9 +878,15 @@ static int build_maps(const exq_moe_weights* w, int proj, const void* act, int64
   }
   (void)n8;
   (void)n16;
+  // activations stage-major [k/64][n_pos][64]: (element, row, stage); map b has a
+  // box of N = 16(b+1) rows x the stages of one B slot
   for (int b = 0; b < 4; ++b) {
-    if (!make_map(&p.tm_b[b], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, act, k, (uint64_t)n_pos, 2 * k, 64,
-                  16u << b, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B))
+    const uint32_t nb = 16u * (b + 1);
+    const uint64_t d[3] = {64, (uint64_t)n_pos, (uint64_t)(k / 64)};
+    const uint64_t s3[2] = {128, (uint64_t)n_pos * 128};
+    const uint32_t bx[3] = {64, nb, (uint32_t)b_stages_per_slot((int)nb)};
+    if (!make_map_nd(&p.tm_b[b], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, act, 3, d, s3, bx,
+                     CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B))
       return EXQ_ERR_CUDA;
   }
   p.s8 = static_cast<const __half*>(st[EXQ_TIER_INT8]);
@@ -1130,6 +1137,7 @@ extern "C" int exq_moe_layer_forward_range(const exq_moe_weights* w, const void*
     p.nblocks = static_cast<int>(proj == 0 ? I / 64 : H / 128);
     p.out = proj == 0 ? static_cast<void*>(ws.mid) : static_cast<void*>(ws.partial);
     p.out_stride = proj == 0 ? I : H;
+    p.n_pos = n_slots;
     p.status = status;
     // down right after gate_up in this call: its tile list predates gate_up
     p.weights_early = proj == 1 && first_stage <= 2;

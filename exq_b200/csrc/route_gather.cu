@@ -246,8 +246,9 @@ __global__ void __launch_bounds__(kRgThreads) route_gather_kernel(const RouteGat
       const int idx = i0 + u * kRgThreads;
       if (idx < total) {
         const int r = idx / octs, pos = p0 + r;
-        // positions past the routed total: zero rows
-        reinterpret_cast<uint4*>(p.act + static_cast<int64_t>(pos) * p.hidden_size)[idx - r * octs] =
+        // act is stage-major [H/64][n][64]; positions past the routed total: zero rows
+        const int o = idx - r * octs;
+        reinterpret_cast<uint4*>(p.act)[(static_cast<int64_t>(o >> 3) * n + pos) * 8 + (o & 7)] =
             pos < carry ? permute_octet<T>(v[u]) : make_uint4(0, 0, 0, 0);
       }
     }
