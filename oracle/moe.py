@@ -65,11 +65,15 @@ def moe_layer(hidden: torch.Tensor, topk_ids: torch.Tensor, topk_weights: torch.
     ``w13_f32[e]`` / ``w2_f32[e]`` are the dequantised fp32 weights of expert e
     (``None`` for experts that cannot be routed to); ``w13_f32`` may instead be
     a callable ``e -> (w13, w2)`` that dequantises on demand (``w2_f32`` is
-    then ignored).  With ``round_intermediates`` the gate_up, mid and down
-    tensors are rounded to ``act_dtype`` where the reference stores them.
+    then ignored).  With ``round_intermediates`` the activations are cast to
+    fp16 and the gate_up, mid and down tensors are rounded to fp16, where and
+    as the reference does whatever the model dtype: its GEMM loads the
+    activations ``.to(tl.float16)`` (exq/kernels/moe_int4_kernel.py:199) and
+    stores out1 / mid / out2 as fp16 (:386-410).  ``act_dtype`` is the dtype
+    of the caller's hidden states (the output is cast to it by the caller).
     """
-    rd = act_dtype if round_intermediates else None
-    x = hidden.float()
+    rd = torch.float16 if round_intermediates else None
+    x = _round(hidden.float(), rd)
     t, k = topk_ids.shape
     flat = topk_ids.reshape(-1).long()
     wts = topk_weights.reshape(-1).float()
