@@ -432,13 +432,48 @@ def ep_measure(dev, world, rank, name, steps=50, warmup=5):
     if world > 1:
         dist.all_reduce(wbytes, op=dist.ReduceOp.MAX)
     us = float(sec.item()) * 1e6
+    out = {"model": c.name, "experts": c.n_experts, "top_k": c.top_k, "hidden": c.hidden,
+           "inter": c.inter, "shared": c.n_shared, "tokens_per_rank": t,
+           "experts_per_rank": per, "us_per_step": round(us, 1),
+           "weight_GBps_per_rank": round(float(wbytes.item()) / (us * 1e-6) / 1e9, 1),
+           "tokens_per_s_total": round(world * t / (us * 1e-6), 1)}
+    if world == 1 and name == "mixtral":
+        out["prefill"] = prefill_measure(layer, c, dev)
     del layer, local, shared
     torch.cuda.empty_cache()
-    return {"model": c.name, "experts": c.n_experts, "top_k": c.top_k, "hidden": c.hidden,
-            "inter": c.inter, "shared": c.n_shared, "tokens_per_rank": t,
-            "experts_per_rank": per, "us_per_step": round(us, 1),
-            "weight_GBps_per_rank": round(float(wbytes.item()) / (us * 1e-6) / 1e9, 1),
-            "tokens_per_s_total": round(world * t / (us * 1e-6), 1)}
+    return out
+
+
+def prefill_measure(bank, c, dev, tokens=4096, steps=5):
+    """C4 prefill: the whole Mixtral layer at T=4096 on one GPU (tensor-bound:
+    F = 2*T*k*3*I*H flops), against the measured dense bf16 peak."""
+    import torch
+    from exq_b200.synth import hidden_states, zipf_router
+    ids, w = zipf_router(tokens, c.n_experts, c.top_k, seed=3)
+    x = hidden_states(tokens, c.hidden, seed=3).to(dev, c.act_dtype)
+    ids, w = ids.to(dev), w.to(dev)
+    for _ in range(2):
+        bank(x, ids, w)
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        bank(x, ids, w)
+    e1.record()
+    torch.cuda.synchronize(dev)
+    sec = e0.elapsed_time(e1) / 1e3 / steps
+    flops = 2 * tokens * c.top_k * 3 * c.inter * c.hidden
+    peak = None
+    try:
+        # about 20 ms of timed work: the burst figure
+        peak = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()).get("bf16_tflops")
+    except (OSError, ValueError):
+        pass
+    tf = flops / sec / 1e12
+    return {"tokens": tokens, "ms_per_layer": round(sec * 1e3, 3), "tflops": round(tf, 1),
+            "bound": "tensor", "peak_tflops": peak,
+            "frac": round(tf / peak, 3) if peak else None,
+            "peak_kind": "measured bf16 burst" if peak else None}
 
 
 def profile_case():
