@@ -75,7 +75,9 @@ constexpr int kOffMisc = kOffBar + kNumBars * 8;
 constexpr int kItemTab = 128;  // work items of this CTA decoded into shared memory up front
 constexpr int kOffItems = kOffMisc + 64;
 constexpr int kItemBytes = 48;  // sizeof(Item)
-constexpr int kSmemBytes = kOffItems + kItemTab * kItemBytes + 1024;  // + slack to align the base to 1024 B
+constexpr int kHistBuckets = 1024;  // experts the in-kernel tile list handles
+constexpr int kOffHist = kOffItems + kItemTab * kItemBytes;  // 3 x (kHistBuckets + 1) ints
+constexpr int kSmemBytes = kOffHist + 3 * (kHistBuckets + 1) * 4 + 1024;  // + slack to align the base to 1024 B
 
 enum : int { kTierBF16 = EXQ_TIER_BF16, kTierINT8 = EXQ_TIER_INT8, kTierINT4 = EXQ_TIER_INT4 };
 
@@ -96,6 +98,12 @@ struct TcParams {
   int k;
   int nblocks;
   int weights_early;      // 1: the predecessor kernel writes only the activations (see below)
+  // tiles_from_ids: build the tile list from the routing ids (below) instead of
+  // reading tile_info, so the weight stream need not wait for the predecessor
+  int tiles_from_ids;
+  const void* ids;        // [T, top_k] expert ids
+  int ids_dtype, top_k, spt, n_routed, n_buckets;
+  int64_t n_slots;
   int64_t n_pos;          // rows of the activation / mid buffers
   void* out;
   int64_t out_stride;
@@ -369,19 +377,101 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
   tc_fence_after();
   const uint32_t tmem = misc[0];
   // everything above overlaps the tail of the previous kernel in the stream.
-  // With p.weights_early the tile list was written two launches back, so only
-  // the activation producer (which reads the predecessor's output) waits: the
-  // weight producer and the dequantisers start on the first slots right away.
-  if (!p.weights_early) pdl_wait();
+  // With p.weights_early the tile list was written two launches back; with
+  // p.tiles_from_ids the CTA builds it from the routing ids.  Either way only
+  // the activation producer (which reads the predecessor's output) waits, and
+  // the weight producer and the dequantisers start on the first slots at once.
+  const bool early = p.weights_early || p.tiles_from_ids;
+  if (!early) pdl_wait();
   pdl_trigger();
-  const int n_tiles = min(*p.n_tiles_ptr, p.max_tiles);
-  const int n_items = n_tiles * p.nblocks;
-  // decode this CTA's items once, so no role waits on global loads at an item boundary
   Item* items_tab = reinterpret_cast<Item*>(gbase + kOffItems);
-  for (int t = threadIdx.x; t < kItemTab; t += kThreads) {
-    const int item = static_cast<int>(blockIdx.x) + t * static_cast<int>(gridDim.x);
-    if (item < n_items) items_tab[t] = make_item(p, item, n_tiles);
+  int n_tiles;
+  if (p.tiles_from_ids) {
+    // The same tile list the routing kernel writes: experts in order, rows in
+    // tiles of kMaxN from each expert's first sorted position.  Per-expert
+    // counts (an order-independent histogram), then two exclusive scans.
+    int* cnt = reinterpret_cast<int*>(gbase + kOffHist);
+    int* rbase = cnt + kHistBuckets + 1;
+    int* tstart = rbase + kHistBuckets + 1;
+    const int nbk = p.n_buckets;
+    for (int i = threadIdx.x; i < nbk; i += kThreads) cnt[i] = 0;
+    __syncthreads();
+    for (int i = threadIdx.x; i < p.n_slots; i += kThreads) {
+      const int t = i / p.spt, j = i - t * p.spt;
+      int e = p.n_routed + (j - p.top_k);  // always-on shared expert
+      if (j < p.top_k) {
+        const int64_t v = load_index(p.ids, p.ids_dtype, static_cast<int64_t>(t) * p.top_k + j);
+        e = (v >= 0 && v < p.n_routed) ? static_cast<int>(v) : -1;  // dropped (flagged by routing)
+      }
+      if (e >= 0) atomicAdd(&cnt[e], 1);
+    }
+    __syncthreads();
+    if (warp == 0) {
+      const int per = (nbk + 31) / 32;
+      const int lo = lane * per, hi = min(nbk, lo + per);
+      int rs = 0, ts = 0;
+      for (int e = lo; e < hi; ++e) {
+        rs += cnt[e];
+        ts += (cnt[e] + kMaxN - 1) / kMaxN;
+      }
+      int rx = rs, tx = ts;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, rx, o);
+        const int z = __shfl_up_sync(0xffffffffu, tx, o);
+        if (lane >= o) {
+          rx += y;
+          tx += z;
+        }
+      }
+      if (lane == 31) tstart[nbk] = tx;
+      rx -= rs;
+      tx -= ts;
+      for (int e = lo; e < hi; ++e) {
+        rbase[e] = rx;
+        tstart[e] = tx;
+        rx += cnt[e];
+        tx += (cnt[e] + kMaxN - 1) / kMaxN;
+      }
+    }
+    __syncthreads();
+    n_tiles = min(tstart[nbk], p.max_tiles);
+    const int n_items0 = n_tiles * p.nblocks;
+    for (int t = threadIdx.x; t < kItemTab; t += kThreads) {
+      const int item = static_cast<int>(blockIdx.x) + t * static_cast<int>(gridDim.x);
+      if (item >= n_items0) continue;
+      const int tile = item % n_tiles;
+      int lo = 0, hi = nbk - 1;  // last expert whose first tile is <= tile
+      while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (tstart[mid] <= tile) lo = mid;
+        else hi = mid - 1;
+      }
+      const int lt = tile - tstart[lo];
+      Item it;
+      it.nb = item / n_tiles;
+      it.e = lo;
+      it.m0 = rbase[lo] + lt * kMaxN;
+      it.mc = min(kMaxN, cnt[lo] - lt * kMaxN);
+      const int code = __ldg(p.expert_slot + lo);
+      it.tier = code >> 24;
+      it.idx = code & 0xFFFFFF;
+      it.n = max(16, (it.mc + 15) & ~15);
+      it.r0 = p.gate_up ? it.nb * 64 : it.nb * 128;
+      it.sps = stages_per_slot(it.tier);
+      it.per_slot = b_stages_per_slot(it.n);
+      it.pad0 = it.pad1 = 0;
+      items_tab[t] = it;
+    }
+  } else {
+    n_tiles = min(*p.n_tiles_ptr, p.max_tiles);
+    // decode this CTA's items once, so no role waits on global loads at an item boundary
+    for (int t = threadIdx.x; t < kItemTab; t += kThreads) {
+      const int item = static_cast<int>(blockIdx.x) + t * static_cast<int>(gridDim.x);
+      if (item < n_tiles * p.nblocks) items_tab[t] = make_item(p, item, n_tiles);
+    }
   }
+  const int n_items = n_tiles * p.nblocks;
   __syncthreads();
   auto aborted = [&]() { return misc[1] != 0; };
   auto do_abort = [&]() { misc[1] = 1; };
@@ -448,7 +538,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
     }
   } else if (warp == kWarpB) {
     // ---------------------------------------------------------- activations
-    if (p.weights_early) pdl_wait();
+    if (early) pdl_wait();
     Ring r;
     int issued = 0;
     for (int item = blockIdx.x, li = 0; item < n_items && !aborted(); item += gridDim.x, ++li) {
@@ -1142,6 +1232,19 @@ extern "C" int exq_moe_layer_forward_range(const exq_moe_weights* w, const void*
     // down right after gate_up in this call: its tile list predates gate_up
     p.weights_early = proj == 1 && first_stage <= 2;
     const int64_t max_items = ws.max_tiles * p.nblocks;
+    // gate_up right after the fused routing in this call: build the tiles from
+    // the ids (complete before routing started) and stream weights at once;
+    // every CTA's items must fit its shared table
+    const int64_t grid = max_items < num_sms() ? max_items : num_sms();
+    p.tiles_from_ids = proj == 0 && fused && first_stage == 0 && n_total <= tc::kHistBuckets &&
+                       max_items <= static_cast<int64_t>(tc::kItemTab) * (grid > 0 ? grid : 1);
+    p.ids = topk_ids;
+    p.ids_dtype = ids_dtype;
+    p.top_k = top_k;
+    p.spt = spt;
+    p.n_routed = w->n_routed;
+    p.n_buckets = n_total;
+    p.n_slots = n_slots;
     st = tc::launch_tc(p, static_cast<int>(max_items < INT32_MAX ? max_items : INT32_MAX), s);
     if (st != EXQ_OK) return st;
   }
