@@ -266,7 +266,11 @@ class ExpertBank:
     def forward(self, hidden_states: torch.Tensor, topk_ids: torch.Tensor,
                 topk_weights: torch.Tensor, out: torch.Tensor | None = None,
                 workspace: torch.Tensor | None = None) -> torch.Tensor:
-        """route -> prep -> gate_up -> down -> weighted combine (5 launches)."""
+        """The five stages route -> prep -> gate_up -> down -> weighted combine.
+
+        Up to 4096 (token, expert) slots the route and prep stages are one
+        fused launch and gate_up rebuilds its tile list from the ids, so a
+        call is four launches; above that it is five."""
         return self.forward_range(hidden_states, topk_ids, topk_weights, 0, 5, out, workspace)
 
     def forward_range(self, hidden_states, topk_ids, topk_weights, first: int, end: int,

@@ -132,6 +132,23 @@ def test_layer_mixtral_long_k_vs_oracle(cuda):
     assert OM.rel_l2(y, ref) < TOL
 
 
+@pytest.mark.parametrize("tiers", [None, "mixed"])
+def test_layer_above_fused_routing_limit(cuda, tiers):
+    """More than 4096 slots (Qwen3 shape, 600 tokens x top-8 = 4800): the
+    routing runs as the single-CTA sort plus the separate activation prep, the
+    GEMM builds no tile list of its own; checked on a token sample, all tiers."""
+    from exq_b200.synth import CONFIGS, hidden_states, tier_plan, zipf_router
+    c0 = CONFIGS["qwen3"]
+    bank, c = _bank("qwen3", cuda, tiers=tier_plan(c0.n_experts, seed=4) if tiers else None)
+    ids, w = zipf_router(600, 128, 8, seed=21)
+    x = hidden_states(600, c.hidden, seed=21)
+    assert ids.numel() > 4096
+    y = bank(x.to(cuda), ids.to(cuda), w.to(cuda)).cpu()
+    sample = torch.tensor([0, 3, 299, 300, 598, 599])
+    ref = oracle_layer(bank, x, ids, w, tokens=sample)
+    assert OM.rel_l2(y[sample], ref) < TOL
+
+
 def test_layer_full_size_sampled_tokens(cuda):
     """Qwen3 at 256 tokens (all 128 experts touched, hot experts > 32 rows):
     every token's output depends on that token only, so a sample of tokens is
