@@ -612,7 +612,10 @@ def main():
                      "frac": round(gu_ach / peak, 3),
                      "traffic": (traffic or {}).get("gate_up_bytes_per_launch"),
                      "algorithmic_bytes": int(gu_bytes), "peak_kind": peak_kind,
-                     "per_launch_us": {k: round(v * 1e6, 2) for k, v in per_kernel.items()},
+                     # event-to-event device time of each stage; with <= 4096
+                     # slots the prep stage launches nothing and is left out
+                     "per_launch_us": {k: round(v * 1e6, 2) for k, v in per_kernel.items()
+                                       if k != "prep" or c["tokens"] * c["top_k"] > 4096},
                      "down_achieved": round(dn_bytes / per_kernel["down"] / 1e9, 1)},
         "cpu_baseline": cpu,
         "e2e": {"value": round(e2e_val, 1), "unit": UNIT, "h2d_bytes_per_step": h2d,
