@@ -337,34 +337,58 @@ def gemm_timing(banks, inputs, dev, reps=40):
 
 def e2e_timing(banks, inputs, dev, steps, warmup):
     """Same metric through the public API with host (pinned) buffers: every
-    step copies its inputs host->device and its output device->host."""
+    step copies its inputs host->device and its output device->host.  The
+    copies run on their own streams, so step i+1's inputs travel while step i
+    computes and step i's output returns while step i+1 computes (one set of
+    device buffers per rotating layer, guarded by events)."""
     import torch
+    L = len(banks)
     hosts = []
     for (x, ids, w, _) in inputs:
         hosts.append((x.cpu().pin_memory(), ids.cpu().pin_memory(), w.cpu().pin_memory(),
                       torch.empty(x.shape, dtype=x.dtype).pin_memory()))
-    dbufs = [(torch.empty_like(x), torch.empty_like(ids), torch.empty_like(w))
+    dbufs = [(torch.empty_like(x), torch.empty_like(ids), torch.empty_like(w), torch.empty_like(x))
              for (x, ids, w, _) in inputs]
-    stream = torch.cuda.current_stream(dev)
+    s_c = torch.cuda.current_stream(dev)
+    s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    ev_in = [torch.cuda.Event() for _ in range(L)]     # inputs of layer slot li landed
+    ev_done = [torch.cuda.Event() for _ in range(L)]   # layer slot li computed
+    ev_out = [torch.cuda.Event() for _ in range(L)]    # its output is back on the host
+    used = [False] * L
 
     def one(i):
-        li = i % len(banks)
+        li = i % L
         hx, hi, hw, hy = hosts[li]
-        dx, di, dw = dbufs[li]
-        dx.copy_(hx, non_blocking=True)
-        di.copy_(hi, non_blocking=True)
-        dw.copy_(hw, non_blocking=True)
-        y = banks[li](dx, di, dw)
-        hy.copy_(y, non_blocking=True)
+        dx, di, dw, dy = dbufs[li]
+        with torch.cuda.stream(s_in):
+            if used[li]:
+                s_in.wait_event(ev_done[li])   # the previous step on these buffers read them
+            dx.copy_(hx, non_blocking=True)
+            di.copy_(hi, non_blocking=True)
+            dw.copy_(hw, non_blocking=True)
+            ev_in[li].record(s_in)
+        s_c.wait_event(ev_in[li])
+        if used[li]:
+            s_c.wait_event(ev_out[li])         # its output left dy
+        banks[li](dx, di, dw, out=dy)
+        ev_done[li].record(s_c)
+        with torch.cuda.stream(s_out):
+            s_out.wait_event(ev_done[li])
+            hy.copy_(dy, non_blocking=True)
+            ev_out[li].record(s_out)
+        used[li] = True
 
     for i in range(warmup):
         one(i)
     torch.cuda.synchronize(dev)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
+    e0.record(s_c)
+    s_in.wait_event(e0)
+    s_out.wait_event(e0)
     for i in range(steps):
         one(i)
-    e1.record(stream)
+    s_c.wait_stream(s_out)                     # the last output is on the host
+    e1.record(s_c)
     torch.cuda.synchronize(dev)
     x, ids, w, _ = inputs[0]
     h2d = x.numel() * x.element_size() + ids.numel() * ids.element_size() + w.numel() * w.element_size()
