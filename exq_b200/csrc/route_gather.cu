@@ -4,21 +4,20 @@
 // exq/runtime/sglang_backend.py:102-131 (moe_align_block_size, then the
 // hidden-state gather the Triton GEMM performs through sorted_token_ids).
 //
-// Every CTA recomputes the same stable counting sort of the T*(top_k+shared)
-// slots in shared memory (a few thousand elements; the ids are read from L2),
-// so all CTAs agree on the placement without a grid-wide barrier.  The sorted
-// positions are then split into contiguous chunks, one per CTA, and each CTA
-//   - copies the hidden-state rows of its positions into the fp16 activation
-//     buffer, converting bf16 and permuting every octet of k to
-//     [0,4,1,5,2,6,3,7] (the k order of the dequantised weights),
-//   - writes the router weight and the slot -> position map of its positions.
-// CTA 0 also writes the GEMM tile list, the expert ends and the -1 entries of
-// dropped slots (expert id out of range).
-//
-// The sort is the same three-pass scheme as route.cu (per-warp histograms
-// built with shared-memory atomics, a column scan plus a block scan, stable
-// placement), with 8 warps instead of 32; pass 3 ranks lanes with one ballot per
-// bit of the expert id.
+// Every CTA reads all T*(top_k+shared) slots' expert ids (a few thousand, from
+// L2) and computes the same bucket counts and bucket bases in shared memory,
+// so all CTAs agree on the stable counting sort without a grid-wide barrier.
+// The slots are split into contiguous chunks, one per CTA; a CTA places only
+// its own chunk (position = bucket base + the bucket's slots before the chunk
+// + the slot's rank among the chunk's slots of its bucket, by match_any on one
+// warp) and, slot by slot,
+//   - copies the hidden-state row into the fp16 activation buffer at the
+//     slot's sorted position, converting bf16 and permuting every octet of k
+//     to [0,4,1,5,2,6,3,7] (the k order of the dequantised weights),
+//   - writes the slot -> position map and the router weight at the position.
+// CTA 0 also writes the GEMM tile list and the expert ends; dropped slots
+// (expert id out of range) map to -1, and the positions past the routed total
+// get zero rows.
 #include <type_traits>
 
 #include "internal.cuh"
@@ -29,7 +28,7 @@ constexpr int kRgThreads = 256;
 constexpr int kRgWarps = kRgThreads / 32;
 
 size_t route_gather_smem_bytes(int n_buckets, int64_t n) {
-  return sizeof(int) * (static_cast<size_t>(kRgWarps + 2) * n_buckets + 34 + 3 * n);
+  return sizeof(int) * (static_cast<size_t>(4) * n_buckets + 34 + 3 * n);
 }
 
 namespace {
@@ -62,20 +61,6 @@ __device__ __forceinline__ int rg_exclusive_scan(int v, int* tmp, int* excl) {
   return total;
 }
 
-// Lanes of the warp holding the same bucket as this lane (e = -1 for none):
-// one ballot per bit of the bucket id plus one for validity.
-__device__ __forceinline__ unsigned same_bucket_lanes(int e, int nbits) {
-  const bool valid = e >= 0;
-  const unsigned v = __ballot_sync(0xffffffffu, valid);
-  unsigned m = valid ? v : ~v;
-  for (int b = 0; b < nbits; ++b) {
-    const bool bit = valid && ((e >> b) & 1);
-    const unsigned x = __ballot_sync(0xffffffffu, bit);
-    m &= bit ? x : ~x;
-  }
-  return m;
-}
-
 // fp16 or bf16 octet -> fp16 octet in [0,4,1,5,2,6,3,7] order
 template <typename T>
 __device__ __forceinline__ uint4 permute_octet(uint4 v) {
@@ -101,20 +86,20 @@ __global__ void __launch_bounds__(kRgThreads) route_gather_kernel(const RouteGat
   extern __shared__ int smem[];
   const int nb = p.n_buckets;
   const int n = static_cast<int>(p.n);
-  int* cnt = smem;                   // [8 warps][nb] counts, then write cursors
-  int* base = cnt + kRgWarps * nb;   // [nb] first sorted position of every bucket
+  int* cnt_all = smem;               // [nb] slots of every bucket
+  int* cnt_pre = cnt_all + nb;       // [nb] of them before this CTA's chunk, then cursors
+  int* base = cnt_pre + nb;          // [nb] first sorted position of every bucket
   int* tstart = base + nb;           // [nb] first tile of every bucket
   int* tmp = tstart + nb;            // [33] scan scratch, [33] routed total
   int* bkt = tmp + 34;               // [n] bucket of every slot (-1: dropped)
-  int* slot_at = bkt + n;            // [n] slot at every sorted position
-  float* wslot = reinterpret_cast<float*>(slot_at + n);  // [n] router weight of every slot
+  int* slot_pos = bkt + n;           // [chunk] sorted position of this CTA's slots (-1: dropped)
+  float* wslot = reinterpret_cast<float*>(slot_pos + n);  // [n] router weight of every slot
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int nbits = 32 - __clz(nb > 1 ? nb - 1 : 1);
 
   pdl_wait();
   pdl_trigger();
 
-  for (int i = threadIdx.x; i < kRgWarps * nb; i += kRgThreads) cnt[i] = 0;
+  for (int i = threadIdx.x; i < 2 * nb; i += kRgThreads) cnt_all[i] = 0;
   // bucket of every slot; the id loads of 8 slots are issued before any is used
   for (int i0 = threadIdx.x; i0 < n; i0 += 8 * kRgThreads) {
     int64_t v[8];
@@ -146,29 +131,29 @@ __global__ void __launch_bounds__(kRgThreads) route_gather_kernel(const RouteGat
   }
   __syncthreads();
 
-  // pass 1: per-warp histograms over contiguous segments (counts do not
-  // depend on the order of the atomics)
-  const int per_warp = ((n + kRgWarps - 1) / kRgWarps + 31) / 32 * 32;
-  const int seg_lo = warp * per_warp, seg_hi = min(n, seg_lo + per_warp);
-  for (int i = seg_lo + lane; i < seg_hi; i += 32) {
+  // This CTA's slots [s0, s1).  A slot's sorted position is the first
+  // position of its bucket, plus the slots of the same bucket before s0, plus
+  // its rank among this chunk's slots of that bucket (a stable counting sort,
+  // with only the chunk's own slots placed here).
+  const int chunk = (n + static_cast<int>(gridDim.x) - 1) / static_cast<int>(gridDim.x);
+  const int s0 = min(n, static_cast<int>(blockIdx.x) * chunk), s1 = min(n, s0 + chunk);
+
+  // pass 1: bucket counts of all slots and of the slots before s0 (order-free)
+  for (int i = threadIdx.x; i < n; i += kRgThreads) {
     const int e = bkt[i];
-    if (e >= 0) atomicAdd(&cnt[warp * nb + e], 1);
+    if (e >= 0) {
+      atomicAdd(&cnt_all[e], 1);
+      if (i < s0) atomicAdd(&cnt_pre[e], 1);
+    }
   }
   __syncthreads();
 
-  // pass 2: per-(warp, bucket) offsets, bucket bases and tile starts
+  // pass 2: bucket bases and tile starts (one scan of (tiles << 16 | rows):
+  // both stay below 2^16, n <= 4096)
   int carry = 0, tile_carry = 0;
   for (int c0 = 0; c0 < nb; c0 += kRgThreads) {
     const int e = c0 + threadIdx.x;
-    int total = 0;
-    if (e < nb) {
-      for (int w = 0; w < kRgWarps; ++w) {
-        const int v = cnt[w * nb + e];
-        cnt[w * nb + e] = total;
-        total += v;
-      }
-    }
-    // one scan of (tiles << 16 | rows): both stay below 2^16 (n <= 4096)
+    const int total = e < nb ? cnt_all[e] : 0;
     int packed_excl;
     const int packed = rg_exclusive_scan(((total + p.mt - 1) / p.mt) << 16 | total, tmp, &packed_excl);
     const int sum = packed & 0xFFFF, tsum = packed >> 16;
@@ -176,29 +161,31 @@ __global__ void __launch_bounds__(kRgThreads) route_gather_kernel(const RouteGat
     if (e < nb) {
       base[e] = carry + excl;
       tstart[e] = tile_carry + texcl;
-      for (int w = 0; w < kRgWarps; ++w) cnt[w * nb + e] += carry + excl;
     }
     carry += sum;
     tile_carry += tsum;
   }
   __syncthreads();
 
-  // pass 3: stable placement
-  const unsigned lt_mask = (1u << lane) - 1u;
-  for (int b0 = seg_lo; b0 < seg_hi; b0 += 32) {
-    const int i = b0 + lane;
-    const int e = i < seg_hi ? bkt[i] : -1;
-    const unsigned peers = same_bucket_lanes(e, nbits);
-    if (e >= 0) slot_at[cnt[warp * nb + e] + __popc(peers & lt_mask)] = i;
-    __syncwarp();
-    if (e >= 0 && lane == __ffs(peers) - 1) cnt[warp * nb + e] += __popc(peers);
-    __syncwarp();
+  // pass 3: the chunk's slots in order, 32 at a time, on warp 0
+  if (warp == 0) {
+    const unsigned lt_mask = (1u << lane) - 1u;
+    for (int b0 = s0; b0 < s1; b0 += 32) {
+      const int i = b0 + lane;
+      const int e = i < s1 ? bkt[i] : -1;
+      const unsigned peers = __match_any_sync(0xffffffffu, e);
+      if (e >= 0) slot_pos[i - s0] = base[e] + cnt_pre[e] + __popc(peers & lt_mask);
+      else if (i < s1) slot_pos[i - s0] = -1;
+      __syncwarp();
+      if (e >= 0 && lane == __ffs(peers) - 1) cnt_pre[e] += __popc(peers);
+      __syncwarp();
+    }
   }
   __syncthreads();
 
   if (blockIdx.x == 0) {
     for (int e = threadIdx.x; e < nb; e += kRgThreads) {
-      const int c = ((e + 1 < nb) ? base[e + 1] : carry) - base[e];
+      const int c = cnt_all[e];
       if (p.ends) p.ends[e] = base[e];
       for (int t = 0; t * p.mt < c; ++t) {
         const int64_t ti = tstart[e] + t;
@@ -213,45 +200,48 @@ __global__ void __launch_bounds__(kRgThreads) route_gather_kernel(const RouteGat
       if (p.ends) p.ends[nb] = carry;
       p.n_tiles[0] = tile_carry;
     }
-    for (int i = threadIdx.x; i < n; i += kRgThreads)
-      if (bkt[i] < 0) p.pos_of_slot[i] = -1;
   }
-
-  // this CTA's chunk of sorted positions
-  const int chunk = (n + gridDim.x - 1) / gridDim.x;
-  const int p0 = blockIdx.x * chunk, p1 = min(n, p0 + chunk);
-  for (int pos = p0 + threadIdx.x; pos < p1; pos += kRgThreads) {
-    if (pos >= carry) continue;
-    const int slot = slot_at[pos];
-    p.pos_of_slot[slot] = pos;
-    p.sorted_w[pos] = wslot[slot];
+  for (int i = s0 + threadIdx.x; i < s1; i += kRgThreads) {
+    const int pos = slot_pos[i - s0];
+    p.pos_of_slot[i] = pos;
+    if (pos >= 0) p.sorted_w[pos] = wslot[i];
   }
-  // row copies: each thread issues 8 independent 16-byte loads before storing
+  // row copies, slot by slot: each thread issues 8 independent 16-byte loads
+  // before storing
   const int octs = static_cast<int>(p.hidden_size / 8);
   const T* hid = static_cast<const T*>(p.hidden);
-  const int total = max(0, p1 - p0) * octs;
+  const int total = (s1 - s0) * octs;
   constexpr int kU = 8;
   for (int i0 = threadIdx.x; i0 < total; i0 += kU * kRgThreads) {
     uint4 v[kU];
 #pragma unroll
     for (int u = 0; u < kU; ++u) {  // unconditional loads (row 0 stands in for unused ones)
       const int idx = i0 + u * kRgThreads;
-      const int r = idx / octs, pos = p0 + r;
-      const bool used = idx < total && pos < carry;
-      const int64_t tok = used ? slot_at[pos] / p.spt : 0;
+      const int r = idx / octs;
+      const bool used = idx < total && slot_pos[r] >= 0;
+      const int64_t tok = used ? (s0 + r) / p.spt : 0;
       v[u] = __ldg(reinterpret_cast<const uint4*>(hid + tok * p.hidden_size) + (used ? idx - r * octs : 0));
     }
 #pragma unroll
     for (int u = 0; u < kU; ++u) {
       const int idx = i0 + u * kRgThreads;
       if (idx < total) {
-        const int r = idx / octs, pos = p0 + r;
-        // act is stage-major [H/64][n][64]; positions past the routed total: zero rows
+        const int r = idx / octs, pos = slot_pos[r];
+        if (pos < 0) continue;  // a dropped slot has no row
+        // act is stage-major [H/64][n][64]
         const int o = idx - r * octs;
         reinterpret_cast<uint4*>(p.act)[(static_cast<int64_t>(o >> 3) * n + pos) * 8 + (o & 7)] =
-            pos < carry ? permute_octet<T>(v[u]) : make_uint4(0, 0, 0, 0);
+            permute_octet<T>(v[u]);
       }
     }
+  }
+  // positions past the routed total (as many as dropped slots): zero rows
+  const int zc = (n - carry + static_cast<int>(gridDim.x) - 1) / static_cast<int>(gridDim.x);
+  const int z0 = carry + static_cast<int>(blockIdx.x) * zc, z1 = min(n, z0 + zc);
+  for (int idx = threadIdx.x; idx < max(0, z1 - z0) * octs; idx += kRgThreads) {
+    const int pos = z0 + idx / octs, o = idx % octs;
+    reinterpret_cast<uint4*>(p.act)[(static_cast<int64_t>(o >> 3) * n + pos) * 8 + (o & 7)] =
+        make_uint4(0, 0, 0, 0);
   }
 }
 
