@@ -90,18 +90,26 @@ __device__ __forceinline__ void store4<__nv_bfloat16>(__nv_bfloat16* o, float4 a
   *reinterpret_cast<uint2*>(o) = v;
 }
 
-// The token's slot positions are staged in shared memory first so that the
-// row loads of all its slots are independent and issue together.
+// y[t] = sum over the token's slots j, in slot order, of w[t, j] * partial[pos]
+// (w = 1 for the always-on shared experts; product and sum rounded
+// separately in fp32).  The token's slot positions and weights are staged in
+// shared memory first so that the row loads of all its slots are independent
+// and issue together.
 template <typename Tout>
 __global__ void combine_partials_kernel(const float* __restrict__ partial, int64_t H,
                                         const int32_t* __restrict__ pos_of_slot,
+                                        const void* __restrict__ topk_w, int w_dtype, int top_k,
                                         int64_t n_tokens, int spt, Tout* __restrict__ out) {
-  extern __shared__ int32_t spos[];  // [spt]
+  extern __shared__ int32_t spos[];  // [spt] positions, then [spt] weights
+  float* sw = reinterpret_cast<float*>(spos + spt);
   pdl_wait();
   pdl_trigger();
   const int64_t hv = H / 4;
   for (int64_t t = blockIdx.x; t < n_tokens; t += gridDim.x) {
-    for (int j = threadIdx.x; j < spt; j += blockDim.x) spos[j] = pos_of_slot[t * spt + j];
+    for (int j = threadIdx.x; j < spt; j += blockDim.x) {
+      spos[j] = pos_of_slot[t * spt + j];
+      sw[j] = j < top_k ? load_as_f32(topk_w, w_dtype, t * top_k + j) : 1.0f;
+    }
     __syncthreads();
     for (int64_t c = threadIdx.x; c < hv; c += blockDim.x) {
       float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -115,10 +123,11 @@ __global__ void combine_partials_kernel(const float* __restrict__ partial, int64
         }
 #pragma unroll
         for (int u = 0; u < 8; ++u) {  // sum in slot order
-          acc.x += v[u].x;
-          acc.y += v[u].y;
-          acc.z += v[u].z;
-          acc.w += v[u].w;
+          const float wj = j0 + u < spt ? sw[j0 + u] : 0.f;
+          acc.x = __fadd_rn(acc.x, __fmul_rn(wj, v[u].x));
+          acc.y = __fadd_rn(acc.y, __fmul_rn(wj, v[u].y));
+          acc.z = __fadd_rn(acc.z, __fmul_rn(wj, v[u].z));
+          acc.w = __fadd_rn(acc.w, __fmul_rn(wj, v[u].w));
         }
       }
       store4<Tout>(out + t * H + 4 * c, acc);
@@ -212,20 +221,20 @@ inline int grid_for(int64_t work, int threads, int max_blocks_per_sm = 8) {
 }
 
 int launch_combine_partials(const float* partial, int64_t H, const int32_t* pos_of_slot,
-                            int64_t n_tokens, int spt, void* out, int dtype,
-                            cudaStream_t stream) {
+                            const void* topk_w, int w_dtype, int top_k, int64_t n_tokens, int spt,
+                            void* out, int dtype, cudaStream_t stream) {
   if (n_tokens == 0) return EXQ_OK;
   const int threads = static_cast<int>(H / 4 < 256 ? (H / 4 < 32 ? 32 : H / 4) : 256);
   const int grid = static_cast<int>(n_tokens < 65535 ? n_tokens : 65535);
   cudaError_t e;
   if (dtype == EXQ_F16)
     e = launch_pdl(combine_partials_kernel<__half>, dim3(grid), dim3(threads),
-                   sizeof(int32_t) * spt, stream, partial, H, pos_of_slot, n_tokens, spt,
-                   static_cast<__half*>(out));
+                   2 * sizeof(int32_t) * spt, stream, partial, H, pos_of_slot, topk_w, w_dtype,
+                   top_k, n_tokens, spt, static_cast<__half*>(out));
   else
     e = launch_pdl(combine_partials_kernel<__nv_bfloat16>, dim3(grid), dim3(threads),
-                   sizeof(int32_t) * spt, stream, partial, H, pos_of_slot, n_tokens, spt,
-                   static_cast<__nv_bfloat16*>(out));
+                   2 * sizeof(int32_t) * spt, stream, partial, H, pos_of_slot, topk_w, w_dtype,
+                   top_k, n_tokens, spt, static_cast<__nv_bfloat16*>(out));
   if (e != cudaSuccess) {
     set_error("combine_partials_kernel: %s", cudaGetErrorString(e));
     return EXQ_ERR_CUDA;

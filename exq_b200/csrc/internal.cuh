@@ -140,9 +140,10 @@ struct GemmParams {
 int launch_gemm(const GemmParams& p, int act_dtype, int max_items, cudaStream_t stream);
 
 // ------------------------------------------------------------- elementwise
+// y[t] = sum_j w[t, j] * partial[pos_of_slot[t * spt + j]] (w = 1 past top_k).
 int launch_combine_partials(const float* partial, int64_t H, const int32_t* pos_of_slot,
-                            int64_t n_tokens, int spt, void* out, int dtype,
-                            cudaStream_t stream);
+                            const void* topk_w, int w_dtype, int top_k, int64_t n_tokens, int spt,
+                            void* out, int dtype, cudaStream_t stream);
 
 uint32_t* device_status_ptr();
 

@@ -684,24 +684,19 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
         }
       } else {
         const int h = it.r0 + row;
-        float s = 1.f;
-        if (it.tier == kTierINT8) s = __half2float(p.s8[static_cast<int64_t>(it.idx) * p.n_rows + h]);
-        // router weights of the item's tokens, loaded once: lane l holds tokens
-        // l and 32 + l, every token's weight is then a shuffle away
-        const float w_lo = lane < it.mc ? __ldg(p.sorted_w + it.m0 + lane) : 0.f;
-        const float w_hi = 32 + lane < it.mc ? __ldg(p.sorted_w + it.m0 + 32 + lane) : 0.f;
         float* prow = static_cast<float*>(p.out) + static_cast<int64_t>(it.m0) * p.out_stride + h;
+        // the router weights are applied by the combine; INT8 rows carry a scale
+        const float s = it.tier == kTierINT8
+                            ? __half2float(p.s8[static_cast<int64_t>(it.idx) * p.n_rows + h])
+                            : 1.f;
         for (int c = 0; c < it.n; c += 16) {
           uint32_t v[16];
           tmem_ld16(taddr + c, v);
           tmem_wait_ld();
-          const float wsrc = c < 32 ? w_lo : w_hi;
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
             const int tok = c + i;
-            const float wt = __shfl_sync(0xffffffffu, wsrc, tok & 31);
-            if (tok < it.mc)
-              prow[static_cast<int64_t>(tok) * p.out_stride] = __uint_as_float(v[i]) * s * wt;
+            if (tok < it.mc) prow[static_cast<int64_t>(tok) * p.out_stride] = __uint_as_float(v[i]) * s;
           }
         }
       }
@@ -1249,6 +1244,7 @@ extern "C" int exq_moe_layer_forward_range(const exq_moe_weights* w, const void*
     if (st != EXQ_OK) return st;
   }
   if (first_stage <= 4 && end_stage > 4)
-    return launch_combine_partials(ws.partial, H, ws.pos_of_slot, n_tokens, spt, out, act_dtype, s);
+    return launch_combine_partials(ws.partial, H, ws.pos_of_slot, topk_weights, w_dtype, top_k,
+                                   n_tokens, spt, out, act_dtype, s);
   return EXQ_OK;
 }
