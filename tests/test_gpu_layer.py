@@ -93,6 +93,23 @@ def test_layer_int4_vs_oracle(cuda, cfg, t):
     assert OM.rel_l2(y, ref) < TOL
 
 
+@pytest.mark.parametrize("wdt", [torch.float16, torch.bfloat16])
+def test_layer_router_weight_dtypes(cuda, wdt):
+    """The combine reads the router weights in the caller's dtype (fp32, fp16 or
+    bf16), as the reference's combine does; a heavy expert (tiles of 64) and
+    light ones in the same call."""
+    from exq_b200.synth import hidden_states, zipf_router
+    bank, c = _bank("qwen3", cuda, n_experts=32)
+    ids, w = zipf_router(96, 32, 8, seed=31)
+    x = hidden_states(96, c.hidden, seed=31)
+    wq = w.to(wdt)
+    y = bank(x.to(cuda), ids.to(cuda), wq.to(cuda))
+    ref = oracle_layer(bank, x, ids, wq.float())
+    assert OM.rel_l2(y, ref) < TOL
+    y32 = bank(x.to(cuda), ids.to(cuda), wq.float().to(cuda))
+    assert torch.equal(y, y32)  # the same weight values give the same bits
+
+
 def test_layer_mixed_tiers_vs_oracle(cuda):
     """6 BF16 / 13 INT8 / 45 INT4 experts in one launch."""
     from exq_b200.synth import hidden_states, tier_plan, zipf_router
