@@ -8,15 +8,16 @@ tokens to their experts with one all-to-all each way:
 1. one kernel (``exq_ep_pack``) groups the (token, expert) slots of this
    rank's tokens by destination rank, copies their hidden rows into a send
    buffer and counts them; an all-to-all of the counts tells every rank what
-   it receives (the step's one host synchronisation, for NCCL's split sizes);
+   it receives (the step's one host synchronisation, for NCCL's split sizes;
+   the shared experts, which every rank holds and runs on its own tokens,
+   are computed while the host waits for the counts);
 2. the rows and their expert index local to the destination go out in
    all-to-alls;
 3. each rank runs its experts on the rows it received with the fused layer
    kernel (every received row is a token with one expert of weight 1);
 4. the expert outputs return by the reverse all-to-all, in send order;
 5. the owner of each token applies the router weights and sums its slots,
-   plus the shared experts (every rank holds them and runs them on its own
-   tokens), in one kernel (``exq_ep_combine``).
+   plus the shared experts' output, in one kernel (``exq_ep_combine``).
 
 Rank r owns routed experts [r*E/P, (r+1)*E/P).  Counts travel to the host
 once per call to size the exchange, so a call is not CUDA-graph capturable.
@@ -93,10 +94,19 @@ class ExpertParallelLayer:
         if local_bank is not None and getattr(local_bank, "n_routed", self.per_rank) != self.per_rank:
             raise ValueError(f"local bank holds {local_bank.n_routed} experts, rank {self.rank} "
                              f"owns {self.per_rank}")
+        self._counts = None
         self.local_fn = local_fn or self._bank_rows
         self.combine_fn = combine_fn or _cuda_combine
         self.shared_fn = shared_fn or self._shared_rows
         self.pack_fn = pack_fn or _cuda_pack
+
+    def _host_counts(self, device) -> torch.Tensor:
+        """[2 * world] int64 host buffer for the send / receive counts (pinned
+        when the layer runs on a GPU)."""
+        if self._counts is None:
+            self._counts = torch.empty(2 * self.world, dtype=torch.int64,
+                                       pin_memory=device.type == "cuda")
+        return self._counts
 
     # default compute: the fused layer kernel, one expert of weight 1 per row
     def _bank_rows(self, rows: torch.Tensor, local_ids: torch.Tensor) -> torch.Tensor:
@@ -128,7 +138,18 @@ class ExpertParallelLayer:
         send_counts = send_counts.to(torch.int64)
         recv_counts = torch.empty_like(send_counts)
         dist.all_to_all_single(recv_counts, send_counts, group=self.group)
-        sc, rc = send_counts.tolist(), recv_counts.tolist()   # the one host sync of a step
+        # the one host sync of a step: the counts travel to pinned memory, and
+        # the shared experts (independent of the exchange) run while the host waits
+        counts = self._host_counts(hidden.device)
+        counts[:self.world].copy_(send_counts, non_blocking=True)
+        counts[self.world:].copy_(recv_counts, non_blocking=True)
+        ready = torch.cuda.Event() if hidden.is_cuda else None
+        if ready is not None:
+            ready.record()
+        shared = self.shared_fn(hidden)
+        if ready is not None:
+            ready.synchronize()
+        sc, rc = counts[:self.world].tolist(), counts[self.world:].tolist()
         n_send = sum(sc)
         recv_rows = hidden.new_empty(sum(rc), h)
         recv_ids = torch.empty(sum(rc), dtype=torch.int32, device=hidden.device)
@@ -138,8 +159,6 @@ class ExpertParallelLayer:
         out_rows = self.local_fn(recv_rows, recv_ids).contiguous()
         back = hidden.new_empty(max(n_send, 1), h)
         dist.all_to_all_single(back[:n_send], out_rows, sc, rc, group=self.group)
-
-        shared = self.shared_fn(hidden)
         return self.combine_fn(back, slot_row, topk_weights, shared)
 
     __call__ = forward
