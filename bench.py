@@ -400,12 +400,14 @@ EP_CASES = ("mixtral", "dsv2_lite")   # the expert-sharded configs (C4, C5), dec
 
 
 def ep_measure(dev, world, rank, name, steps=50, warmup=5):
-    """Expert-parallel layer over NCCL: rank r owns E/world routed experts and
-    its own T=256 tokens; one step = all-to-all out, local fused layer,
-    all-to-all back, weighted combine (+ shared experts).  On one GPU the step
-    is the whole layer (no exchange), the baseline of the scaling.  Device time
-    of `steps` steps, max over ranks.  Reports per-step latency and the weight
-    bytes of the locally owned experts that received tokens, per rank."""
+    """Expert-parallel layer: rank r owns E/world routed experts and its own
+    T=256 tokens; one step = rows out to the experts' ranks, local fused layer,
+    rows back, weighted combine (+ shared experts).  The headline exchange is
+    the peer-memory one (NVLink stores, no host sync); the NCCL all-to-all
+    exchange is timed beside it.  On one GPU the step is the whole layer (no
+    exchange), the baseline of the scaling.  Device time of `steps` steps, max
+    over ranks.  Reports per-step latency and the weight bytes of the locally
+    owned experts that received tokens, per rank."""
     import torch
     import torch.distributed as dist
     from exq_b200.ep import ExpertParallelLayer, build_rank_banks
@@ -425,27 +427,38 @@ def ep_measure(dev, world, rank, name, steps=50, warmup=5):
     else:
         local, shared = build_rank_banks(w13, w2, world, rank, act_dtype=c.act_dtype,
                                          shared_w13=sw13, shared_w2=sw2)
-        layer = ExpertParallelLayer(local, c.n_experts, shared_bank=shared)
+        layer = ExpertParallelLayer(local, c.n_experts, shared_bank=shared, max_tokens=t,
+                                    top_k=c.top_k)
     del w13, w2, sw13, sw2
     torch.cuda.empty_cache()
     ids, w = zipf_router(t, c.n_experts, c.top_k, seed=11 + rank)
     x = hidden_states(t, c.hidden, seed=11 + rank).to(dev, c.act_dtype)
     ids, w = ids.to(dev), w.to(dev)
-    for _ in range(warmup):
-        layer(x, ids, w)
-    torch.cuda.synchronize(dev)
+
+    def timed(fn):
+        for _ in range(warmup):
+            fn(x, ids, w)
+        torch.cuda.synchronize(dev)
+        if world > 1:
+            dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            fn(x, ids, w)
+        e1.record()
+        torch.cuda.synchronize(dev)
+        sec = torch.tensor([e0.elapsed_time(e1) / 1e3 / steps], device=dev)
+        if world > 1:
+            dist.all_reduce(sec, op=dist.ReduceOp.MAX)
+        return sec
+
+    sec = timed(layer)
+    nccl_us = None
     if world > 1:
-        dist.barrier()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for _ in range(steps):
-        layer(x, ids, w)
-    e1.record()
-    torch.cuda.synchronize(dev)
-    sec = torch.tensor([e0.elapsed_time(e1) / 1e3 / steps], device=dev)
+        nccl = ExpertParallelLayer(local, c.n_experts, shared_bank=shared)
+        nccl_us = round(float(timed(nccl).item()) * 1e6, 1)
     all_ids = [ids]
     if world > 1:
-        dist.all_reduce(sec, op=dist.ReduceOp.MAX)
         # weight bytes per rank: owned experts that received a slot from any rank
         all_ids = [torch.empty_like(ids) for _ in range(world)]
         dist.all_gather(all_ids, ids)
@@ -461,8 +474,13 @@ def ep_measure(dev, world, rank, name, steps=50, warmup=5):
            "experts_per_rank": per, "us_per_step": round(us, 1),
            "weight_GBps_per_rank": round(float(wbytes.item()) / (us * 1e-6) / 1e9, 1),
            "tokens_per_s_total": round(world * t / (us * 1e-6), 1)}
+    if world > 1:
+        out["exchange"] = "peer memory (NVLink stores)"
+        out["nccl_us_per_step"] = nccl_us
     if world == 1 and name == "mixtral":
         out["prefill"] = prefill_measure(layer, c, dev)
+    if world > 1:
+        layer.close()
     del layer, local, shared
     torch.cuda.empty_cache()
     return out

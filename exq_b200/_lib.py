@@ -50,6 +50,17 @@ SIGNATURES = {
     "exq_ep_pack": (C.c_int, [vp, C.c_int, i64, i32, i32, i32, vp, C.c_int, i64, vp, vp, vp, vp,
                               vp]),
     "exq_ep_combine": (C.c_int, [vp, C.c_int, vp, vp, C.c_int, i64, i32, i64, vp, vp, vp]),
+    "exq_ep_buffer_bytes": (sz, [i32, i64, i64]),
+    "exq_ep_buffer_init": (C.c_int, [vp, i32, i64, i64, vp]),
+    "exq_ep_ipc_alloc": (C.c_int, [sz, C.POINTER(C.c_void_p), vp]),
+    "exq_ep_ipc_free": (C.c_int, [vp]),
+    "exq_ep_ipc_open": (C.c_int, [vp, C.POINTER(C.c_void_p)]),
+    "exq_ep_ipc_close": (C.c_int, [vp]),
+    "exq_ep_dispatch": (C.c_int, [vp, C.c_int, i64, i32, i32, i32, i32, vp, C.c_int, i64, i64, vp,
+                                  vp, vp]),
+    "exq_ep_expert_forward": (C.c_int, [vp, C.c_int, i32, i32, i64, vp, vp, vp, sz, vp]),
+    "exq_ep_combine_peer": (C.c_int, [vp, i32, i64, i64, C.c_int, vp, vp, C.c_int, i64, i32, vp,
+                                      vp, vp]),
     "exq_combine_noalloc": (C.c_int, [vp, C.c_int, i64, i64, vp, vp, C.c_int, i64, i32, vp,
                                       C.c_int, vp]),
     "exq_silu_and_mul": (C.c_int, [vp, vp, C.c_int, i64, i64, vp]),

@@ -147,4 +147,10 @@ int launch_combine_partials(const float* partial, int64_t H, const int32_t* pos_
 
 uint32_t* device_status_ptr();
 
+// Views into a layer workspace (exq_moe_layer_forward_range) for a caller that
+// replaces the combine stage: the fp32 down partials [n_slots, hidden] by
+// sorted position and the slot -> sorted position map (-1: no expert).
+void layer_partials(void* workspace, int64_t n_slots, int n_buckets, int64_t hidden,
+                    int64_t inter, const float** partial, const int32_t** pos_of_slot);
+
 }  // namespace exq

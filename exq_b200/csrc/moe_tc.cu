@@ -797,15 +797,17 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
 }
 
 // Activation prep: A[pos, :] = fp16(hidden[token(pos), :]) with every octet of
-// k permuted to [0,4,1,5,2,6,3,7].
+// k permuted to [0,4,1,5,2,6,3,7].  Positions at or past *routed_total + mt
+// are read by no GEMM tile and are left alone.
 template <typename T>
 __global__ void prep_act_kernel(const T* __restrict__ hidden, int64_t hid, int64_t n_tokens,
                                 const int32_t* sorted_slot, int spt, int64_t n_pos,
-                                __half* __restrict__ out) {
+                                const int32_t* routed_total, int mt, __half* __restrict__ out) {
   pdl_wait();
   pdl_trigger();
   const int64_t octs = hid / 8;
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n_pos * octs;
+  const int64_t lim = min(n_pos, static_cast<int64_t>(*routed_total) + mt);
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < lim * octs;
        i += (int64_t)gridDim.x * blockDim.x) {
     const int64_t pos = i / octs, o = i - pos * octs;
     const int32_t slot = sorted_slot[pos];
@@ -1010,8 +1012,8 @@ int launch_tc(const TcParams& p, int max_items, cudaStream_t stream) {
 }
 
 int launch_prep(const void* hidden, int act_dtype, int64_t hid, int64_t n_tokens,
-                const int32_t* sorted_slot, int spt, int64_t n_pos, __half* out,
-                cudaStream_t stream) {
+                const int32_t* sorted_slot, int spt, int64_t n_pos, const int32_t* routed_total,
+                int mt, __half* out, cudaStream_t stream) {
   if (n_pos == 0) return EXQ_OK;
   const int64_t work = n_pos * (hid / 8);
   int64_t grid = (work + 255) / 256;
@@ -1019,11 +1021,12 @@ int launch_prep(const void* hidden, int act_dtype, int64_t hid, int64_t n_tokens
   cudaError_t e;
   if (act_dtype == EXQ_F16)
     e = launch_pdl(prep_act_kernel<__half>, dim3((int)grid), dim3(256), 0, stream,
-                   static_cast<const __half*>(hidden), hid, n_tokens, sorted_slot, spt, n_pos, out);
+                   static_cast<const __half*>(hidden), hid, n_tokens, sorted_slot, spt, n_pos,
+                   routed_total, mt, out);
   else
     e = launch_pdl(prep_act_kernel<__nv_bfloat16>, dim3((int)grid), dim3(256), 0, stream,
                    static_cast<const __nv_bfloat16*>(hidden), hid, n_tokens, sorted_slot, spt, n_pos,
-                   out);
+                   routed_total, mt, out);
   if (e != cudaSuccess) {
     set_error("prep_act_kernel: %s", cudaGetErrorString(e));
     return EXQ_ERR_CUDA;
@@ -1081,6 +1084,13 @@ TcWs carve_tc(void* base, int64_t n_slots, int n_buckets, int64_t hidden, int64_
 bool is_act(int d) { return d == EXQ_F16 || d == EXQ_BF16; }
 
 }  // namespace
+
+void exq::layer_partials(void* workspace, int64_t n_slots, int n_buckets, int64_t hidden,
+                         int64_t inter, const float** partial, const int32_t** pos_of_slot) {
+  const TcWs ws = carve_tc(workspace, n_slots, n_buckets, hidden, inter);
+  *partial = ws.partial;
+  *pos_of_slot = ws.pos_of_slot;
+}
 
 extern "C" size_t exq_moe_layer_workspace_bytes(int64_t n_tokens, int32_t top_k, int32_t n_shared,
                                                 int32_t n_experts_total, int64_t hidden,
@@ -1201,7 +1211,8 @@ extern "C" int exq_moe_layer_forward_range(const exq_moe_weights* w, const void*
     if (st != EXQ_OK) return st;
   }
   if (!fused && first_stage <= 1 && end_stage > 1) {
-    st = tc::launch_prep(hidden_states, act_dtype, H, n_tokens, ws.sorted_slot, spt, n_slots, ws.act,
+    st = tc::launch_prep(hidden_states, act_dtype, H, n_tokens, ws.sorted_slot, spt, n_slots,
+                         ws.ends + n_total, kLayerMT, ws.act,
                          s);
     if (st != EXQ_OK) return st;
   }

@@ -40,7 +40,8 @@ __device__ __forceinline__ int route_bucket(const RouteParams& p, int mode, int6
     *value = i;
     if (j >= p.top_k) return p.n_routed + (j - p.top_k);  // shared expert
     const int64_t e = load_index(p.ids, p.ids_dtype, t * p.top_k + j);
-    if (e < 0 || e >= p.n_routed) {
+    if (e < 0) return -1;  // a padding slot: no expert
+    if (e >= p.n_routed) {
       atomicOr(p.status, EXQ_DEV_BAD_EXPERT_ID);
       return -1;
     }

@@ -16,8 +16,8 @@
 //     to [0,4,1,5,2,6,3,7] (the k order of the dequantised weights),
 //   - writes the slot -> position map and the router weight at the position.
 // CTA 0 also writes the GEMM tile list and the expert ends; dropped slots
-// (expert id out of range) map to -1, and the positions past the routed total
-// get zero rows.
+// (expert id out of range or negative) map to -1, and the positions past the
+// routed total that the last GEMM tile reads get zero rows.
 #include <type_traits>
 
 #include "internal.cuh"
@@ -122,8 +122,9 @@ __global__ void __launch_bounds__(kRgThreads) route_gather_kernel(const RouteGat
       if (j >= p.top_k) {
         e = p.n_routed + (j - p.top_k);  // always-on shared expert
       } else {
+        // negative: a padding slot (no expert); past the experts: dropped and flagged
         e = (v[u] >= 0 && v[u] < p.n_routed) ? static_cast<int>(v[u]) : -1;
-        if (e < 0 && blockIdx.x == 0) atomicOr(p.status, EXQ_DEV_BAD_EXPERT_ID);
+        if (v[u] >= p.n_routed && blockIdx.x == 0) atomicOr(p.status, EXQ_DEV_BAD_EXPERT_ID);
       }
       bkt[i] = e;
       wslot[i] = j < p.top_k ? wv[u] : 1.0f;  // shared experts weigh 1
@@ -235,9 +236,11 @@ __global__ void __launch_bounds__(kRgThreads) route_gather_kernel(const RouteGat
       }
     }
   }
-  // positions past the routed total (as many as dropped slots): zero rows
-  const int zc = (n - carry + static_cast<int>(gridDim.x) - 1) / static_cast<int>(gridDim.x);
-  const int z0 = carry + static_cast<int>(blockIdx.x) * zc, z1 = min(n, z0 + zc);
+  // positions past the routed total that the last GEMM tile reads (a tile
+  // starts below the total and spans mt rows): zero rows
+  const int zend = min(n, carry + p.mt);
+  const int zc = (zend - carry + static_cast<int>(gridDim.x) - 1) / static_cast<int>(gridDim.x);
+  const int z0 = carry + static_cast<int>(blockIdx.x) * zc, z1 = min(zend, z0 + zc);
   for (int idx = threadIdx.x; idx < max(0, z1 - z0) * octs; idx += kRgThreads) {
     const int pos = z0 + idx / octs, o = idx % octs;
     reinterpret_cast<uint4*>(p.act)[(static_cast<int64_t>(o >> 3) * n + pos) * 8 + (o & 7)] =

@@ -1,33 +1,40 @@
-"""Expert parallelism for the MoE expert layer (one process per GPU, NCCL).
+"""Expert parallelism for the MoE expert layer (one process per GPU).
 
 The reference has no expert-parallel path of its own: its layer runs whole on
 one GPU (exq/runtime/sglang_backend.py:65-158).  This module shards the
-routed experts of one layer across the ranks of a process group and moves
-tokens to their experts with one all-to-all each way:
+routed experts of one layer across the ranks of a process group; rank r owns
+routed experts [r*E/P, (r+1)*E/P).  Two exchanges move tokens to their experts.
 
-1. one kernel (``exq_ep_pack``) groups the (token, expert) slots of this
-   rank's tokens by destination rank, copies their hidden rows into a send
-   buffer and counts them; an all-to-all of the counts tells every rank what
-   it receives (the step's one host synchronisation, for NCCL's split sizes;
-   the shared experts, which every rank holds and runs on its own tokens,
-   are computed while the host waits for the counts);
-2. the rows and their expert index local to the destination go out in
-   all-to-alls;
-3. each rank runs its experts on the rows it received with the fused layer
-   kernel (every received row is a token with one expert of weight 1);
-4. the expert outputs return by the reverse all-to-all, in send order;
-5. the owner of each token applies the router weights and sums its slots,
-   plus the shared experts' output, in one kernel (``exq_ep_combine``).
+Peer memory (``max_tokens`` given, GPUs of one node): every rank allocates one
+buffer and maps the other ranks' buffers through CUDA IPC (``PeerExchange``).
+A step is four kernels' worth of work on the caller's stream, with no NCCL and
+no host synchronisation (so it can be captured in a CUDA graph):
+1. ``exq_ep_dispatch`` groups this rank's (token, expert) slots by destination
+   and stores each hidden row and local expert id straight into the
+   destination's receive block over NVLink, then raises an arrival flag there;
+2. the shared experts (replicated) run on the rank's own tokens meanwhile;
+3. ``exq_ep_expert_forward`` waits for every arrival flag, runs the local
+   experts on the fixed-size receive area (unused rows have id -1 and cost no
+   GEMM work) and stores each output row back into its source's return block,
+   raising a return flag there;
+4. ``exq_ep_combine_peer`` waits for every return flag, applies the router
+   weights and sums each token's slots plus the shared output.
+Each destination reserves ``max_tokens * top_k`` rows per source, so no
+count exchange is needed; a call with more tokens is refused on the host.
 
-Rank r owns routed experts [r*E/P, (r+1)*E/P).  Counts travel to the host
-once per call to size the exchange, so a call is not CUDA-graph capturable.
-
-The packing, the local expert compute and the combine are functions of the
-layer (``pack_fn``, ``local_fn``, ``combine_fn``).  By default they are this
-package's CUDA kernels; the multi-process CPU tests substitute the CPU oracle
-to check the exchange logic on ``gloo`` ranks.
+NCCL (default): one kernel (``exq_ep_pack``) groups the slots by destination
+rank into a send buffer and counts them; an all-to-all of the counts sizes the
+exchange (one host synchronisation, during which the shared experts run);
+all-to-alls move the rows and local ids, each rank runs its experts on what it
+received, the outputs return by the reverse all-to-all, and ``exq_ep_combine``
+applies the router weights.  The packing, the local expert compute and the
+combine are functions of the layer (``pack_fn``, ``local_fn``, ``combine_fn``);
+the multi-process CPU tests substitute the CPU oracle to check this exchange on
+``gloo`` ranks.
 """
 from __future__ import annotations
+
+import ctypes as C
 
 import torch
 import torch.distributed as dist
@@ -73,16 +80,83 @@ def _cuda_combine(back: torch.Tensor, slot_row: torch.Tensor, weights: torch.Ten
     return y
 
 
+class PeerExchange:
+    """This rank's expert-parallel buffer, mapped into every rank of the group.
+
+    Collective: every rank of ``group`` constructs it with the same sizes.  The
+    buffer holds ``world * capacity`` receive and return rows (``capacity``
+    rows reserved per source rank) plus the arrival flags; ``peers`` is the
+    device array of all ranks' buffer addresses as mapped in this process.
+    ``close`` (also collective) unmaps and frees it."""
+
+    def __init__(self, group, capacity: int, hidden: int, device: torch.device):
+        lib = L.lib()
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.capacity, self.hidden, self.device = capacity, hidden, device
+        nbytes = int(lib.exq_ep_buffer_bytes(self.world, capacity, hidden))
+        if nbytes == 0:
+            raise ValueError(f"bad expert-parallel buffer sizes: {self.world} ranks, capacity "
+                             f"{capacity}, hidden {hidden}")
+        self.nbytes = nbytes
+        with torch.cuda.device(device):
+            own = C.c_void_p()
+            handle = (C.c_uint8 * 64)()
+            L.check(lib.exq_ep_ipc_alloc(nbytes, C.byref(own), handle), "ep_ipc_alloc")
+            self.ptr = own.value
+            self._mapped = []
+            L.check(lib.exq_ep_buffer_init(self.ptr, self.world, capacity, hidden,
+                                           L.stream_of(device)), "ep_buffer_init")
+            # every rank's buffer is initialised before its handle is published,
+            # so no rank writes into a buffer that is still being cleared
+            torch.cuda.synchronize(device)
+            mine = torch.tensor(list(bytes(handle)), dtype=torch.uint8, device=device)
+            every = torch.empty(self.world, 64, dtype=torch.uint8, device=device)
+            dist.all_gather_into_tensor(every, mine, group=group)
+            every = every.cpu()
+            addrs = []
+            for r in range(self.world):
+                if r == self.rank:
+                    addrs.append(self.ptr)
+                    continue
+                p = C.c_void_p()
+                h = (C.c_uint8 * 64)(*every[r].tolist())
+                L.check(lib.exq_ep_ipc_open(h, C.byref(p)), "ep_ipc_open")
+                self._mapped.append(p.value)
+                addrs.append(p.value)
+            self.peers = torch.tensor(addrs, dtype=torch.int64, device=device)
+
+    def close(self) -> None:
+        if self.ptr is None:
+            return
+        lib = L.lib()
+        torch.cuda.synchronize(self.device)
+        # no rank may still be writing into a buffer that is about to go
+        flag = torch.zeros(1, device=self.device)
+        dist.all_reduce(flag, group=self.group)
+        torch.cuda.synchronize(self.device)
+        with torch.cuda.device(self.device):
+            for p in self._mapped:
+                L.check(lib.exq_ep_ipc_close(p), "ep_ipc_close")
+            L.check(lib.exq_ep_ipc_free(self.ptr), "ep_ipc_free")
+        self._mapped, self.ptr = [], None
+
+
 class ExpertParallelLayer:
     """One MoE layer whose routed experts are sharded over a process group.
 
     ``local_bank`` holds this rank's routed experts (``n_routed / world`` of
     them, as an :class:`exq_b200.ExpertBank`); ``shared_bank`` optionally holds
-    the always-on shared experts (replicated on every rank).
+    the always-on shared experts (replicated on every rank).  With
+    ``max_tokens`` (and ``top_k``) the layer exchanges over peer memory and a
+    call takes at most ``max_tokens`` tokens of at most ``top_k`` experts;
+    constructing it is then collective.  Without, it exchanges over NCCL.
     """
 
     def __init__(self, local_bank, n_routed: int, group=None, shared_bank=None,
-                 local_fn=None, combine_fn=None, shared_fn=None, pack_fn=None):
+                 local_fn=None, combine_fn=None, shared_fn=None, pack_fn=None,
+                 max_tokens: int | None = None, top_k: int | None = None):
         self.group = group
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
@@ -99,6 +173,19 @@ class ExpertParallelLayer:
         self.combine_fn = combine_fn or _cuda_combine
         self.shared_fn = shared_fn or self._shared_rows
         self.pack_fn = pack_fn or _cuda_pack
+        self.peer = None
+        if max_tokens is not None:
+            if top_k is None or top_k <= 0 or max_tokens <= 0 or local_bank is None:
+                raise ValueError("the peer exchange needs max_tokens > 0, top_k > 0 and a bank")
+            self.peer = PeerExchange(group, max_tokens * top_k, local_bank.hidden,
+                                     local_bank.device)
+            self.local_bank.reserve(self.world * self.peer.capacity, 1)
+
+    def close(self) -> None:
+        """Release the peer buffers (collective)."""
+        if self.peer is not None:
+            self.peer.close()
+            self.peer = None
 
     def _host_counts(self, device) -> torch.Tensor:
         """[2 * world] int64 host buffer for the send / receive counts (pinned
@@ -131,6 +218,8 @@ class ExpertParallelLayer:
         as in the single-GPU layer."""
         if topk_ids.shape != topk_weights.shape or topk_ids.shape[0] != hidden.shape[0]:
             raise ValueError("topk_ids / topk_weights must be [T, k] for hidden [T, H]")
+        if self.peer is not None:
+            return self._forward_peer(hidden, topk_ids, topk_weights)
         t, k = topk_ids.shape
         h = hidden.shape[1]
         send_rows, send_ids, slot_row, send_counts = self.pack_fn(hidden.contiguous(), topk_ids,
@@ -160,6 +249,32 @@ class ExpertParallelLayer:
         back = hidden.new_empty(max(n_send, 1), h)
         dist.all_to_all_single(back[:n_send], out_rows, sc, rc, group=self.group)
         return self.combine_fn(back, slot_row, topk_weights, shared)
+
+    def _forward_peer(self, hidden, topk_ids, topk_weights):
+        px, bank, lib = self.peer, self.local_bank, L.lib()
+        t, k = topk_ids.shape
+        if t * k > px.capacity:
+            raise ValueError(f"{t} tokens x top-{k} exceed the exchange's {px.capacity} rows "
+                             "per rank (max_tokens * top_k)")
+        dev = L.require_cuda(hidden, topk_ids, topk_weights)
+        x, ids, w = hidden.contiguous(), topk_ids.contiguous(), topk_weights.contiguous()
+        h = x.shape[1]
+        s = L.stream_of(dev)
+        slot_row = torch.empty(t * k, dtype=torch.int32, device=dev)
+        L.check(lib.exq_ep_dispatch(L.ptr(ids), L.tag(ids), t, k, self.per_rank, self.world,
+                                    self.rank, L.ptr(x), L.tag(x), h, px.capacity,
+                                    L.ptr(px.peers), L.ptr(slot_row), s), "ep_dispatch")
+        shared = self.shared_fn(x)
+        ws = bank._ws
+        L.check(lib.exq_ep_expert_forward(C.byref(bank.cstruct), L.tag(x), self.world, self.rank,
+                                          px.capacity, px.ptr, L.ptr(px.peers), L.ptr(ws),
+                                          ws.numel(), s), "ep_expert_forward")
+        y = torch.empty(t, h, dtype=x.dtype, device=dev)
+        L.check(lib.exq_ep_combine_peer(px.ptr, self.world, px.capacity, h, L.tag(x),
+                                        L.ptr(slot_row), L.ptr(w), L.tag(w), t, k,
+                                        None if shared is None else L.ptr(shared), L.ptr(y), s),
+                "ep_combine_peer")
+        return y
 
     __call__ = forward
 

@@ -131,14 +131,15 @@ EXQ_API int exq_combine(const void* down_out, int dtype, int64_t n_active, int64
 /* ---------------------------------------------------------------- expert parallelism */
 
 /* No counterpart in the reference (its layer runs whole on one GPU,
- * exq/runtime/sglang_backend.py:65-158).  The send side of the expert-parallel
- * exchange of exq_b200/ep.py: the T*k slots of topk_ids [T, k], grouped by
- * destination rank d = expert / experts_per_rank in ascending slot order,
- * become send_rows [T*k, hidden_size] (the hidden row of each slot, same
- * dtype), send_ids[r] (the expert index local to the destination),
- * slot_row[slot] (send row of the slot, -1 if its expert id is out of range:
- * dropped and flagged in the device status) and counts[n_ranks] (rows per
- * destination).  At most 4096 slots and 64 ranks; hidden_size % 8 == 0. */
+ * exq/runtime/sglang_backend.py:65-158).  The send side of the NCCL
+ * expert-parallel exchange of exq_b200/ep.py: the T*k slots of topk_ids
+ * [T, k], grouped by destination rank d = expert / experts_per_rank in
+ * ascending slot order, become send_rows [T*k, hidden_size] (the hidden row
+ * of each slot, same dtype), send_ids[r] (the expert index local to the
+ * destination), slot_row[slot] (send row of the slot, -1 if its expert id is
+ * out of range: dropped and flagged in the device status) and
+ * counts[n_ranks] (rows per destination).  At most 4096 slots and 64 ranks;
+ * hidden_size % 8 == 0. */
 EXQ_API int exq_ep_pack(const void* topk_ids, int ids_dtype, int64_t n_tokens, int32_t top_k,
                         int32_t experts_per_rank, int32_t n_ranks, const void* hidden, int dtype,
                         int64_t hidden_size, void* send_rows, int32_t* send_ids,
@@ -249,12 +250,15 @@ typedef struct exq_moe_weights {
 /* The whole MoE layer of exq/runtime/sglang_backend.py:65-158 (and
  * moe_int4_full_forward, moe_int4_kernel.py:330-426): route -> activation
  * prep (gather + fp16 + octet permutation) -> gate_up tcgen05 grouped GEMM with
- * fused SiLU*mul -> down tcgen05 grouped GEMM writing router-weighted fp32
- * partials -> deterministic top-k combine.  The experts may mix the three
+ * fused SiLU*mul -> down tcgen05 grouped GEMM writing fp32 partials -> the
+ * deterministic router-weighted top-k combine.  The experts may mix the three
  * tiers.  hidden_states/out: [n_tokens, hidden] (fp16 or bf16; the matrix
  * products run on fp16 operands with fp32 accumulation, as the reference's
- * kernel does); topk_ids [n_tokens, top_k] int32/int64; topk_weights
- * [n_tokens, top_k] f32/f16/bf16.  Five launches, no host synchronisation. */
+ * kernel does); topk_ids [n_tokens, top_k] int32/int64, where a negative id
+ * marks an unused slot (no expert) and an id >= n_routed is dropped and
+ * flagged (EXQ_DEV_BAD_EXPERT_ID); topk_weights [n_tokens, top_k]
+ * f32/f16/bf16.  Four launches up to 4096 slots (route and prep fused), five
+ * above; no host synchronisation. */
 EXQ_API size_t exq_moe_layer_workspace_bytes(int64_t n_tokens, int32_t top_k, int32_t n_shared,
                                              int32_t n_experts_total, int64_t hidden,
                                              int64_t inter);
@@ -276,6 +280,74 @@ EXQ_API int exq_moe_layer_forward_range(const exq_moe_weights* weights,
                                         const void* topk_weights, int w_dtype, int32_t top_k,
                                         void* out, void* workspace, size_t workspace_bytes,
                                         void* stream, int32_t first_stage, int32_t end_stage);
+
+/* ------------------------------------------------ expert parallelism over peer memory
+ *
+ * No counterpart in the reference.  The exchange without NCCL or a host sync:
+ * every rank holds one "EP buffer" (exq_ep_buffer_bytes), shared with the
+ * other ranks of one node through CUDA IPC, and `peers` is a DEVICE array of
+ * the n_ranks buffer addresses as mapped in this process (peers[rank] = own).
+ * One buffer: a header of arrival flags, then, for n_ranks * capacity rows,
+ * the received local expert ids (int32, -1 = unused), a column of 1.0f, the
+ * received hidden rows and the returned expert output rows.  Block s of
+ * `capacity` rows belongs to source rank s.  A step is, in stream order on
+ * every rank: exq_ep_dispatch -> (shared experts) -> exq_ep_expert_forward
+ * -> exq_ep_combine_peer.  Every rank must make the same calls in the same
+ * order.  Waits on other ranks are bounded (about 5 s): on expiry the kernel
+ * sets EXQ_DEV_TIMEOUT in the device status and returns. */
+#define EXQ_IPC_HANDLE_BYTES 64
+
+/* Bytes of one rank's EP buffer; 0 for invalid sizes. */
+EXQ_API size_t exq_ep_buffer_bytes(int32_t n_ranks, int64_t capacity, int64_t hidden_size);
+
+/* Clears the flags and ids and writes the 1.0f column of a fresh buffer.
+ * Every rank must finish it (stream synchronised, then a group barrier)
+ * before any rank's first exq_ep_dispatch. */
+EXQ_API int exq_ep_buffer_init(void* buffer, int32_t n_ranks, int64_t capacity,
+                               int64_t hidden_size, void* stream);
+
+/* cudaMalloc of `bytes` plus its IPC handle (EXQ_IPC_HANDLE_BYTES bytes
+ * written to handle_out); exq_ep_ipc_free releases it. */
+EXQ_API int exq_ep_ipc_alloc(size_t bytes, void** ptr_out, void* handle_out);
+EXQ_API int exq_ep_ipc_free(void* ptr);
+/* Maps another process's buffer on the current device (peer access enabled
+ * lazily); exq_ep_ipc_close unmaps it. */
+EXQ_API int exq_ep_ipc_open(const void* handle, void** ptr_out);
+EXQ_API int exq_ep_ipc_close(void* ptr);
+
+/* One launch: groups this rank's T*k slots by destination rank (as
+ * exq_ep_pack) and writes each slot's hidden row and local expert id straight
+ * into block `rank` of the destination's buffer (NVLink stores), fills the
+ * rest of every block's ids with -1, then raises this rank's arrival flag in
+ * every destination.  slot_row[slot] = d * capacity + q, the row of this
+ * rank's return area that rank d fills for the slot (-1: dropped id).
+ * n_tokens <= capacity / top_k is the caller's contract; a destination past
+ * its capacity is flagged EXQ_DEV_BAD_SLOT and its extra rows dropped.
+ * At most 4096 slots and 64 ranks; hidden_size % 8 == 0. */
+EXQ_API int exq_ep_dispatch(const void* topk_ids, int ids_dtype, int64_t n_tokens, int32_t top_k,
+                            int32_t experts_per_rank, int32_t n_ranks, int32_t rank,
+                            const void* hidden, int dtype, int64_t hidden_size, int64_t capacity,
+                            void* const* peers, int32_t* slot_row, void* stream);
+
+/* Waits for every rank's arrival flag, runs this rank's routed experts
+ * (`weights`, no shared experts) on all n_ranks * capacity received rows
+ * (the layer of exq_moe_layer_forward with top_k 1 and weight 1; unused rows
+ * carry id -1 and cost nothing in the GEMMs), then writes each output row,
+ * rounded to `dtype`, into its source rank's return area (NVLink stores) and
+ * raises this rank's return flag there.  workspace: exq_moe_layer_workspace_bytes(
+ * n_ranks * capacity, 1, 0, n_routed, hidden, inter). */
+EXQ_API int exq_ep_expert_forward(const exq_moe_weights* weights, int dtype, int32_t n_ranks,
+                                  int32_t rank, int64_t capacity, void* buffer,
+                                  void* const* peers, void* workspace, size_t workspace_bytes,
+                                  void* stream);
+
+/* Waits for every rank's return flag, then
+ * out[t] = base[t] + sum_j weights[t, j] * returned[slot_row[t*k + j]]
+ * as exq_ep_combine (base may be NULL). */
+EXQ_API int exq_ep_combine_peer(const void* buffer, int32_t n_ranks, int64_t capacity,
+                                int64_t hidden_size, int dtype, const int32_t* slot_row,
+                                const void* weights, int w_dtype, int64_t n_tokens,
+                                int32_t top_k, const void* base, void* out, void* stream);
 
 #ifdef __cplusplus
 }

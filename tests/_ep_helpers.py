@@ -90,27 +90,64 @@ def cpu_worker(rank, world, port, case, t_per_rank):
         dist.destroy_process_group()
 
 
-def gpu_worker(rank, world, port):
-    """EP over NCCL on `world` GPUs vs the whole layer on one GPU (Mixtral-like, bf16)."""
+def _gpu_step_inputs(step, rank, world, t, case, e, h, k, dev):
+    from exq_b200.synth import hidden_states, zipf_router
+    seed = 10 * step + rank
+    if t == 0:
+        ids = torch.zeros(0, k, dtype=torch.int64)
+        w = torch.zeros(0, k)
+    elif case == "one_rank":   # every slot to the experts of rank 0
+        g = torch.Generator().manual_seed(seed)
+        ids = torch.stack([torch.randperm(e // world, generator=g)[:k] for _ in range(t)])
+        w = torch.rand(t, k, generator=g)
+    else:
+        ids, w = zipf_router(t, e, k, seed=seed)
+    x = hidden_states(max(t, 1), h, seed=seed)[:t].to(dev, torch.bfloat16)
+    return x, ids.to(dev), w.to(dev)
+
+
+def gpu_worker(rank, world, port, mode="nccl"):
+    """EP on `world` GPUs vs the whole layer on one GPU (Mixtral-like, bf16),
+    over four steps: spread routing, a rank with no tokens, every slot to rank
+    0's experts, spread again.  mode "peer": the peer-memory exchange, also
+    checked bit for bit against the NCCL exchange when world > 1."""
     from exq_b200 import ExpertBank
+    from exq_b200 import _lib as L
     from exq_b200.ep import ExpertParallelLayer, build_rank_banks
-    from exq_b200.synth import expert_weights, hidden_states, zipf_router
+    from exq_b200.synth import expert_weights
     torch.cuda.set_device(rank)
     dev = torch.device("cuda", rank)
     _init(rank, world, port, "nccl")
     try:
-        e, h, inter, k, t = 8, 512, 256, 2, 48
+        e, h, inter, k = 8, 512, 256, 2
         w13, w2 = expert_weights(e, inter, h, seed=0, device=dev)
         local, _ = build_rank_banks(w13, w2, world, rank, act_dtype=torch.bfloat16)
-        layer = ExpertParallelLayer(local, e)
-        ids, w = zipf_router(t, e, k, seed=rank)
-        x = hidden_states(t, h, seed=rank).to(dev, torch.bfloat16)
-        y = layer(x, ids.to(dev), w.to(dev))
         full = ExpertBank.from_dense(w13, w2, None, act_dtype=torch.bfloat16)
-        ref = full(x, ids.to(dev), w.to(dev))
+        if mode == "peer":
+            layer = ExpertParallelLayer(local, e, max_tokens=64, top_k=k)
+            nccl = ExpertParallelLayer(local, e) if world > 1 else None
+        else:
+            layer, nccl = ExpertParallelLayer(local, e), None
+        L.read_device_status(dev, clear=True)
+        steps = [(48, "spread"), (0 if rank == 0 else 17, "spread"), (64, "one_rank"),
+                 (48, "spread")]
+        for step, (t, case) in enumerate(steps):
+            x, ids, w = _gpu_step_inputs(step, rank, world, t, case, e, h, k, dev)
+            y = layer(x, ids, w)
+            assert y.shape == (t, h) and y.dtype == torch.bfloat16
+            if nccl is not None:
+                y2 = nccl(x, ids, w)
+                assert torch.equal(y, y2), f"rank {rank} step {step}: peer != NCCL exchange"
+            if t:
+                ref = full(x, ids, w)
+                torch.cuda.synchronize(dev)
+                err = OM.rel_l2(y.float().cpu(), ref.float().cpu())
+                assert err < 5e-3, f"rank {rank} step {step}: rel-L2 {err:.2e} vs one GPU"
         torch.cuda.synchronize(dev)
-        err = OM.rel_l2(y.float().cpu(), ref.float().cpu())
-        assert err < 5e-3, f"rank {rank}: rel-L2 {err:.2e} vs the single-GPU layer"
+        status = L.read_device_status(dev, clear=True)
+        assert status == 0, f"rank {rank}: device status {status:#x}"
+        if mode == "peer":
+            layer.close()
         dist.barrier()
     finally:
         dist.destroy_process_group()

@@ -1,5 +1,6 @@
-"""Expert parallelism: the exchange logic on gloo ranks (CPU) and the CUDA path
-over NCCL (needs two GPUs)."""
+"""Expert parallelism: the exchange logic on gloo ranks (CPU), the CUDA path
+over NCCL and over peer memory (two GPUs), and the peer-memory path as a
+one-rank group (one GPU)."""
 import socket
 
 import pytest
@@ -35,4 +36,18 @@ def test_shard_range():
 def test_ep_nccl_two_gpus_matches_single_gpu():
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
-    mp.spawn(EH.gpu_worker, args=(2, _free_port()), nprocs=2, join=True)
+    mp.spawn(EH.gpu_worker, args=(2, _free_port(), "nccl"), nprocs=2, join=True)
+
+
+@pytest.mark.gpu
+def test_ep_peer_one_gpu_matches_single_gpu():
+    """The peer-memory exchange with one rank: dispatch, flags, the local layer
+    on the padded receive area, the return and the combine on one GPU."""
+    mp.spawn(EH.gpu_worker, args=(1, _free_port(), "peer"), nprocs=1, join=True)
+
+
+@pytest.mark.gpu
+def test_ep_peer_two_gpus_matches_nccl_and_single_gpu():
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    mp.spawn(EH.gpu_worker, args=(2, _free_port(), "peer"), nprocs=2, join=True)
