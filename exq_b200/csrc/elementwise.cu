@@ -222,17 +222,17 @@ inline int grid_for(int64_t work, int threads, int max_blocks_per_sm = 8) {
 
 int launch_combine_partials(const float* partial, int64_t H, const int32_t* pos_of_slot,
                             const void* topk_w, int w_dtype, int top_k, int64_t n_tokens, int spt,
-                            void* out, int dtype, cudaStream_t stream) {
+                            void* out, int dtype, cudaStream_t stream, bool pdl) {
   if (n_tokens == 0) return EXQ_OK;
   const int threads = static_cast<int>(H / 4 < 256 ? (H / 4 < 32 ? 32 : H / 4) : 256);
   const int grid = static_cast<int>(n_tokens < 65535 ? n_tokens : 65535);
   cudaError_t e;
   if (dtype == EXQ_F16)
-    e = launch_pdl(combine_partials_kernel<__half>, dim3(grid), dim3(threads),
+    e = launch_pdl(pdl, combine_partials_kernel<__half>, dim3(grid), dim3(threads),
                    2 * sizeof(int32_t) * spt, stream, partial, H, pos_of_slot, topk_w, w_dtype,
                    top_k, n_tokens, spt, static_cast<__half*>(out));
   else
-    e = launch_pdl(combine_partials_kernel<__nv_bfloat16>, dim3(grid), dim3(threads),
+    e = launch_pdl(pdl, combine_partials_kernel<__nv_bfloat16>, dim3(grid), dim3(threads),
                    2 * sizeof(int32_t) * spt, stream, partial, H, pos_of_slot, topk_w, w_dtype,
                    top_k, n_tokens, spt, static_cast<__nv_bfloat16*>(out));
   if (e != cudaSuccess) {

@@ -224,7 +224,12 @@ __global__ void __launch_bounds__(kEpThreads) ep_pack_kernel(EpPackArgs a) {
   const int chunk = (total + gridDim.x - 1) / gridDim.x;
   const int r0 = blockIdx.x * chunk, r1 = min(total, r0 + chunk);
   for (int r = r0 + threadIdx.x; r < r1; r += kEpThreads) {
-    const int slot = row_slot[r], d = dst[slot];
+    const int slot = row_slot[r];
+    if (slot < 0 || slot >= n) {  // cannot happen: every grouped row has a slot
+      atomicOr(a.status, EXQ_DEV_BAD_SLOT);
+      continue;
+    }
+    const int d = dst[slot];
     const int64_t e = load_index(a.ids, a.ids_dtype, slot);
     int32_t* p = ids_of(r, d);
     if (p) *p = static_cast<int32_t>(e - static_cast<int64_t>(d) * a.per_rank);
@@ -234,6 +239,7 @@ __global__ void __launch_bounds__(kEpThreads) ep_pack_kernel(EpPackArgs a) {
     const int r = r0 + static_cast<int>(idx / vecs);
     const int64_t v = idx - static_cast<int64_t>(r - r0) * vecs;
     const int slot = row_slot[r];
+    if (slot < 0 || slot >= n) continue;  // flagged above
     uint8_t* p = row_of(r, dst[slot]);
     if (!p) continue;
     const int tok = slot / a.top_k;

@@ -5,19 +5,22 @@
 
 namespace exq {
 
-// Programmatic dependent launch.  A kernel launched with launch_pdl may start
-// while its predecessor in the stream is still running: it must call
+// Programmatic dependent launch.  A kernel launched with launch_pdl(true, ...)
+// may start while its predecessor in the stream is still running: it must call
 // pdl_wait() before touching anything the predecessor writes, and calls
 // pdl_trigger() to let its own successor launch early.  Both are no-ops for
-// ordinary launches.
+// ordinary launches (launch_pdl(false, ...)).  Only a kernel whose stream
+// predecessor is another kernel of the same call is launched programmatically:
+// the first kernel of a call may follow a copy or a wait on another stream's
+// event (an NCCL collective), which griddepcontrol.wait does not cover.
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_trigger() {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
 template <typename... KArgs, typename... Args>
-inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
-                              cudaStream_t stream, Args... args) {
+inline cudaError_t launch_pdl(bool pdl, void (*kernel)(KArgs...), dim3 grid, dim3 block,
+                              size_t smem, cudaStream_t stream, Args... args) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = block;
@@ -27,7 +30,7 @@ inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, s
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = pdl ? 1 : 0;
   return cudaLaunchKernelEx(&cfg, kernel, args...);
 }
 
@@ -104,7 +107,7 @@ struct RouteGatherParams {
   uint32_t* status;
 };
 
-int launch_route_gather(RouteGatherParams& p, cudaStream_t stream);
+int launch_route_gather(RouteGatherParams& p, cudaStream_t stream, bool pdl);
 
 // ------------------------------------------------------------ grouped GEMM
 constexpr int kGmMTHost = 32;   // max token rows per GEMM tile
@@ -143,7 +146,7 @@ int launch_gemm(const GemmParams& p, int act_dtype, int max_items, cudaStream_t 
 // y[t] = sum_j w[t, j] * partial[pos_of_slot[t * spt + j]] (w = 1 past top_k).
 int launch_combine_partials(const float* partial, int64_t H, const int32_t* pos_of_slot,
                             const void* topk_w, int w_dtype, int top_k, int64_t n_tokens, int spt,
-                            void* out, int dtype, cudaStream_t stream);
+                            void* out, int dtype, cudaStream_t stream, bool pdl);
 
 uint32_t* device_status_ptr();
 

@@ -377,10 +377,12 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
   tc_fence_after();
   const uint32_t tmem = misc[0];
   // everything above overlaps the tail of the previous kernel in the stream.
-  // With p.weights_early the tile list was written two launches back; with
-  // p.tiles_from_ids the CTA builds it from the routing ids.  Either way only
-  // the activation producer (which reads the predecessor's output) waits, and
-  // the weight producer and the dequantisers start on the first slots at once.
+  // With p.weights_early the tile list was written two launches back, by a
+  // routing kernel that had finished before the predecessor let this kernel
+  // launch; with p.tiles_from_ids the CTA builds it from the routing ids, which
+  // predate the routing kernel.  Either way only the activation producer
+  // (which reads the predecessor's output) waits, and the weight producer and
+  // the dequantisers start on the first slots at once.
   const bool early = p.weights_early || p.tiles_from_ids;
   if (!early) pdl_wait();
   pdl_trigger();
@@ -982,7 +984,7 @@ static int build_maps(const exq_moe_weights* w, int proj, const void* act, int64
   return EXQ_OK;
 }
 
-int launch_tc(const TcParams& p, int max_items, cudaStream_t stream) {
+int launch_tc(const TcParams& p, int max_items, cudaStream_t stream, bool pdl) {
   static int attr_done[64] = {0};
   static int sms[64] = {0};
   int dev = 0;
@@ -1002,7 +1004,8 @@ int launch_tc(const TcParams& p, int max_items, cudaStream_t stream) {
   int grid = sms[dev];
   if (max_items < grid) grid = max_items;
   if (grid < 1) grid = 1;
-  const cudaError_t e = launch_pdl(moe_tc_kernel, dim3(grid), dim3(kThreads), kSmemBytes, stream, p);
+  const cudaError_t e =
+      launch_pdl(pdl, moe_tc_kernel, dim3(grid), dim3(kThreads), kSmemBytes, stream, p);
   if (e != cudaSuccess) {
     set_error("moe_tc_kernel: %s", cudaGetErrorString(e));
     return EXQ_ERR_CUDA;
@@ -1013,18 +1016,18 @@ int launch_tc(const TcParams& p, int max_items, cudaStream_t stream) {
 
 int launch_prep(const void* hidden, int act_dtype, int64_t hid, int64_t n_tokens,
                 const int32_t* sorted_slot, int spt, int64_t n_pos, const int32_t* routed_total,
-                int mt, __half* out, cudaStream_t stream) {
+                int mt, __half* out, cudaStream_t stream, bool pdl) {
   if (n_pos == 0) return EXQ_OK;
   const int64_t work = n_pos * (hid / 8);
   int64_t grid = (work + 255) / 256;
   if (grid > 65535) grid = 65535;
   cudaError_t e;
   if (act_dtype == EXQ_F16)
-    e = launch_pdl(prep_act_kernel<__half>, dim3((int)grid), dim3(256), 0, stream,
+    e = launch_pdl(pdl, prep_act_kernel<__half>, dim3((int)grid), dim3(256), 0, stream,
                    static_cast<const __half*>(hidden), hid, n_tokens, sorted_slot, spt, n_pos,
                    routed_total, mt, out);
   else
-    e = launch_pdl(prep_act_kernel<__nv_bfloat16>, dim3((int)grid), dim3(256), 0, stream,
+    e = launch_pdl(pdl, prep_act_kernel<__nv_bfloat16>, dim3((int)grid), dim3(256), 0, stream,
                    static_cast<const __nv_bfloat16*>(hidden), hid, n_tokens, sorted_slot, spt, n_pos,
                    routed_total, mt, out);
   if (e != cudaSuccess) {
@@ -1160,6 +1163,9 @@ extern "C" int exq_moe_layer_forward_range(const exq_moe_weights* w, const void*
   uint32_t* status = device_status_ptr();
   if (!status) return EXQ_ERR_CUDA;
   int st = EXQ_OK;
+  // Launch programmatically (overlapping the previous kernel's tail) only after
+  // a kernel of this call: the first launch may follow a copy or an event wait.
+  bool chained = false;
 
   // decode-sized calls route and gather in one kernel (stage 0; stage 1 is empty)
   const bool fused = n_slots <= kRouteGatherMaxSlots && n_total <= kRouteGatherMaxBuckets;
@@ -1185,8 +1191,9 @@ extern "C" int exq_moe_layer_forward_range(const exq_moe_weights* w, const void*
     rg.tile_info = ws.tile_info;
     rg.n_tiles = ws.n_tiles;
     rg.max_tiles = ws.max_tiles;
-    st = launch_route_gather(rg, s);
+    st = launch_route_gather(rg, s, chained);
     if (st != EXQ_OK) return st;
+    chained = true;
   }
   if (!fused && first_stage <= 0 && end_stage > 0) {
     RouteParams rp{};
@@ -1207,15 +1214,17 @@ extern "C" int exq_moe_layer_forward_range(const exq_moe_weights* w, const void*
     rp.tile_info = ws.tile_info;
     rp.n_tiles = ws.n_tiles;
     rp.max_tiles = ws.max_tiles;
-    st = launch_route(rp, kRouteLayer, s, true);
+    st = launch_route(rp, kRouteLayer, s, chained);
     if (st != EXQ_OK) return st;
+    chained = true;
   }
   if (!fused && first_stage <= 1 && end_stage > 1) {
     st = tc::launch_prep(hidden_states, act_dtype, H, n_tokens, ws.sorted_slot, spt, n_slots,
-                         ws.ends + n_total, kLayerMT, ws.act,
-                         s);
+                         ws.ends + n_total, kLayerMT, ws.act, s, chained);
     if (st != EXQ_OK) return st;
+    chained = true;
   }
+  bool gate_up_from_ids = false;  // gate_up of this call let down launch at once
   for (int proj = 0; proj < 2; ++proj) {
     const int stage = 2 + proj;
     if (!(first_stage <= stage && end_stage > stage)) continue;
@@ -1235,15 +1244,27 @@ extern "C" int exq_moe_layer_forward_range(const exq_moe_weights* w, const void*
     p.out_stride = proj == 0 ? I : H;
     p.n_pos = n_slots;
     p.status = status;
-    // down right after gate_up in this call: its tile list predates gate_up
-    p.weights_early = proj == 1 && first_stage <= 2;
     const int64_t max_items = ws.max_tiles * p.nblocks;
-    // gate_up right after the fused routing in this call: build the tiles from
-    // the ids (complete before routing started) and stream weights at once;
-    // every CTA's items must fit its shared table
     const int64_t grid = max_items < num_sms() ? max_items : num_sms();
-    p.tiles_from_ids = proj == 0 && fused && first_stage == 0 && n_total <= tc::kHistBuckets &&
-                       max_items <= static_cast<int64_t>(tc::kItemTab) * (grid > 0 ? grid : 1);
+    // a CTA can build its items from the ids: the experts fit the histogram and
+    // every CTA's items fit its shared table
+    const bool ids_ok = n_total <= tc::kHistBuckets &&
+                        max_items <= static_cast<int64_t>(tc::kItemTab) * (grid > 0 ? grid : 1);
+    if (proj == 0) {
+      // right after the fused routing of this call: build the tiles from the ids
+      // (complete before routing started) and stream weights at once, letting
+      // down launch before the routing kernel has finished
+      p.tiles_from_ids = fused && first_stage == 0 && ids_ok;
+      gate_up_from_ids = p.tiles_from_ids;
+    } else if (gate_up_from_ids) {
+      // the routing kernel's tile list may still be being written: build the
+      // tiles from the ids as gate_up did, or read the list after waiting
+      p.tiles_from_ids = ids_ok;
+    } else {
+      // gate_up of this call waited for the routing before letting down launch,
+      // so the tile list is complete: stream weights at once
+      p.weights_early = first_stage <= 2;
+    }
     p.ids = topk_ids;
     p.ids_dtype = ids_dtype;
     p.top_k = top_k;
@@ -1251,11 +1272,13 @@ extern "C" int exq_moe_layer_forward_range(const exq_moe_weights* w, const void*
     p.n_routed = w->n_routed;
     p.n_buckets = n_total;
     p.n_slots = n_slots;
-    st = tc::launch_tc(p, static_cast<int>(max_items < INT32_MAX ? max_items : INT32_MAX), s);
+    st = tc::launch_tc(p, static_cast<int>(max_items < INT32_MAX ? max_items : INT32_MAX), s,
+                       chained);
     if (st != EXQ_OK) return st;
+    chained = true;
   }
   if (first_stage <= 4 && end_stage > 4)
     return launch_combine_partials(ws.partial, H, ws.pos_of_slot, topk_weights, w_dtype, top_k,
-                                   n_tokens, spt, out, act_dtype, s);
+                                   n_tokens, spt, out, act_dtype, s, chained);
   return EXQ_OK;
 }

@@ -279,7 +279,8 @@ int launch_route(RouteParams& p, int mode, cudaStream_t stream, bool pdl) {
     attr_set[dev] = true;
   }
   if (pdl) {
-    const cudaError_t e = launch_pdl(route_kernel, dim3(1), dim3(kRouteThreads), smem, stream, p, mode);
+    const cudaError_t e =
+        launch_pdl(true, route_kernel, dim3(1), dim3(kRouteThreads), smem, stream, p, mode);
     if (e != cudaSuccess) {
       set_error("route_kernel: %s", cudaGetErrorString(e));
       return EXQ_ERR_CUDA;

@@ -250,7 +250,7 @@ __global__ void __launch_bounds__(kRgThreads) route_gather_kernel(const RouteGat
 
 }  // namespace
 
-int launch_route_gather(RouteGatherParams& p, cudaStream_t stream) {
+int launch_route_gather(RouteGatherParams& p, cudaStream_t stream, bool pdl) {
   if (p.n_buckets < 1 || p.n_buckets > kRouteGatherMaxBuckets || p.n > kRouteGatherMaxSlots) {
     set_error("route_gather: %d buckets / %lld slots outside the fused path", p.n_buckets,
               (long long)p.n);
@@ -277,10 +277,10 @@ int launch_route_gather(RouteGatherParams& p, cudaStream_t stream) {
   if (grid > cap) grid = cap;
   cudaError_t e;
   if (p.act_dtype == EXQ_F16)
-    e = launch_pdl(route_gather_kernel<__half>, dim3(static_cast<int>(grid)), dim3(kRgThreads),
-                   smem, stream, p);
+    e = launch_pdl(pdl, route_gather_kernel<__half>, dim3(static_cast<int>(grid)),
+                   dim3(kRgThreads), smem, stream, p);
   else
-    e = launch_pdl(route_gather_kernel<__nv_bfloat16>, dim3(static_cast<int>(grid)),
+    e = launch_pdl(pdl, route_gather_kernel<__nv_bfloat16>, dim3(static_cast<int>(grid)),
                    dim3(kRgThreads), smem, stream, p);
   if (e != cudaSuccess) {
     set_error("route_gather_kernel: %s", cudaGetErrorString(e));

@@ -56,8 +56,9 @@ def _cuda_pack(hidden: torch.Tensor, topk_ids: torch.Tensor, per_rank: int, worl
     t, k = topk_ids.shape
     dev = hidden.device
     ids = topk_ids.contiguous()
-    send_rows = torch.empty(t * k, hidden.shape[1], dtype=hidden.dtype, device=dev)
-    send_ids = torch.empty(t * k, dtype=torch.int32, device=dev)
+    # at least one row, so that an empty exchange still hands NCCL real buffers
+    send_rows = torch.empty(max(t * k, 1), hidden.shape[1], dtype=hidden.dtype, device=dev)
+    send_ids = torch.empty(max(t * k, 1), dtype=torch.int32, device=dev)
     slot_row = torch.empty(t * k, dtype=torch.int32, device=dev)
     counts = torch.empty(world, dtype=torch.int32, device=dev)
     L.check(L.lib().exq_ep_pack(L.ptr(ids), L.tag(ids), t, k, per_rank, world,
@@ -198,7 +199,7 @@ class ExpertParallelLayer:
     # default compute: the fused layer kernel, one expert of weight 1 per row
     def _bank_rows(self, rows: torch.Tensor, local_ids: torch.Tensor) -> torch.Tensor:
         if rows.shape[0] == 0:
-            return rows.new_empty(0, rows.shape[1])
+            return rows.new_empty(1, rows.shape[1])[:0]
         ones = torch.ones(rows.shape[0], 1, dtype=torch.float32, device=rows.device)
         return self.local_bank(rows, local_ids.view(-1, 1), ones)
 
@@ -240,8 +241,10 @@ class ExpertParallelLayer:
             ready.synchronize()
         sc, rc = counts[:self.world].tolist(), counts[self.world:].tolist()
         n_send = sum(sc)
-        recv_rows = hidden.new_empty(sum(rc), h)
-        recv_ids = torch.empty(sum(rc), dtype=torch.int32, device=hidden.device)
+        n_recv = sum(rc)
+        # buffers of at least one row: an empty exchange still passes NCCL real addresses
+        recv_rows = hidden.new_empty(max(n_recv, 1), h)[:n_recv]
+        recv_ids = torch.empty(max(n_recv, 1), dtype=torch.int32, device=hidden.device)[:n_recv]
         dist.all_to_all_single(recv_rows, send_rows[:n_send], rc, sc, group=self.group)
         dist.all_to_all_single(recv_ids, send_ids[:n_send], rc, sc, group=self.group)
 

@@ -4,7 +4,10 @@ The CPU workers run the exchange of exq_b200.ep.ExpertParallelLayer on gloo
 ranks with the CPU oracle as the local expert compute and the combine; the
 GPU worker runs the real kernels over NCCL and compares with the full layer
 on one GPU."""
+import faulthandler
 import os
+import sys
+import traceback
 
 import torch
 import torch.distributed as dist
@@ -15,6 +18,9 @@ H, I, E, K = 64, 32, 8, 2
 
 
 def _init(rank, world, port, backend):
+    # a rank that is still running after 50 s prints every thread's stack, so
+    # a stuck rank shows where it waits before the group timeout ends the test
+    faulthandler.dump_traceback_later(50, exit=False)
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     from datetime import timedelta
@@ -106,11 +112,12 @@ def _gpu_step_inputs(step, rank, world, t, case, e, h, k, dev):
     return x, ids.to(dev), w.to(dev)
 
 
-def gpu_worker(rank, world, port, mode="nccl"):
+def gpu_worker(rank, world, port, mode="nccl", max_tokens=64):
     """EP on `world` GPUs vs the whole layer on one GPU (Mixtral-like, bf16),
     over four steps: spread routing, a rank with no tokens, every slot to rank
-    0's experts, spread again.  mode "peer": the peer-memory exchange, also
-    checked bit for bit against the NCCL exchange when world > 1."""
+    0's experts, spread again.  mode "peer": the peer-memory exchange (receive
+    area of world * max_tokens * top_k rows), also checked bit for bit against
+    the NCCL exchange when world > 1."""
     from exq_b200 import ExpertBank
     from exq_b200 import _lib as L
     from exq_b200.ep import ExpertParallelLayer, build_rank_banks
@@ -124,7 +131,7 @@ def gpu_worker(rank, world, port, mode="nccl"):
         local, _ = build_rank_banks(w13, w2, world, rank, act_dtype=torch.bfloat16)
         full = ExpertBank.from_dense(w13, w2, None, act_dtype=torch.bfloat16)
         if mode == "peer":
-            layer = ExpertParallelLayer(local, e, max_tokens=64, top_k=k)
+            layer = ExpertParallelLayer(local, e, max_tokens=max_tokens, top_k=k)
             nccl = ExpertParallelLayer(local, e) if world > 1 else None
         else:
             layer, nccl = ExpertParallelLayer(local, e), None
@@ -149,5 +156,10 @@ def gpu_worker(rank, world, port, mode="nccl"):
         if mode == "peer":
             layer.close()
         dist.barrier()
+    except BaseException:
+        # print before the process group teardown, which may abort the process
+        traceback.print_exc()
+        sys.stderr.flush()
+        raise
     finally:
         dist.destroy_process_group()

@@ -40,10 +40,13 @@ def test_ep_nccl_two_gpus_matches_single_gpu():
 
 
 @pytest.mark.gpu
-def test_ep_peer_one_gpu_matches_single_gpu():
+@pytest.mark.parametrize("max_tokens", [64, 2100])
+def test_ep_peer_one_gpu_matches_single_gpu(max_tokens):
     """The peer-memory exchange with one rank: dispatch, flags, the local layer
-    on the padded receive area, the return and the combine on one GPU."""
-    mp.spawn(EH.gpu_worker, args=(1, _free_port(), "peer"), nprocs=1, join=True)
+    on the padded receive area, the return and the combine on one GPU.  With
+    max_tokens 2100 the receive area (4200 rows) is above the fused routing
+    limit, so the layer takes its separate route and prep kernels."""
+    mp.spawn(EH.gpu_worker, args=(1, _free_port(), "peer", max_tokens), nprocs=1, join=True)
 
 
 @pytest.mark.gpu

@@ -220,6 +220,29 @@ def test_layer_deterministic_and_token_count_edges(cuda):
     assert OM.rel_l2(ys, ref) < TOL
 
 
+def test_layer_back_to_back_calls_keep_their_own_tiles(cuda):
+    """Calls launched back to back on one stream, with different routings on
+    one cached workspace, each equal bit for bit the same call made alone: a
+    kernel that starts before its predecessors finish (programmatic launch)
+    must not read the previous call's tile list."""
+    from exq_b200.synth import hidden_states, zipf_router
+    bank, c = _bank("qwen3", cuda, n_experts=64)
+    calls = []
+    for i, t in enumerate([256, 3, 64, 1, 200, 17]):
+        ids, w = zipf_router(t, 64, 8, seed=40 + i)
+        x = hidden_states(t, c.hidden, seed=40 + i).to(cuda)
+        calls.append((x, ids.to(cuda), w.to(cuda)))
+    alone = []
+    for args in calls:
+        alone.append(bank(*args))
+        torch.cuda.synchronize()
+    for _ in range(20):
+        outs = [bank(*args) for args in calls]
+        torch.cuda.synchronize()
+        for o, a in zip(outs, alone):
+            assert torch.equal(o, a)
+
+
 def test_layer_bad_expert_id_dropped_and_flagged(cuda):
     from exq_b200 import _lib as L
     from exq_b200.synth import hidden_states, zipf_router
