@@ -163,3 +163,50 @@ def gpu_worker(rank, world, port, mode="nccl", max_tokens=64):
         raise
     finally:
         dist.destroy_process_group()
+
+
+def gpu_graph_worker(rank, world, port):
+    """The peer-memory exchange captured in a CUDA graph: each replay with new
+    inputs in the captured buffers equals an eager call bit for bit (the step
+    counter lives on the device, so replays and eager calls interleave)."""
+    from exq_b200 import _lib as L
+    from exq_b200.ep import ExpertParallelLayer, build_rank_banks
+    from exq_b200.synth import expert_weights
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    _init(rank, world, port, "nccl")
+    try:
+        e, h, inter, k, t = 8, 512, 256, 2, 40
+        w13, w2 = expert_weights(e, inter, h, seed=0, device=dev)
+        local, _ = build_rank_banks(w13, w2, world, rank, act_dtype=torch.bfloat16)
+        layer = ExpertParallelLayer(local, e, max_tokens=64, top_k=k)
+        x0, ids0, w0 = _gpu_step_inputs(0, rank, world, t, "spread", e, h, k, dev)
+        xs, idss, ws = x0.clone(), ids0.clone(), w0.clone()
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            layer(xs, idss, ws)
+        torch.cuda.current_stream(dev).wait_stream(side)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            ys = layer(xs, idss, ws)
+        for step in range(1, 4):
+            x, ids, w = _gpu_step_inputs(step, rank, world, t, "spread", e, h, k, dev)
+            xs.copy_(x)
+            idss.copy_(ids.to(idss.dtype))
+            ws.copy_(w)
+            graph.replay()
+            ref = layer(x, ids, w)
+            torch.cuda.synchronize(dev)
+            assert torch.equal(ys, ref), f"rank {rank} replay {step} differs from the eager call"
+        status = L.read_device_status(dev, clear=True)
+        assert status == 0, f"rank {rank}: device status {status:#x}"
+        del graph
+        layer.close()
+        dist.barrier()
+    except BaseException:
+        traceback.print_exc()
+        sys.stderr.flush()
+        raise
+    finally:
+        dist.destroy_process_group()

@@ -50,6 +50,13 @@ def test_ep_peer_one_gpu_matches_single_gpu(max_tokens):
 
 
 @pytest.mark.gpu
+def test_ep_peer_step_replays_from_a_cuda_graph():
+    """A peer-memory step captured once in a CUDA graph and replayed with new
+    inputs equals the eager call (one-rank group, one GPU)."""
+    mp.spawn(EH.gpu_graph_worker, args=(1, _free_port()), nprocs=1, join=True)
+
+
+@pytest.mark.gpu
 def test_ep_peer_two_gpus_matches_nccl_and_single_gpu():
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
