@@ -410,6 +410,7 @@ def ep_measure(dev, world, rank, name, steps=50, warmup=5):
     owned experts that received tokens, per rank."""
     import torch
     import torch.distributed as dist
+    from exq_b200 import _lib as L
     from exq_b200.ep import ExpertParallelLayer, build_rank_banks
     from exq_b200.synth import CONFIGS, expert_weights, hidden_states, zipf_router
     c = CONFIGS[name]
@@ -427,8 +428,13 @@ def ep_measure(dev, world, rank, name, steps=50, warmup=5):
     else:
         local, shared = build_rank_banks(w13, w2, world, rank, act_dtype=c.act_dtype,
                                          shared_w13=sw13, shared_w2=sw2)
-        layer = ExpertParallelLayer(local, c.n_experts, shared_bank=shared, max_tokens=t,
-                                    top_k=c.top_k)
+        try:
+            layer = ExpertParallelLayer(local, c.n_experts, shared_bank=shared, max_tokens=t,
+                                        top_k=c.top_k)
+            exchange = "peer memory (NVLink stores)"
+        except RuntimeError as e:  # raised on every rank alike: time the NCCL exchange
+            layer = ExpertParallelLayer(local, c.n_experts, shared_bank=shared)
+            exchange = f"nccl ({e})"
     del w13, w2, sw13, sw2
     torch.cuda.empty_cache()
     ids, w = zipf_router(t, c.n_experts, c.top_k, seed=11 + rank)
@@ -475,11 +481,15 @@ def ep_measure(dev, world, rank, name, steps=50, warmup=5):
            "weight_GBps_per_rank": round(float(wbytes.item()) / (us * 1e-6) / 1e9, 1),
            "tokens_per_s_total": round(world * t / (us * 1e-6), 1)}
     if world > 1:
-        out["exchange"] = "peer memory (NVLink stores)"
+        out["exchange"] = exchange
         out["nccl_us_per_step"] = nccl_us
+        # EXQ_DEV_* bits any rank's kernels raised (a wait that ran out: 8)
+        st = torch.tensor([L.read_device_status(dev)], device=dev, dtype=torch.int64)
+        dist.all_reduce(st, op=dist.ReduceOp.MAX)
+        out["device_status"] = int(st.item())
     if world == 1 and name == "mixtral":
         out["prefill"] = prefill_measure(layer, c, dev)
-    if world > 1:
+    if world > 1 and layer.peer is not None:
         layer.close()
     del layer, local, shared
     torch.cuda.empty_cache()

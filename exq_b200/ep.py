@@ -101,32 +101,57 @@ class PeerExchange:
             raise ValueError(f"bad expert-parallel buffer sizes: {self.world} ranks, capacity "
                              f"{capacity}, hidden {hidden}")
         self.nbytes = nbytes
+        self.ptr, self._mapped = None, []
         with torch.cuda.device(device):
-            own = C.c_void_p()
             handle = (C.c_uint8 * 64)()
-            L.check(lib.exq_ep_ipc_alloc(nbytes, C.byref(own), handle), "ep_ipc_alloc")
-            self.ptr = own.value
-            self._mapped = []
-            L.check(lib.exq_ep_buffer_init(self.ptr, self.world, capacity, hidden,
-                                           L.stream_of(device)), "ep_buffer_init")
-            # every rank's buffer is initialised before its handle is published,
-            # so no rank writes into a buffer that is still being cleared
-            torch.cuda.synchronize(device)
+            err = None
+            try:
+                own = C.c_void_p()
+                L.check(lib.exq_ep_ipc_alloc(nbytes, C.byref(own), handle), "ep_ipc_alloc")
+                self.ptr = own.value
+                L.check(lib.exq_ep_buffer_init(self.ptr, self.world, capacity, hidden,
+                                               L.stream_of(device)), "ep_buffer_init")
+                # every rank's buffer is initialised before its handle is
+                # published, so no rank writes into a buffer still being cleared
+                torch.cuda.synchronize(device)
+            except Exception as e:  # noqa: BLE001 - reported to every rank below
+                err = e
+            self._agree(err)
             mine = torch.tensor(list(bytes(handle)), dtype=torch.uint8, device=device)
             every = torch.empty(self.world, 64, dtype=torch.uint8, device=device)
             dist.all_gather_into_tensor(every, mine, group=group)
             every = every.cpu()
             addrs = []
-            for r in range(self.world):
-                if r == self.rank:
-                    addrs.append(self.ptr)
-                    continue
-                p = C.c_void_p()
-                h = (C.c_uint8 * 64)(*every[r].tolist())
-                L.check(lib.exq_ep_ipc_open(h, C.byref(p)), "ep_ipc_open")
-                self._mapped.append(p.value)
-                addrs.append(p.value)
+            try:
+                for r in range(self.world):
+                    if r == self.rank:
+                        addrs.append(self.ptr)
+                        continue
+                    p = C.c_void_p()
+                    h = (C.c_uint8 * 64)(*every[r].tolist())
+                    L.check(lib.exq_ep_ipc_open(h, C.byref(p)), "ep_ipc_open")
+                    self._mapped.append(p.value)
+                    addrs.append(p.value)
+            except Exception as e:  # noqa: BLE001
+                err = e
+            self._agree(err)
             self.peers = torch.tensor(addrs, dtype=torch.int64, device=device)
+
+    def _agree(self, err) -> None:
+        """Collective: every rank raises if any rank failed, so that no rank is
+        left waiting for a peer that gave up."""
+        ok = torch.tensor([0 if err else 1], dtype=torch.int32, device=self.device)
+        dist.all_reduce(ok, op=dist.ReduceOp.MIN, group=self.group)
+        if int(ok.item()) == 1:
+            return
+        lib = L.lib()
+        for p in self._mapped:
+            lib.exq_ep_ipc_close(p)
+        if self.ptr is not None:
+            lib.exq_ep_ipc_free(self.ptr)
+        self._mapped, self.ptr = [], None
+        why = f"{type(err).__name__}: {err}" if err else "failed on another rank"
+        raise RuntimeError(f"peer-memory exchange unavailable on rank {self.rank}: {why}")
 
     def close(self) -> None:
         if self.ptr is None:

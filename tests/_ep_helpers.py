@@ -210,3 +210,23 @@ def gpu_graph_worker(rank, world, port):
         raise
     finally:
         dist.destroy_process_group()
+
+
+def agree_worker(rank, world, port):
+    """PeerExchange setup failures are collective: a failure on one rank makes
+    every rank raise, so no rank waits for a peer that gave up."""
+    from exq_b200.ep import PeerExchange
+    _init(rank, world, port, "gloo")
+    try:
+        px = PeerExchange.__new__(PeerExchange)
+        px.group, px.world, px.rank = None, world, rank
+        px.device, px._mapped, px.ptr = torch.device("cpu"), [], None
+        px._agree(None)
+        try:
+            px._agree(ValueError("no peer access") if rank == 0 else None)
+        except RuntimeError as e:
+            assert ("no peer access" in str(e)) == (rank == 0), str(e)
+        else:
+            raise AssertionError(f"rank {rank} went on although rank 0 failed")
+    finally:
+        dist.destroy_process_group()

@@ -24,6 +24,10 @@ def test_ep_exchange_matches_single_process_oracle(case, t_per_rank):
     mp.spawn(EH.cpu_worker, args=(2, _free_port(), case, t_per_rank), nprocs=2, join=True)
 
 
+def test_peer_exchange_setup_failure_is_collective():
+    mp.spawn(EH.agree_worker, args=(2, _free_port()), nprocs=2, join=True)
+
+
 def test_shard_range():
     from exq_b200.ep import shard_range
     assert shard_range(8, 2, 1) == (4, 8)
