@@ -18,7 +18,8 @@
 //                tensor memory and B (tokens) in shared memory, M=128 rows,
 //                N=tokens, K=16, into a double-buffered accumulator
 //   warps 3-6    epilogue: tcgen05.ld of the accumulator, fused SiLU*mul
-//                (gate_up) or router-weighted fp32 partials (down)
+//                (gate_up) or fp32 partials, INT8 row scale applied (down);
+//                the router weights are applied by the combine
 //   warps 7-18   dequantisers, three groups of four warps (one per lane
 //                quarter).  Group g takes every third weight slot (weight-ring
 //                positions g and g+3, tensor-memory A buffer g), so each ring
@@ -60,7 +61,8 @@ constexpr int kWStages = 6, kABufs = 3, kBStages = 3;  // weight slots, TMEM A b
 constexpr int kWSlot = 16384, kSSlot = 512, kBSlot = 32768;
 constexpr int kACols = 128;  // tensor-memory columns per A buffer (128 rows x 256 fp16)
 constexpr int kMaxN = 64;        // tokens per item (the MMA's N)
-static_assert(kMaxN <= 64, "the down epilogue holds the router weights of 64 tokens per warp");
+static_assert(kMaxN <= 64, "two accumulators of kMaxN columns and three 128-column A buffers "
+                            "fill the 512 tensor-memory columns");
 constexpr int kBRows = 256;      // activation rows one B slot holds (256 rows x 128 B)
 constexpr int kTmemCols = 512;
 constexpr int kTmemA = 2 * kMaxN;  // first tensor-memory column of the A buffers
