@@ -62,6 +62,40 @@ def test_invalid_arguments_rejected_on_host(lib_path):
                                            1 << 30, None, 3, 9) == -1
 
 
+def test_ep_entry_points_validate_on_host(lib_path):
+    """The expert-parallel entry points size their buffer with plain arithmetic
+    and reject bad arguments before any CUDA call."""
+    lib = L.lib()
+    up = lambda v: (v + 255) // 256 * 256  # noqa: E731
+    p, cap, h = 2, 512, 4096
+    rows = p * cap
+    assert lib.exq_ep_buffer_bytes(p, cap, h) == 1024 + 2 * up(4 * rows) + 2 * up(rows * 2 * h)
+    for bad in [(0, cap, h), (65, cap, h), (p, 0, h), (p, cap, 7), (64, 1 << 25, h)]:
+        assert lib.exq_ep_buffer_bytes(*bad) == 0
+    assert lib.exq_ep_buffer_init(None, p, cap, h, None) == -1
+    assert "buffer is null" in lib.exq_last_error().decode()
+    assert lib.exq_ep_ipc_alloc(0, C.byref(C.c_void_p()), None) == -1
+    assert lib.exq_ep_ipc_open(None, C.byref(C.c_void_p())) == -1
+    assert lib.exq_ep_ipc_free(None) == 0 and lib.exq_ep_ipc_close(None) == 0
+    peers = 256
+    # rank outside the group
+    assert lib.exq_ep_dispatch(1, L.I32, 4, 2, 4, p, p, 256, L.F16, h, cap, peers, 1, None) == -1
+    assert "rank 2 of 2" in lib.exq_last_error().decode()
+    # ids dtype, activation dtype, more slots than one call takes
+    assert lib.exq_ep_dispatch(1, L.F32, 4, 2, 4, p, 0, 256, L.F16, h, cap, peers, 1, None) == -1
+    assert lib.exq_ep_dispatch(1, L.I32, 4, 2, 4, p, 0, 256, L.F32, h, cap, peers, 1, None) == -1
+    assert lib.exq_ep_dispatch(1, L.I32, 4097, 1, 4, p, 0, 256, L.F16, h, cap, peers, 1,
+                               None) == -2
+    # the local bank holds routed experts only
+    from exq_b200.experts import MoeWeightsC
+    w = MoeWeightsC()
+    w.n_routed, w.n_shared, w.hidden, w.inter = 4, 1, h, 256
+    assert lib.exq_ep_expert_forward(C.byref(w), L.F16, p, 0, cap, 256, peers, 256, 1 << 30,
+                                     None) == -1
+    assert "shared experts" in lib.exq_last_error().decode()
+    assert lib.exq_ep_combine_peer(256, p, cap, h, L.F16, 1, 1, L.I32, 4, 2, None, 1, None) == -1
+
+
 def test_workspace_sizes_grow_with_tokens(lib_path):
     lib = L.lib()
     a = lib.exq_moe_layer_workspace_bytes(1, 8, 0, 128, 2048, 768)
