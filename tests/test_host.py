@@ -23,6 +23,25 @@ def test_library_exports_every_header_symbol(lib_path):
     assert L.lib().exq_abi_version() == 1
 
 
+def test_ctypes_bindings_match_header_arity():
+    """Every function the header declares is bound in exq_b200._lib with as many
+    arguments as the declaration has parameters (a stale binding would pass
+    shifted arguments to the library)."""
+    import re
+    from pathlib import Path
+    src = (Path(__file__).resolve().parent.parent / "include" / "exq_b200.h").read_text()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    decls = {}
+    for m in re.finditer(r"EXQ_API\s+[\w\s\*]*?\b(exq_\w+)\s*\(([^;]*?)\)\s*;", src, flags=re.S):
+        params = m.group(2).strip()
+        decls[m.group(1)] = 0 if params in ("", "void") else params.count(",") + 1
+    assert len(decls) >= 30
+    for name, n in decls.items():
+        assert name in L.SIGNATURES, f"{name} is declared but not bound"
+        assert len(L.SIGNATURES[name][1]) == n, f"{name}: {n} parameters, bound with " \
+            f"{len(L.SIGNATURES[name][1])}"
+
+
 def test_status_strings(lib_path):
     for code in (0, -1, -2, -3, -4):
         assert L.lib().exq_status_string(code)
