@@ -241,7 +241,9 @@ class ExpertParallelLayer:
         """[T, H] output for this rank's T tokens (same dtype as ``hidden``).
 
         Expert ids out of range are dropped and flagged in the device status,
-        as in the single-GPU layer."""
+        as in the single-GPU layer.  Every rank passes the same activation
+        dtype: a rank runs its experts on the rows it receives in the dtype of
+        its own ``hidden``."""
         if topk_ids.shape != topk_weights.shape or topk_ids.shape[0] != hidden.shape[0]:
             raise ValueError("topk_ids / topk_weights must be [T, k] for hidden [T, H]")
         if self.peer is not None:
