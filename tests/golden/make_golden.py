@@ -1,9 +1,9 @@
 """Generate the golden fixtures under tests/golden/ from the reference itself.
 
-Run in a container that has the reference checkout (read-only) at
-``$EXQ_REFERENCE`` (default /root/reference):
+Run in a container that has the reference checkout (read-only), with
+``$EXQ_REFERENCE`` set to its directory:
 
-    python tests/golden/make_golden.py
+    EXQ_REFERENCE=<reference checkout> python tests/golden/make_golden.py
 
 The reference's Python modules are loaded by file path (``exq/__init__.py``
 imports a Rust extension that is not built here), its ``@triton.jit`` kernels
@@ -38,7 +38,9 @@ os.environ["TRITON_INTERPRET"] = "1"
 import numpy as np  # noqa: E402
 import torch  # noqa: E402
 
-REF = Path(os.environ.get("EXQ_REFERENCE", "/root/reference"))
+if "EXQ_REFERENCE" not in os.environ:
+    sys.exit("set EXQ_REFERENCE to the reference checkout's directory")
+REF = Path(os.environ["EXQ_REFERENCE"])
 OUT = Path(__file__).resolve().parent
 
 
