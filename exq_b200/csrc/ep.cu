@@ -609,7 +609,7 @@ extern "C" int exq_ep_expert_forward(const exq_moe_weights* weights, int dtype, 
   if (r != EXQ_OK) return r;
   const float* partial = nullptr;
   const int32_t* pos = nullptr;
-  layer_partials(workspace, rows, weights->n_routed, H, weights->inter, &partial, &pos);
+  layer_partials(workspace, rows, rows, weights->n_routed, H, weights->inter, &partial, &pos);
   int grid = static_cast<int>(rows < 2 * num_sms() ? rows : 2 * num_sms());
   if (dtype == EXQ_F16)
     ep_return_kernel<__half><<<grid, kEpThreads, 0, s>>>(

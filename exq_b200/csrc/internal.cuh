@@ -75,6 +75,8 @@ struct RouteParams {
   int32_t* tile_info;          // LAYER: [max_tiles][3] = expert, first row, rows
   int32_t* n_tiles;            // LAYER: [1]
   int64_t max_tiles;
+  int32_t* counters;           // LAYER: zeroed (the GEMM's tile and combine counters)
+  int64_t n_counters;
   uint32_t* status;
 };
 
@@ -104,6 +106,9 @@ struct RouteGatherParams {
   int32_t* tile_info;   // [max_tiles][3]
   int32_t* n_tiles;     // [1]
   int64_t max_tiles;
+  int32_t* sorted_slot; // [n] slot at every sorted position (or null)
+  int32_t* counters;    // [n_counters] zeroed (the GEMM's tile and combine counters)
+  int64_t n_counters;
   uint32_t* status;
 };
 
@@ -153,7 +158,8 @@ uint32_t* device_status_ptr();
 // Views into a layer workspace (exq_moe_layer_forward_range) for a caller that
 // replaces the combine stage: the fp32 down partials [n_slots, hidden] by
 // sorted position and the slot -> sorted position map (-1: no expert).
-void layer_partials(void* workspace, int64_t n_slots, int n_buckets, int64_t hidden,
-                    int64_t inter, const float** partial, const int32_t** pos_of_slot);
+void layer_partials(void* workspace, int64_t n_slots, int64_t n_tokens, int n_buckets,
+                    int64_t hidden, int64_t inter, const float** partial,
+                    const int32_t** pos_of_slot);
 
 }  // namespace exq

@@ -52,9 +52,12 @@
 namespace exq {
 namespace tc {
 
-constexpr int kWarps = 19;
+constexpr int kWarps = 20;
 constexpr int kThreads = kWarps * 32;
 constexpr int kWarpW = 0, kWarpB = 1, kWarpMma = 2;
+constexpr int kWarpCmb = 19;    // fused top-k combine
+constexpr int kCmbRing = 4;     // down items the epilogue may run ahead of the combine warp
+constexpr int kCmbMaxSpt = 16;  // slots per token the fused combine handles
 constexpr int kEpiWarp0 = 3, kNumEpiWarps = 4;
 constexpr int kDqWarp0 = 7, kDqGroups = 3, kDqGroupWarps = 4;  // 3 groups x 4 lane quarters
 constexpr int kWStages = 6, kABufs = 3, kBStages = 3;  // weight slots, TMEM A buffers, B slots
@@ -72,34 +75,69 @@ constexpr int kOffB = 0;
 constexpr int kOffW = kOffB + kBStages * kBSlot;
 constexpr int kOffS = kOffW + kWStages * kWSlot;
 constexpr int kOffBar = kOffS + kWStages * kSSlot;
-constexpr int kNumBars = 2 * kWStages + 2 * kABufs + 2 * kBStages + 4;
+constexpr int kNumBars = 2 * kWStages + 2 * kABufs + 2 * kBStages + 4 + 2 * kCmbRing;
 constexpr int kOffMisc = kOffBar + kNumBars * 8;
 constexpr int kItemTab = 128;  // work items of this CTA decoded into shared memory up front
 constexpr int kOffItems = kOffMisc + 64;
 constexpr int kItemBytes = 48;  // sizeof(Item)
 constexpr int kHistBuckets = 1024;  // experts the in-kernel tile list handles
 constexpr int kOffHist = kOffItems + kItemTab * kItemBytes;  // 3 x (kHistBuckets + 1) ints
+// The histogram region is free once the item table is built; the combine
+// warp then keeps the slot positions and router weights of an item's rows
+// there: [kMaxN rows][kCmbMaxSpt] ints + floats.
+constexpr int kOffCmb = kOffHist;
+static_assert(2 * kMaxN * kCmbMaxSpt * 4 <= 3 * (kHistBuckets + 1) * 4, "combine staging size");
 constexpr int kSmemBytes = kOffHist + 3 * (kHistBuckets + 1) * 4 + 1024;  // + slack to align the base to 1024 B
+constexpr int kEpiBar = 1;  // named barrier of the four epilogue warps
 
 enum : int { kTierBF16 = EXQ_TIER_BF16, kTierINT8 = EXQ_TIER_INT8, kTierINT4 = EXQ_TIER_INT4 };
 
-struct TcParams {
-  CUtensorMap tm_w[3];  // weights of this projection per tier storage
-  CUtensorMap tm_s;     // INT4 group scales (group-major) of this projection
+// Constants of one projection (gate_up or down).
+struct ProjParams {
+  CUtensorMap tm_w[3];  // weights per tier storage
+  CUtensorMap tm_s;     // INT4 group scales (group-major)
   CUtensorMap tm_b[4];  // activations, stage-major [k/64][n_pos][64] fp16 (octet-permuted);
                         // map b: box of N = 16(b+1) rows x the stages of one B slot
+  const __half* s8;     // INT8 per-row scales
+  void* out;            // gate_up: mid (fp16, stage-major); down: fp32 partials [n_pos, H]
+  int64_t out_stride;
+  int gate_up;          // 1: gate_up (rows interleave gate/up), 0: down
+  int n_rows;           // rows of the projection (2I or H)
+  int k;
+  int nblocks;          // row blocks per tile: I/64 gate/up pairs, or H/128
+};
+
+// A launch runs the gate_up items (if run_gu) and then the down items (if
+// run_dn) of every tile.  Items are numbered tile-major inside each
+// projection: gate_up item i is (tile i / nb_gu, row block i % nb_gu).
+struct TcParams {
+  ProjParams pj[2];  // [0] gate_up, [1] down
+  int run_gu, run_dn;
+  // link (both projections in one launch): a gate_up item adds 1 to
+  // tile_done[tile] once its mid rows are stored; a down item's activation
+  // producer waits until all nb_gu row blocks of its tile have done so.
+  int link;
+  int* tile_done;
+  // fuse_combine (down items): y[t] = sum_j w[t, j] * partial[pos(t, j)] is
+  // computed by the combine warp of the CTA that stores a token's last partial
+  // row of a 128-column block, counted in comb_cnt[t * (H/128) + block]
+  // (zeroed by the route stage).  Same order and rounding as
+  // combine_partials_kernel.
+  int fuse_combine;
+  int* comb_cnt;
+  const int32_t* sorted_slot;  // slot at every sorted position
+  const int32_t* pos_of_slot;  // sorted position of every slot (-1: dropped)
+  const void* topk_w;
+  int w_dtype;
+  void* y;
+  int y_dtype;
+  int64_t hidden;
   const int32_t* expert_slot;  // tier << 24 | index inside the tier storage
   const int32_t* tile_info;
   const int32_t* n_tiles_ptr;
   int max_tiles;
-  const float* sorted_w;  // down: router weight of every sorted position
-  const __half* s8;       // INT8 per-row scales of this projection
-  int gate_up;            // 1: gate_up (rows interleave gate/up), 0: down
-  int n_rows;             // rows of the projection (2I or H)
   int inter;
-  int k;
-  int nblocks;
-  int weights_early;      // 1: the predecessor kernel writes only the activations (see below)
+  int weights_early;      // 1: the tile list is complete before this kernel starts (see below)
   // tiles_from_ids: build the tile list from the routing ids (below) instead of
   // reading tile_info, so the weight stream need not wait for the predecessor
   int tiles_from_ids;
@@ -107,8 +145,6 @@ struct TcParams {
   int ids_dtype, top_k, spt, n_routed, n_buckets;
   int64_t n_slots;
   int64_t n_pos;          // rows of the activation / mid buffers
-  void* out;
-  int64_t out_stride;
   uint32_t* status;
 };
 
@@ -126,29 +162,71 @@ __host__ __device__ __forceinline__ int b_stages_per_slot(int n) {
 
 // Everything a warp needs about a work item, computed once per CTA.
 struct Item {
-  int e, m0, mc, nb;      // expert, first sorted row, rows, 128-row block of the projection
+  int e, m0, mc, nb;      // expert, first sorted row, rows, row block of the projection
   int tier, idx, n, r0;   // tier, index in the tier storage, MMA N (mc rounded up to 16), first row
-  int sps, per_slot, pad0, pad1;  // k-stages per weight slot, per activation slot
+  int sps, per_slot, prj, tile;  // k-stages per weight slot, per activation slot; projection, tile
 };
 
 static_assert(sizeof(Item) == kItemBytes, "item table entry size");
 
-__device__ __forceinline__ Item make_item(const TcParams& p, int item, int n_tiles) {
-  Item it;
-  it.nb = item / n_tiles;
-  const int tile = item - it.nb * n_tiles;
-  it.e = __ldg(p.tile_info + 3 * tile);
-  it.m0 = __ldg(p.tile_info + 3 * tile + 1);
-  it.mc = __ldg(p.tile_info + 3 * tile + 2);
+__device__ __forceinline__ int num_items(const TcParams& p, int n_tiles) {
+  return (p.run_gu ? n_tiles * p.pj[0].nblocks : 0) + (p.run_dn ? n_tiles * p.pj[1].nblocks : 0);
+}
+
+// Projection, tile and row block of global item `item` (gate_up items first).
+__device__ __forceinline__ void item_coords(const TcParams& p, int item, int n_tiles, int& prj,
+                                            int& tile, int& nb) {
+  const int ngu = p.run_gu ? n_tiles * p.pj[0].nblocks : 0;
+  prj = (item < ngu) ? 0 : 1;
+  const int j = item - (prj ? ngu : 0);
+  const int nbk = p.pj[prj].nblocks;
+  tile = j / nbk;
+  nb = j - tile * nbk;
+}
+
+// The fields that follow from (expert, rows, projection, row block).
+__device__ __forceinline__ void finish_item(const TcParams& p, Item& it) {
   const int code = __ldg(p.expert_slot + it.e);
   it.tier = code >> 24;
   it.idx = code & 0xFFFFFF;
   it.n = max(16, (it.mc + 15) & ~15);
-  it.r0 = p.gate_up ? it.nb * 64 : it.nb * 128;
+  it.r0 = p.pj[it.prj].gate_up ? it.nb * 64 : it.nb * 128;
   it.sps = stages_per_slot(it.tier);
   it.per_slot = b_stages_per_slot(it.n);
-  it.pad0 = it.pad1 = 0;
+}
+
+__device__ __forceinline__ Item make_item(const TcParams& p, int item, int n_tiles) {
+  Item it;
+  item_coords(p, item, n_tiles, it.prj, it.tile, it.nb);
+  it.e = __ldcg(p.tile_info + 3 * it.tile);
+  it.m0 = __ldcg(p.tile_info + 3 * it.tile + 1);
+  it.mc = __ldcg(p.tile_info + 3 * it.tile + 2);
+  finish_item(p, it);
   return it;
+}
+
+// Bounded acquire-spin until *ctr >= target (one thread).  False on timeout
+// (about 2 s), after flagging the device status.
+__device__ __forceinline__ bool wait_count(const int* ctr, int target, uint32_t* status) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];\n" : "=r"(v) : "l"(ctr) : "memory");
+  if (v >= target) return true;
+  const long long t0 = clock64();
+  for (;;) {
+    __nanosleep(128);
+    asm volatile("ld.acquire.gpu.global.b32 %0, [%1];\n" : "=r"(v) : "l"(ctr) : "memory");
+    if (v >= target) return true;
+    if (clock64() - t0 > 4000000000LL) {
+      atomicOr(status, EXQ_DEV_TIMEOUT);
+      return false;
+    }
+  }
+}
+
+// Generic-proxy global writes/reads of this thread ordered against its
+// async-proxy (TMA) accesses.
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;\n" ::: "memory");
 }
 
 // The CTA's li-th work item (global index `item`): from the shared table for
@@ -339,6 +417,9 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
   auto B_empty = [&](int i) { return bar0 + 8u * (kBarB + kBStages + i); };
   auto Acc_full = [&](int i) { return bar0 + 8u * (kBarAcc + i); };
   auto Acc_empty = [&](int i) { return bar0 + 8u * (kBarAcc + 2 + i); };
+  constexpr int kBarCmb = kBarAcc + 4;
+  auto Cmb_full = [&](int i) { return bar0 + 8u * (kBarCmb + i); };
+  auto Cmb_empty = [&](int i) { return bar0 + 8u * (kBarCmb + kCmbRing + i); };
   volatile uint32_t* misc = reinterpret_cast<volatile uint32_t*>(gbase + kOffMisc);
   // misc[0] = TMEM base address, misc[1] = abort flag
 
@@ -361,14 +442,24 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
       mbar_init(Acc_full(i), 1);
       mbar_init(Acc_empty(i), kNumEpiWarps);
     }
+    for (int i = 0; i < kCmbRing; ++i) {
+      mbar_init(Cmb_full(i), kNumEpiWarps);
+      mbar_init(Cmb_empty(i), 1);
+    }
     misc[1] = 0;
     mbar_fence_init();
   }
   if (threadIdx.x == 32 * kWarpW) {  // tensor-map descriptors into the TMA unit's cache
-    for (int i = 0; i < 3; ++i) tma_prefetch_desc(&p.tm_w[i]);
-    tma_prefetch_desc(&p.tm_s);
+    for (int j = 0; j < 2; ++j) {
+      if (j == 0 ? !p.run_gu : !p.run_dn) continue;
+      for (int i = 0; i < 3; ++i) tma_prefetch_desc(&p.pj[j].tm_w[i]);
+      tma_prefetch_desc(&p.pj[j].tm_s);
+    }
   } else if (threadIdx.x == 32 * kWarpB) {
-    for (int i = 0; i < 4; ++i) tma_prefetch_desc(&p.tm_b[i]);
+    for (int j = 0; j < 2; ++j) {
+      if (j == 0 ? !p.run_gu : !p.run_dn) continue;
+      for (int i = 0; i < 4; ++i) tma_prefetch_desc(&p.pj[j].tm_b[i]);
+    }
   }
   if (warp == kWarpMma) {
     tmem_alloc(base + kOffMisc, kTmemCols);
@@ -440,42 +531,35 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
     }
     __syncthreads();
     n_tiles = min(tstart[nbk], p.max_tiles);
-    const int n_items0 = n_tiles * p.nblocks;
+    const int n_items0 = num_items(p, n_tiles);
     for (int t = threadIdx.x; t < kItemTab; t += kThreads) {
       const int item = static_cast<int>(blockIdx.x) + t * static_cast<int>(gridDim.x);
       if (item >= n_items0) continue;
-      const int tile = item % n_tiles;
+      Item it;
+      item_coords(p, item, n_tiles, it.prj, it.tile, it.nb);
       int lo = 0, hi = nbk - 1;  // last expert whose first tile is <= tile
       while (lo < hi) {
         const int mid = (lo + hi + 1) >> 1;
-        if (tstart[mid] <= tile) lo = mid;
+        if (tstart[mid] <= it.tile) lo = mid;
         else hi = mid - 1;
       }
-      const int lt = tile - tstart[lo];
-      Item it;
-      it.nb = item / n_tiles;
+      const int lt = it.tile - tstart[lo];
       it.e = lo;
       it.m0 = rbase[lo] + lt * kMaxN;
       it.mc = min(kMaxN, cnt[lo] - lt * kMaxN);
-      const int code = __ldg(p.expert_slot + lo);
-      it.tier = code >> 24;
-      it.idx = code & 0xFFFFFF;
-      it.n = max(16, (it.mc + 15) & ~15);
-      it.r0 = p.gate_up ? it.nb * 64 : it.nb * 128;
-      it.sps = stages_per_slot(it.tier);
-      it.per_slot = b_stages_per_slot(it.n);
-      it.pad0 = it.pad1 = 0;
+      finish_item(p, it);
       items_tab[t] = it;
     }
   } else {
-    n_tiles = min(*p.n_tiles_ptr, p.max_tiles);
+    n_tiles = min(__ldcg(p.n_tiles_ptr), p.max_tiles);
     // decode this CTA's items once, so no role waits on global loads at an item boundary
+    const int n_items0 = num_items(p, n_tiles);
     for (int t = threadIdx.x; t < kItemTab; t += kThreads) {
       const int item = static_cast<int>(blockIdx.x) + t * static_cast<int>(gridDim.x);
-      if (item < n_tiles * p.nblocks) items_tab[t] = make_item(p, item, n_tiles);
+      if (item < n_items0) items_tab[t] = make_item(p, item, n_tiles);
     }
   }
-  const int n_items = n_tiles * p.nblocks;
+  const int n_items = num_items(p, n_tiles);
   __syncthreads();
   auto aborted = [&]() { return misc[1] != 0; };
   auto do_abort = [&]() { misc[1] = 1; };
@@ -486,14 +570,15 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
     // issues, which keeps the issue path on the warp-uniform datapath.
     Ring r;
     int issued = 0;
-    const int G = p.k >> 7;
     for (int item = blockIdx.x, li = 0; item < n_items && !aborted(); item += gridDim.x, ++li) {
       Item it;
       if (!decode_item(p, items_tab, li, item, n_tiles, it)) {
         if (lane == 0) atomicOr(p.status, EXQ_DEV_BAD_TIER);
         continue;
       }
-      const int nk = p.k / kKS;
+      const ProjParams& pj = p.pj[it.prj];
+      const int G = pj.k >> 7;
+      const int nk = pj.k / kKS;
       const int sps = it.sps;
       bool ok = true;
       for (int kc0 = 0; kc0 < nk; kc0 += sps) {
@@ -506,21 +591,21 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
         if (elect_one()) {
           if (it.tier == kTierINT4) {
             mbar_arrive_tx(bar, kWSlot + kSSlot);
-            if (p.gate_up) {
+            if (pj.gate_up) {
               // weights: (byte, row in block, block, gate/up, expert)
-              tma_load_5d(dst, &p.tm_w[kTierINT4], bar, xb, 0, it.nb, 0, it.idx);
+              tma_load_5d(dst, &pj.tm_w[kTierINT4], bar, xb, 0, it.nb, 0, it.idx);
               // scales: (element in block, block, gate/up, group, expert); 2 groups
-              tma_load_5d(sS + r.idx * kSSlot, &p.tm_s, bar, 0, it.nb, 0, kc0 >> 1, it.idx);
+              tma_load_5d(sS + r.idx * kSSlot, &pj.tm_s, bar, 0, it.nb, 0, kc0 >> 1, it.idx);
             } else {
-              tma_load_2d(dst, &p.tm_w[kTierINT4], bar, xb, it.idx * p.n_rows + it.r0);
-              tma_load_2d(sS + r.idx * kSSlot, &p.tm_s, bar, it.r0, it.idx * G + (kc0 >> 1));
+              tma_load_2d(dst, &pj.tm_w[kTierINT4], bar, xb, it.idx * pj.n_rows + it.r0);
+              tma_load_2d(sS + r.idx * kSSlot, &pj.tm_s, bar, it.r0, it.idx * G + (kc0 >> 1));
             }
           } else {
             mbar_arrive_tx(bar, kWSlot);
-            if (p.gate_up)
-              tma_load_5d(dst, &p.tm_w[it.tier], bar, xb, 0, it.nb, 0, it.idx);
+            if (pj.gate_up)
+              tma_load_5d(dst, &pj.tm_w[it.tier], bar, xb, 0, it.nb, 0, it.idx);
             else
-              tma_load_2d(dst, &p.tm_w[it.tier], bar, xb, it.idx * p.n_rows + it.r0);
+              tma_load_2d(dst, &pj.tm_w[it.tier], bar, xb, it.idx * pj.n_rows + it.r0);
           }
         }
         __syncwarp();
@@ -548,9 +633,26 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
     for (int item = blockIdx.x, li = 0; item < n_items && !aborted(); item += gridDim.x, ++li) {
       Item it;
       if (!decode_item(p, items_tab, li, item, n_tiles, it)) continue;
-      const int nk = p.k / kKS;
+      const ProjParams& pj = p.pj[it.prj];
+      const int nk = pj.k / kKS;
       const int per_slot = it.per_slot;
       const uint32_t stage_bytes = static_cast<uint32_t>(it.n) * 128u;
+      if (p.link && it.prj == 1) {
+        // the tile's mid rows come from nb_gu gate_up items of this launch
+        bool ok = true;
+        if (lane == 0) ok = wait_count(p.tile_done + it.tile, p.pj[0].nblocks, p.status);
+        if (!__shfl_sync(0xffffffffu, ok, 0)) {
+          do_abort();
+          break;
+        }
+        // every lane acquires (the TMA issuer is elected below), then orders
+        // its TMA reads of mid after the acquire
+        int seen;
+        asm volatile("ld.acquire.gpu.global.b32 %0, [%1];\n"
+                     : "=r"(seen) : "l"(p.tile_done + it.tile) : "memory");
+        (void)seen;
+        fence_proxy_async_global();
+      }
       bool ok = true;
       for (int kc0 = 0; kc0 < nk; kc0 += per_slot) {
         if (!__all_sync(0xffffffffu, mbar_wait(B_empty(r.idx), r.phase ^ 1, p.status))) {
@@ -561,7 +663,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
         if (elect_one()) {
           // the whole slot in one box: n rows x per_slot stages (stages past k read as zeros)
           mbar_arrive_tx(bar, static_cast<uint32_t>(per_slot) * stage_bytes);
-          tma_load_3d(sB + r.idx * kBSlot, &p.tm_b[(it.n >> 4) - 1], bar, 0, it.m0, kc0);
+          tma_load_3d(sB + r.idx * kBSlot, &pj.tm_b[(it.n >> 4) - 1], bar, 0, it.m0, kc0);
         }
         __syncwarp();
         r.next(kBStages);
@@ -601,7 +703,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
       MmaItem mi;
       mi.d = tmem + ab * kMaxN;
       mi.idesc = idesc_f16_m128(it.n);
-      mi.nk = p.k / kKS;
+      mi.nk = p.pj[it.prj].k / kKS;
       mi.per_slot = it.per_slot;
       mi.stage_desc = static_cast<uint32_t>(it.n) * 8u;  // n rows x 128 B, in 16 B units
       mi.bdesc0 = bdesc0;
@@ -637,33 +739,38 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
     // ---------------------------------------------------------- epilogue
     const int quarter = warp & 3;  // TMEM lanes 32*quarter .. +31
     const int row = 32 * quarter + lane;
-    int count = 0;
-    for (int item = blockIdx.x, li = 0; item < n_items && !aborted(); item += gridDim.x, ++li, ++count) {
+    const int et = static_cast<int>(threadIdx.x) - 32 * kEpiWarp0;  // 0..127
+    int count = 0, dcount = 0;
+    // The four warps take every decision together (the named barriers below
+    // need all 128 threads): the loop bound and the abort test are agreed at
+    // the barrier after each accumulator wait.
+    for (int item = blockIdx.x, li = 0; item < n_items; item += gridDim.x, ++li, ++count) {
       Item it;
       if (!decode_item(p, items_tab, li, item, n_tiles, it)) {
         --count;
         continue;
       }
+      const ProjParams& pj = p.pj[it.prj];
       const int ab = count & 1;
       const uint32_t acc_phase = (count >> 1) & 1;
-      const bool got = mbar_wait(Acc_full(ab), acc_phase, p.status);
-      if (!__all_sync(0xffffffffu, got)) {  // keep the warp converged
+      const bool got = !aborted() && mbar_wait(Acc_full(ab), acc_phase, p.status);
+      if (named_barrier_or(kEpiBar, 128, !got)) {
         do_abort();
         break;
       }
       tc_fence_after();
       const uint32_t taddr = tmem + (static_cast<uint32_t>(32 * quarter) << 16) + ab * kMaxN;
-      if (p.gate_up) {
+      if (pj.gate_up) {
         // rows in blocks of 8: gate rows have bit 3 clear, the matching up row is row ^ 8
         const int g = it.r0 + ((row >> 4) << 3) + (row & 7);
         const bool is_up = (row & 8) != 0;
         float sg = 1.f, su = 1.f;
         if (it.tier == kTierINT8) {
-          const int64_t rb = static_cast<int64_t>(it.idx) * p.n_rows;
-          sg = __half2float(p.s8[rb + g]);
-          su = __half2float(p.s8[rb + p.inter + g]);
+          const int64_t rb = static_cast<int64_t>(it.idx) * pj.n_rows;
+          sg = __half2float(pj.s8[rb + g]);
+          su = __half2float(pj.s8[rb + p.inter + g]);
         }
-        __half* mid = static_cast<__half*>(p.out);
+        __half* mid = static_cast<__half*>(pj.out);
         const int col = perm_pos(g);
         // mid is stage-major [I/64][n_pos][64]: column col of row m0 + tok
         __half* mrow = mid + static_cast<int64_t>(col >> 6) * p.n_pos * 64 + (col & 63) +
@@ -688,10 +795,10 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
         }
       } else {
         const int h = it.r0 + row;
-        float* prow = static_cast<float*>(p.out) + static_cast<int64_t>(it.m0) * p.out_stride + h;
+        float* prow = static_cast<float*>(pj.out) + static_cast<int64_t>(it.m0) * pj.out_stride + h;
         // the router weights are applied by the combine; INT8 rows carry a scale
         const float s = it.tier == kTierINT8
-                            ? __half2float(p.s8[static_cast<int64_t>(it.idx) * p.n_rows + h])
+                            ? __half2float(pj.s8[static_cast<int64_t>(it.idx) * pj.n_rows + h])
                             : 1.f;
         for (int c = 0; c < it.n; c += 16) {
           uint32_t v[16];
@@ -700,13 +807,149 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
             const int tok = c + i;
-            if (tok < it.mc) prow[static_cast<int64_t>(tok) * p.out_stride] = __uint_as_float(v[i]) * s;
+            if (tok < it.mc) prow[static_cast<int64_t>(tok) * pj.out_stride] = __uint_as_float(v[i]) * s;
           }
         }
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(Acc_empty(ab));
+      if (pj.gate_up && p.link) {
+        // this row block of the tile's mid rows is stored: count it for the
+        // down items of the tile (their TMA loads read mid)
+        fence_proxy_async_global();
+        named_barrier(kEpiBar, 128);
+        if (et == 0) {
+          __threadfence();
+          atomicAdd(p.tile_done + it.tile, 1);
+        }
+      } else if (!pj.gate_up && p.fuse_combine) {
+        // hand the item to the combine warp once its partial rows are stored
+        const uint32_t ci = dcount % kCmbRing, ph = (dcount / kCmbRing) & 1;
+        ++dcount;
+        const bool free_slot = mbar_wait(Cmb_empty(ci), ph ^ 1, p.status);
+        if (!__all_sync(0xffffffffu, free_slot)) do_abort();  // agreed at the next item's barrier
+        __syncwarp();
+        if (lane == 0) mbar_arrive(Cmb_full(ci));
+      }
+    }
+  } else if (warp == kWarpCmb) {
+    // ---------------------------------------------------------- fused top-k combine
+    // For every down item, once the epilogue has stored its rows' fp32
+    // partials: one arrival per row on the (token, 128-column block) counter;
+    // a row whose arrival completes its token's valid slots makes this warp
+    // sum the token's partials in slot order (the other items' rows come from
+    // L2) and write y for the block.  The sums run off the GEMM pipeline: the
+    // epilogue only waits for a free entry of the kCmbRing-deep hand-off.
+    if (p.fuse_combine) {
+      pdl_wait();  // pos_of_slot / sorted_slot come from the routing kernel
+      // a token none of whose slots has an expert gets no arrival: zero row
+      const int64_t n_tok = p.n_slots / p.spt;
+      for (int64_t t = static_cast<int64_t>(blockIdx.x) * 32 + lane; t < n_tok;
+           t += static_cast<int64_t>(gridDim.x) * 32) {
+        int need = 0;
+        for (int j = 0; j < p.spt; ++j) need += __ldcg(p.pos_of_slot + t * p.spt + j) >= 0;
+        if (need == 0) {
+          uint4* yrow = reinterpret_cast<uint4*>(static_cast<__half*>(p.y) + t * p.hidden);
+          for (int64_t c = 0; c < p.hidden / 8; ++c) yrow[c] = make_uint4(0, 0, 0, 0);
+        }
+      }
+      int* spos = reinterpret_cast<int*>(gbase + kOffCmb);     // [kMaxN][kCmbMaxSpt]
+      float* sw = reinterpret_cast<float*>(spos + kMaxN * kCmbMaxSpt);
+      const int nhb = static_cast<int>(p.hidden >> 7);
+      const int spt = p.spt;
+      int dc = 0;
+      for (int item = blockIdx.x, li = 0; item < n_items; item += gridDim.x, ++li) {
+        Item it;
+        if (!decode_item(p, items_tab, li, item, n_tiles, it) || it.prj != 1) continue;
+        const uint32_t ci = dc % kCmbRing, ph = (dc / kCmbRing) & 1;
+        ++dc;
+        // rows lane and lane + 32: token, valid slots, positions and weights
+        // (loaded before the wait; the routing kernel wrote them)
+        int tok[2], need[2] = {0, 0};
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int c = lane + 32 * h;
+          tok[h] = -1;
+          if (c < it.mc) {
+            tok[h] = __ldcg(p.sorted_slot + it.m0 + c) / spt;
+            for (int j = 0; j < spt; ++j) {
+              const int r = __ldcg(p.pos_of_slot + tok[h] * spt + j);
+              need[h] += r >= 0;
+              spos[c * kCmbMaxSpt + j] = r;
+              sw[c * kCmbMaxSpt + j] =
+                  j < p.top_k ? load_as_f32(p.topk_w, p.w_dtype,
+                                            static_cast<int64_t>(tok[h]) * p.top_k + j)
+                              : 1.0f;
+            }
+          }
+        }
+        const bool got = !aborted() && mbar_wait(Cmb_full(ci), ph, p.status);
+        if (!__all_sync(0xffffffffu, got)) {
+          do_abort();
+          break;
+        }
+        // the epilogue's partial stores (ordered before its arrivals) become
+        // visible device-wide before this warp's counter arrivals
+        __threadfence();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(Cmb_empty(ci));
+        bool fin[2];
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          fin[h] = false;
+          if (tok[h] >= 0) {
+            const int old = atomicAdd(p.comb_cnt + tok[h] * nhb + it.nb, 1);
+            fin[h] = old + 1 == need[h];
+          }
+        }
+        uint64_t mask = static_cast<uint64_t>(__ballot_sync(0xffffffffu, fin[0])) |
+                        (static_cast<uint64_t>(__ballot_sync(0xffffffffu, fin[1])) << 32);
+        if (!mask) continue;
+        __threadfence();  // acquire the other items' partial rows of these tokens
+        // lane: 4 consecutive columns of the 128-column block
+        const int col = it.r0 + 4 * lane;
+        const float* part = static_cast<const float*>(p.pj[1].out);
+        const int64_t stride = p.pj[1].out_stride;
+        while (mask) {
+          const int c = __ffsll(static_cast<long long>(mask)) - 1;
+          mask &= mask - 1;
+          const int t = __shfl_sync(0xffffffffu, c < 32 ? tok[0] : tok[1], c & 31);
+          float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+          // the sum of combine_partials_kernel: slot order, product and sum
+          // rounded separately, padded to a multiple of 8 slots with 0 * 0
+          for (int j0 = 0; j0 < spt; j0 += 8) {
+            float4 v[8];
+            float wj[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+              const int j = j0 + u;
+              const int r = j < spt ? spos[c * kCmbMaxSpt + j] : -1;
+              wj[u] = j < spt ? sw[c * kCmbMaxSpt + j] : 0.f;
+              v[u] = r >= 0 ? __ldcg(reinterpret_cast<const float4*>(part + r * stride + col))
+                            : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+              acc.x = __fadd_rn(acc.x, __fmul_rn(wj[u], v[u].x));
+              acc.y = __fadd_rn(acc.y, __fmul_rn(wj[u], v[u].y));
+              acc.z = __fadd_rn(acc.z, __fmul_rn(wj[u], v[u].z));
+              acc.w = __fadd_rn(acc.w, __fmul_rn(wj[u], v[u].w));
+            }
+          }
+          const int64_t yo = static_cast<int64_t>(t) * p.hidden + col;
+          uint2 packed;
+          if (p.y_dtype == EXQ_F16) {
+            __half2 lo = __floats2half2_rn(acc.x, acc.y), hi = __floats2half2_rn(acc.z, acc.w);
+            packed = make_uint2(*reinterpret_cast<uint32_t*>(&lo), *reinterpret_cast<uint32_t*>(&hi));
+          } else {
+            __nv_bfloat162 lo = __floats2bfloat162_rn(acc.x, acc.y),
+                           hi = __floats2bfloat162_rn(acc.z, acc.w);
+            packed = make_uint2(*reinterpret_cast<uint32_t*>(&lo), *reinterpret_cast<uint32_t*>(&hi));
+          }
+          *reinterpret_cast<uint2*>(static_cast<__half*>(p.y) + yo) = packed;
+        }
+      }
     }
   } else {
     // ---------------------------------------------------------- dequant
@@ -722,10 +965,10 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
     for (int item = blockIdx.x, li = 0; item < n_items && !aborted(); item += gridDim.x, ++li) {
       Item it;
       if (!decode_item(p, items_tab, li, item, n_tiles, it)) continue;
-      const int nk = p.k / kKS;
+      const int nk = p.pj[it.prj].k / kKS;
       const int sps = it.sps;
       // gate_up interleaves gate/up rows in blocks of 8 (the epilogue pairs lanes m, m^8)
-      const int lw = p.gate_up ? (((m >> 4) << 3) + (m & 7) + ((m & 8) ? 64 : 0)) : m;
+      const int lw = p.pj[it.prj].gate_up ? (((m >> 4) << 3) + (m & 7) + ((m & 8) ? 64 : 0)) : m;
       const int swz = lw & 7;
       bool ok = true;
       for (int kc0 = 0; kc0 < nk; kc0 += sps, ++gs) {
@@ -915,7 +1158,7 @@ static bool make_map_nd(CUtensorMap* m, CUtensorMapDataType dt, const void* ptr,
 
 // Fill the per-projection maps.  proj 0 = w13 (rows 2I, k = H), 1 = w2 (rows H, k = I).
 static int build_maps(const exq_moe_weights* w, int proj, const void* act, int64_t n_pos,
-                      TcParams& p) {
+                      ProjParams& p) {
   const int64_t I = w->inter, H = w->hidden;
   const int64_t rows = proj == 0 ? 2 * I : H;
   const int64_t k = proj == 0 ? H : I;
@@ -1057,14 +1300,18 @@ struct TcWs {
   int32_t* ends;
   int32_t* tile_info;
   int32_t* n_tiles;
+  int32_t* tile_done;  // [max_tiles] gate_up row blocks stored per tile
+  int32_t* comb_cnt;   // [n_tokens * hidden/128] fused-combine arrivals
   __half* act;
   __half* mid;
   float* partial;
   int64_t max_tiles;
+  int64_t n_counters;  // ints in tile_done + comb_cnt (one contiguous run)
   size_t bytes;
 };
 
-TcWs carve_tc(void* base, int64_t n_slots, int n_buckets, int64_t hidden, int64_t inter) {
+TcWs carve_tc(void* base, int64_t n_slots, int64_t n_tokens, int n_buckets, int64_t hidden,
+              int64_t inter) {
   TcWs w{};
   size_t off = 0;
   auto take = [&](size_t bytes) {
@@ -1079,6 +1326,9 @@ TcWs carve_tc(void* base, int64_t n_slots, int n_buckets, int64_t hidden, int64_
   w.ends = reinterpret_cast<int32_t*>(take(4 * (n_buckets + 1)));
   w.tile_info = reinterpret_cast<int32_t*>(take(12 * w.max_tiles));
   w.n_tiles = reinterpret_cast<int32_t*>(take(16));
+  w.n_counters = w.max_tiles + n_tokens * (hidden / 128);
+  w.tile_done = reinterpret_cast<int32_t*>(take(4 * w.n_counters));
+  w.comb_cnt = w.tile_done ? w.tile_done + w.max_tiles : nullptr;
   w.act = reinterpret_cast<__half*>(take(2 * n_slots * hidden));
   w.mid = reinterpret_cast<__half*>(take(2 * n_slots * inter));
   w.partial = reinterpret_cast<float*>(take(4 * n_slots * hidden));
@@ -1090,9 +1340,10 @@ bool is_act(int d) { return d == EXQ_F16 || d == EXQ_BF16; }
 
 }  // namespace
 
-void exq::layer_partials(void* workspace, int64_t n_slots, int n_buckets, int64_t hidden,
-                         int64_t inter, const float** partial, const int32_t** pos_of_slot) {
-  const TcWs ws = carve_tc(workspace, n_slots, n_buckets, hidden, inter);
+void exq::layer_partials(void* workspace, int64_t n_slots, int64_t n_tokens, int n_buckets,
+                         int64_t hidden, int64_t inter, const float** partial,
+                         const int32_t** pos_of_slot) {
+  const TcWs ws = carve_tc(workspace, n_slots, n_tokens, n_buckets, hidden, inter);
   *partial = ws.partial;
   *pos_of_slot = ws.pos_of_slot;
 }
@@ -1101,7 +1352,8 @@ extern "C" size_t exq_moe_layer_workspace_bytes(int64_t n_tokens, int32_t top_k,
                                                 int32_t n_experts_total, int64_t hidden,
                                                 int64_t inter) {
   if (n_tokens < 0 || top_k <= 0 || n_shared < 0 || n_experts_total <= 0) return 0;
-  return carve_tc(nullptr, n_tokens * (top_k + n_shared), n_experts_total, hidden, inter).bytes;
+  return carve_tc(nullptr, n_tokens * (top_k + n_shared), n_tokens, n_experts_total, hidden, inter)
+      .bytes;
 }
 
 extern "C" int exq_moe_layer_forward(const exq_moe_weights* weights, const void* hidden_states,
@@ -1161,7 +1413,7 @@ extern "C" int exq_moe_layer_forward_range(const exq_moe_weights* w, const void*
   EXQ_CHECK_ARG(reinterpret_cast<uintptr_t>(hidden_states) % 16 == 0,
                 "moe_layer: hidden_states must be 16-byte aligned");
   auto s = static_cast<cudaStream_t>(stream);
-  TcWs ws = carve_tc(workspace, n_slots, n_total, H, I);
+  TcWs ws = carve_tc(workspace, n_slots, n_tokens, n_total, H, I);
   uint32_t* status = device_status_ptr();
   if (!status) return EXQ_ERR_CUDA;
   int st = EXQ_OK;
@@ -1169,6 +1421,12 @@ extern "C" int exq_moe_layer_forward_range(const exq_moe_weights* w, const void*
   // a kernel of this call: the first launch may follow a copy or an event wait.
   bool chained = false;
 
+  // gate_up and down run as one launch when both are asked for; with the
+  // combine too, the down items sum each token's slots (no separate combine)
+  const bool do_gu = first_stage <= 2 && end_stage > 2;
+  const bool do_dn = first_stage <= 3 && end_stage > 3;
+  const bool fuse_combine =
+      do_dn && first_stage <= 4 && end_stage > 4 && spt <= tc::kCmbMaxSpt;
   // decode-sized calls route and gather in one kernel (stage 0; stage 1 is empty)
   const bool fused = n_slots <= kRouteGatherMaxSlots && n_total <= kRouteGatherMaxBuckets;
   if (fused && first_stage <= 0 && end_stage > 0) {
@@ -1193,6 +1451,9 @@ extern "C" int exq_moe_layer_forward_range(const exq_moe_weights* w, const void*
     rg.tile_info = ws.tile_info;
     rg.n_tiles = ws.n_tiles;
     rg.max_tiles = ws.max_tiles;
+    rg.sorted_slot = ws.sorted_slot;
+    rg.counters = ws.tile_done;
+    rg.n_counters = ws.n_counters;
     st = launch_route_gather(rg, s, chained);
     if (st != EXQ_OK) return st;
     chained = true;
@@ -1216,6 +1477,8 @@ extern "C" int exq_moe_layer_forward_range(const exq_moe_weights* w, const void*
     rp.tile_info = ws.tile_info;
     rp.n_tiles = ws.n_tiles;
     rp.max_tiles = ws.max_tiles;
+    rp.counters = ws.tile_done;
+    rp.n_counters = ws.n_counters;
     st = launch_route(rp, kRouteLayer, s, chained);
     if (st != EXQ_OK) return st;
     chained = true;
@@ -1226,46 +1489,56 @@ extern "C" int exq_moe_layer_forward_range(const exq_moe_weights* w, const void*
     if (st != EXQ_OK) return st;
     chained = true;
   }
-  bool gate_up_from_ids = false;  // gate_up of this call let down launch at once
-  for (int proj = 0; proj < 2; ++proj) {
-    const int stage = 2 + proj;
-    if (!(first_stage <= stage && end_stage > stage)) continue;
+  if (do_gu || do_dn) {
     tc::TcParams p;
     memset(&p, 0, sizeof(p));
-    st = tc::build_maps(w, proj, proj == 0 ? ws.act : ws.mid, n_slots, p);
-    if (st != EXQ_OK) return st;
+    for (int proj = 0; proj < 2; ++proj) {
+      if (!(proj == 0 ? do_gu : do_dn)) continue;
+      tc::ProjParams& pj = p.pj[proj];
+      st = tc::build_maps(w, proj, proj == 0 ? ws.act : ws.mid, n_slots, pj);
+      if (st != EXQ_OK) return st;
+      pj.gate_up = proj == 0;
+      pj.nblocks = static_cast<int>(proj == 0 ? I / 64 : H / 128);
+      pj.out = proj == 0 ? static_cast<void*>(ws.mid) : static_cast<void*>(ws.partial);
+      pj.out_stride = proj == 0 ? I : H;
+    }
+    p.run_gu = do_gu;
+    p.run_dn = do_dn;
+    p.link = do_gu && do_dn;
+    p.tile_done = ws.tile_done;
+    p.fuse_combine = fuse_combine;
+    p.comb_cnt = ws.comb_cnt;
+    p.sorted_slot = ws.sorted_slot;
+    p.pos_of_slot = ws.pos_of_slot;
+    p.topk_w = topk_weights;
+    p.w_dtype = w_dtype;
+    p.y = out;
+    p.y_dtype = act_dtype;
+    p.hidden = H;
     p.expert_slot = w->expert_slot;
     p.tile_info = ws.tile_info;
     p.n_tiles_ptr = ws.n_tiles;
     p.max_tiles = static_cast<int>(ws.max_tiles);
-    p.sorted_w = ws.sorted_w;
-    p.gate_up = proj == 0;
     p.inter = static_cast<int>(I);
-    p.nblocks = static_cast<int>(proj == 0 ? I / 64 : H / 128);
-    p.out = proj == 0 ? static_cast<void*>(ws.mid) : static_cast<void*>(ws.partial);
-    p.out_stride = proj == 0 ? I : H;
     p.n_pos = n_slots;
     p.status = status;
-    const int64_t max_items = ws.max_tiles * p.nblocks;
+    const int64_t per_tile = (do_gu ? I / 64 : 0) + (do_dn ? H / 128 : 0);
+    const int64_t max_items = ws.max_tiles * per_tile;
     const int64_t grid = max_items < num_sms() ? max_items : num_sms();
     // a CTA can build its items from the ids: the experts fit the histogram and
     // every CTA's items fit its shared table
     const bool ids_ok = n_total <= tc::kHistBuckets &&
                         max_items <= static_cast<int64_t>(tc::kItemTab) * (grid > 0 ? grid : 1);
-    if (proj == 0) {
-      // right after the fused routing of this call: build the tiles from the ids
-      // (complete before routing started) and stream weights at once, letting
-      // down launch before the routing kernel has finished
-      p.tiles_from_ids = fused && first_stage == 0 && ids_ok;
-      gate_up_from_ids = p.tiles_from_ids;
-    } else if (gate_up_from_ids) {
-      // the routing kernel's tile list may still be being written: build the
-      // tiles from the ids as gate_up did, or read the list after waiting
+    if (fused && first_stage == 0) {
+      // right after the fused routing of this call: build the tiles from the
+      // ids (complete before routing started) and stream weights at once;
+      // otherwise wait for the routing kernel before reading its tile list
       p.tiles_from_ids = ids_ok;
     } else {
-      // gate_up of this call waited for the routing before letting down launch,
-      // so the tile list is complete: stream weights at once
-      p.weights_early = first_stage <= 2;
+      // the tile list was complete before this launch could start: written by
+      // the route kernel two launches back (route -> prep -> here) or by an
+      // earlier call
+      p.weights_early = 1;
     }
     p.ids = topk_ids;
     p.ids_dtype = ids_dtype;
@@ -1279,7 +1552,7 @@ extern "C" int exq_moe_layer_forward_range(const exq_moe_weights* w, const void*
     if (st != EXQ_OK) return st;
     chained = true;
   }
-  if (first_stage <= 4 && end_stage > 4)
+  if (first_stage <= 4 && end_stage > 4 && !fuse_combine)
     return launch_combine_partials(ws.partial, H, ws.pos_of_slot, topk_weights, w_dtype, top_k,
                                    n_tokens, spt, out, act_dtype, s, chained);
   return EXQ_OK;

@@ -186,6 +186,8 @@ __global__ void __launch_bounds__(kRouteThreads, 1) route_kernel(RouteParams p, 
     }
   }
   if (mode == kRouteLayer) {
+    // the GEMM's tile and combine counters start at zero
+    for (int64_t i = threadIdx.x; i < p.n_counters; i += kRouteThreads) p.counters[i] = 0;
     // positions past the routed total (slots dropped for a bad expert id) hold -1
     for (int64_t i = carry + threadIdx.x; i < p.n; i += kRouteThreads) {
       p.sorted_i32[i] = -1;

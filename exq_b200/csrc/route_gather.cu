@@ -205,8 +205,15 @@ __global__ void __launch_bounds__(kRgThreads) route_gather_kernel(const RouteGat
   for (int i = s0 + threadIdx.x; i < s1; i += kRgThreads) {
     const int pos = slot_pos[i - s0];
     p.pos_of_slot[i] = pos;
-    if (pos >= 0) p.sorted_w[pos] = wslot[i];
+    if (pos >= 0) {
+      p.sorted_w[pos] = wslot[i];
+      if (p.sorted_slot) p.sorted_slot[pos] = i;
+    }
   }
+  // the GEMM's tile and combine counters start at zero
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * kRgThreads + threadIdx.x; i < p.n_counters;
+       i += static_cast<int64_t>(gridDim.x) * kRgThreads)
+    p.counters[i] = 0;
   // row copies, slot by slot: each thread issues 8 independent 16-byte loads
   // before storing
   const int octs = static_cast<int>(p.hidden_size / 8);

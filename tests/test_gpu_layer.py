@@ -282,3 +282,69 @@ def test_sglang_forward_with_mock_layer(cuda):
     assert OM.rel_l2(out.hidden_states, ref) < TOL
     layer2 = types.SimpleNamespace(w13_weight=w13, w2_weight=w2, layer_id=3)
     assert B._exq_forward_cuda(None, layer2, disp, lambda *a: "fallthrough", 1) == "fallthrough"
+
+
+def _stage_runs(bank, x, ids, w):
+    """The same call as one fused launch chain and as separately launched
+    stages: (all stages, gate_up+down with the separate combine, every stage
+    alone)."""
+    fused = bank(x, ids, w)
+    y_sep = torch.empty_like(fused)
+    bank.forward_range(x, ids, w, 0, 4, out=y_sep)
+    bank.forward_range(x, ids, w, 4, 5, out=y_sep)
+    y_alone = torch.empty_like(fused)
+    for s in range(5):
+        bank.forward_range(x, ids, w, s, s + 1, out=y_alone)
+    torch.cuda.synchronize()
+    return fused, y_sep, y_alone
+
+
+@pytest.mark.parametrize("cfg,t,tiers", [("qwen3", 1, None), ("qwen3", 8, None),
+                                         ("qwen3", 256, None), ("dsv2_lite", 64, None),
+                                         ("olmoe_mixed", 64, "mixed"), ("qwen3", 600, None)])
+def test_fused_combine_bit_identical_to_separate_combine(cuda, cfg, t, tiers):
+    """The top-k combine fused into the down items (a token's last arriving row
+    block sums its slots in slot order) gives the same bits as the separate
+    combine kernel, and gate_up + down in one launch the same bits as two."""
+    from exq_b200.synth import CONFIGS, hidden_states, tier_plan, zipf_router
+    c0 = CONFIGS[cfg]
+    tl = tier_plan(c0.n_experts, seed=0) if tiers else None
+    bank, c = _bank(cfg, cuda, tiers=tl)
+    ids, w = zipf_router(t, c.n_experts, c.top_k, seed=70 + t)
+    x = hidden_states(t, c.hidden, seed=70 + t, dtype=c.act_dtype).to(cuda)
+    fused, y_sep, y_alone = _stage_runs(bank, x, ids.to(cuda), w.to(cuda))
+    assert torch.equal(fused, y_sep)
+    assert torch.equal(fused, y_alone)
+
+
+def test_fused_combine_tokens_without_experts(cuda):
+    """Tokens whose slots are all padding (-1) or all dropped (id past the
+    experts) get a zero row; the other tokens match the oracle."""
+    from exq_b200 import _lib as L
+    from exq_b200.synth import hidden_states, zipf_router
+    bank, c = _bank("qwen3", cuda, n_experts=16)
+    ids, w = zipf_router(12, 16, 8, seed=9)
+    x = hidden_states(12, c.hidden, seed=9)
+    ids[3] = -1
+    ids[7] = 99
+    L.read_device_status(cuda, clear=True)
+    y = bank(x.to(cuda), ids.to(cuda), w.to(cuda)).cpu()
+    assert L.read_device_status(cuda, clear=True) & L.DEV_BAD_EXPERT_ID
+    assert torch.count_nonzero(y[3]) == 0 and torch.count_nonzero(y[7]) == 0
+    keep = torch.tensor([i for i in range(12) if i not in (3, 7)])
+    ref = oracle_layer(bank, x, ids, w, tokens=keep)
+    assert OM.rel_l2(y[keep], ref) < TOL
+    _, y_sep, _ = _stage_runs(bank, x.to(cuda), ids.to(cuda), w.to(cuda))
+    assert torch.equal(y, y_sep.cpu())
+
+
+@pytest.mark.parametrize("t", [32, 128])
+def test_layer_qwen3_decode_sizes_in_full(cuda, t):
+    """BASELINE config 2 at T=32 and T=128: every token against the oracle."""
+    from exq_b200.synth import hidden_states, zipf_router
+    bank, c = _bank("qwen3", cuda)
+    ids, w = zipf_router(t, c.n_experts, c.top_k, seed=t + 1)
+    x = hidden_states(t, c.hidden, seed=t + 1)
+    y = bank(x.to(cuda), ids.to(cuda), w.to(cuda))
+    ref = oracle_layer(bank, x, ids, w)
+    assert OM.rel_l2(y, ref) < TOL
