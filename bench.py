@@ -41,6 +41,13 @@ WORKLOAD = ("Qwen3-30B-A3B MoE layer (E128 top-8 H2048 I768), INT4 g128 w4a16, f
             "Zipf(1.1) routing, decode T=256; 8 rotating layers (2.5 GB of weights > L2)")
 
 
+def bench_config(world):
+    """The workload description, identical in both arms (no measured values)."""
+    return {"workload": WORKLOAD, "tokens": CFG["tokens"], "n_layers_rotated": N_LAYERS,
+            "l2": "inputs larger than L2 (8 layers x 311 MB rotated)",
+            "parallelism": f"replicas x{world}" if world > 1 else "single GPU"}
+
+
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -66,16 +73,14 @@ def step_bytes(topk_ids, hidden, inter, top_k, tokens, act_bytes=2):
             + tokens * top_k * 8), n_touched
 
 
-def gemm_bytes(topk_ids, hidden, inter, top_k, tokens, proj):
-    """Algorithmic bytes of one grouped-GEMM launch (gate_up: W13 + hidden in
-    + mid out; down: W2 + mid in + fp32 partials out)."""
+def gemm_bytes(topk_ids, hidden, inter, top_k, tokens):
+    """Algorithmic bytes of the layer's GEMM launch (gate_up, SiLU*mul, down and
+    the fused top-k combine): the touched experts' packed weights, the tokens'
+    activations in and the layer output out.  The gathered activations, mid
+    rows and fp32 partials between them stay in L2."""
+    from exq_b200.synth import int4_expert_bytes
     n_touched = len(set(topk_ids.reshape(-1).tolist()))
-    slots = tokens * top_k
-    if proj == 0:
-        w = 2 * inter * hidden // 2 + 2 * (2 * inter * (hidden // 128))
-        return n_touched * w + tokens * hidden * 2 + slots * inter * 2
-    w = hidden * inter // 2 + 2 * (hidden * (inter // 128))
-    return n_touched * w + slots * inter * 2 + slots * hidden * 4
+    return n_touched * int4_expert_bytes(hidden, inter) + 2 * tokens * hidden * 2
 
 
 class ClockSampler:
@@ -228,11 +233,12 @@ def reference_arm(args):
         "ms_per_step": round(1e3 * tot_t / args.steps, 3), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "int4 weights (dequantised to fp32), fp32 math",
         "data": "synthetic (seeded Zipf router, N(0,0.02) weights)",
-        "config": {"workload": WORKLOAD, "l2": "n/a (CPU)"},
+        "config": bench_config(int(os.environ.get("WORLD_SIZE", "1"))),
         "cpu_baseline": {"value": round(value, 3), "unit": UNIT, "cores": meta["threads"],
                          "kind": "port",
                          "sample": f"each step: {n_tok} of the 256 tokens (seeded), full T=256 "
-                                   f"call = {1e3 * t_full:.0f} ms"},
+                                   f"call = {1e3 * t_full:.0f} ms; rank 0 only, host cores, "
+                                   f"dequantised fp32 weights cached"},
         "e2e": {"value": round(value, 3), "unit": UNIT, "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
@@ -300,14 +306,18 @@ def time_graphs(graphs, steps, warmup, dev):
     return e0.elapsed_time(e1) / 1e3
 
 
-STAGES = ("route", "prep", "gate_up", "down", "combine")
+# a layer call is two launches up to 4096 slots: routing fused with the
+# activation gather (stages 0-1), then one GEMM launch for gate_up, SiLU*mul,
+# down and the top-k combine (stages 2-4)
+LAUNCHES = (("route", 0, 2), ("gemm", 2, 5))
 
 
-def gemm_timing(banks, inputs, dev, reps=40):
+def launch_timing(banks, inputs, dev, reps=40):
     """Average device time of each launch of a layer call: one CUDA graph per
-    layer records an (external) event between consecutive launches."""
+    layer records an (external) event between the two launches (which breaks
+    their overlap: the GEMM launch then starts as an ordinary launch)."""
     import torch
-    sums = [0.0] * len(STAGES)
+    sums = [0.0] * len(LAUNCHES)
     s = torch.cuda.Stream(dev)
     s.wait_stream(torch.cuda.current_stream(dev))
     ev_graphs = []
@@ -316,12 +326,12 @@ def gemm_timing(banks, inputs, dev, reps=40):
             bank.reserve(x.shape[0], ids.shape[1])
             out = torch.empty(x.shape[0], bank.hidden, dtype=x.dtype, device=dev)
             evs = [torch.cuda.Event(enable_timing=True, external=True)
-                   for _ in range(len(STAGES) + 1)]
+                   for _ in range(len(LAUNCHES) + 1)]
             g = torch.cuda.CUDAGraph()
             with torch.cuda.graph(g, stream=s):
                 evs[0].record(s)
-                for i in range(len(STAGES)):
-                    bank.forward_range(x, ids, w, i, i + 1, out=out)
+                for i, (_, a, b) in enumerate(LAUNCHES):
+                    bank.forward_range(x, ids, w, a, b, out=out)
                     evs[i + 1].record(s)
             ev_graphs.append((g, evs))
     torch.cuda.current_stream(dev).wait_stream(s)
@@ -330,9 +340,9 @@ def gemm_timing(banks, inputs, dev, reps=40):
         g, evs = ev_graphs[r % len(ev_graphs)]
         g.replay()
         torch.cuda.synchronize(dev)
-        for i in range(len(STAGES)):
+        for i in range(len(LAUNCHES)):
             sums[i] += evs[i].elapsed_time(evs[i + 1])
-    return {nm: sums[i] / reps / 1e3 for i, nm in enumerate(STAGES)}
+    return {nm: sums[i] / reps / 1e3 for i, (nm, _, _) in enumerate(LAUNCHES)}
 
 
 def e2e_timing(banks, inputs, dev, steps, warmup):
@@ -435,6 +445,13 @@ def ep_measure(dev, world, rank, name, steps=50, warmup=5):
         except RuntimeError as e:  # raised on every rank alike: time the NCCL exchange
             layer = ExpertParallelLayer(local, c.n_experts, shared_bank=shared)
             exchange = f"nccl ({e})"
+    full = None
+    if world > 1:
+        # every rank holds all experts' dense weights: the whole layer on this
+        # GPU is the parity reference of the expert-parallel step
+        from exq_b200 import ExpertBank
+        full = ExpertBank.from_dense(w13, w2, None, act_dtype=c.act_dtype, shared_w13=sw13,
+                                     shared_w2=sw2)
     del w13, w2, sw13, sw2
     torch.cuda.empty_cache()
     ids, w = zipf_router(t, c.n_experts, c.top_k, seed=11 + rank)
@@ -487,6 +504,15 @@ def ep_measure(dev, world, rank, name, steps=50, warmup=5):
         st = torch.tensor([L.read_device_status(dev)], device=dev, dtype=torch.int64)
         dist.all_reduce(st, op=dist.ReduceOp.MAX)
         out["device_status"] = int(st.item())
+        # parity: the expert-parallel step against the whole layer on one GPU,
+        # each rank on its own tokens (max over ranks; the exchange returns
+        # each expert row rounded to the activation dtype)
+        y_ep = layer(x, ids, w).float()
+        y_one = full(x, ids, w).float()
+        rel = torch.tensor([float((y_ep - y_one).norm() / y_one.norm())], device=dev)
+        dist.all_reduce(rel, op=dist.ReduceOp.MAX)
+        out["rel_l2_vs_one_gpu"] = float(f"{rel.item():.3e}")
+        del full
     if world == 1 and name == "mixtral":
         out["prefill"] = prefill_measure(layer, c, dev)
     if world > 1 and layer.peer is not None:
@@ -595,15 +621,12 @@ def main():
         t_max, tot_bytes = float(tt.item()), float(bb.item())
     value = tot_bytes / t_max / 1e9
 
-    # ---- per-kernel roofline (gate_up grouped GEMM is the dominant kernel)
-    per_kernel = gemm_timing(banks, inputs, dev)
-    x0, ids0, w0, cpu_ids0 = inputs[0]
-    gu_bytes = statistics.mean(gemm_bytes(ci, c["hidden"], c["inter"], c["top_k"], c["tokens"], 0)
-                               for (_, _, _, ci) in inputs)
-    dn_bytes = statistics.mean(gemm_bytes(ci, c["hidden"], c["inter"], c["top_k"], c["tokens"], 1)
-                               for (_, _, _, ci) in inputs)
+    # ---- per-kernel roofline (the GEMM launch is the dominant kernel)
+    per_kernel = launch_timing(banks, inputs, dev)
+    g_bytes = statistics.mean(gemm_bytes(ci, c["hidden"], c["inter"], c["top_k"], c["tokens"])
+                              for (_, _, _, ci) in inputs)
     peak, peak_kind = measured_peak()
-    gu_ach = gu_bytes / per_kernel["gate_up"] / 1e9
+    g_ach = g_bytes / per_kernel["gemm"] / 1e9
     traffic = profiled_traffic()
 
     # ---- e2e through the public API with host buffers
@@ -654,28 +677,24 @@ def main():
         "scaling": "weak", "vs_baseline": None,
         "dtype": "w4a16: int4 weights, fp16 activations, fp32 accumulate",
         "data": "synthetic (seeded Zipf(1.1) router, N(0,0.02) weights, N(0,1) activations)",
-        "config": {"workload": WORKLOAD, "tokens": c["tokens"], "n_layers_rotated": N_LAYERS,
-                   "l2": "inputs larger than L2 (8 layers x 311 MB rotated)",
-                   "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
-                   "us_per_layer": round(1e6 * t_max / args.steps, 2),
-                   "hbm_frac_of_" + peak_kind: round(value / world / peak, 3)},
-        "roofline": {"bound": "hbm", "kernel": "moe_tc_kernel (gate_up launch)",
-                     "achieved": round(gu_ach, 1), "peak": peak, "unit": "GB/s",
-                     "frac": round(gu_ach / peak, 3),
-                     "traffic": (traffic or {}).get("gate_up_bytes_per_launch"),
-                     "algorithmic_bytes": int(gu_bytes), "peak_kind": peak_kind,
-                     # event-to-event device time of each stage; with <= 4096
-                     # slots the prep stage launches nothing and is left out
-                     "per_launch_us": {k: round(v * 1e6, 2) for k, v in per_kernel.items()
-                                       if k != "prep" or c["tokens"] * c["top_k"] > 4096},
-                     "down_achieved": round(dn_bytes / per_kernel["down"] / 1e9, 1)},
+        "config": bench_config(world),
+        "us_per_layer": round(1e6 * t_max / args.steps, 2),
+        "hbm_frac_of_" + peak_kind: round(value / world / peak, 3),
+        "roofline": {"bound": "hbm",
+                     "kernel": "moe_tc_kernel (gate_up, SiLU*mul, down, top-k combine: one launch)",
+                     "achieved": round(g_ach, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(g_ach / peak, 3),
+                     "traffic": (traffic or {}).get("gemm_bytes_per_launch"),
+                     "algorithmic_bytes": int(g_bytes), "peak_kind": peak_kind,
+                     # event-to-event device time of each launch of a call
+                     "per_launch_us": {k: round(v * 1e6, 2) for k, v in per_kernel.items()}},
         "cpu_baseline": cpu,
         "e2e": {"value": round(e2e_val, 1), "unit": UNIT, "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "steps": e2e_steps,
                 "us_per_layer": round(1e6 * t_e2e / e2e_steps, 2)},
-        # route+gather, gate_up, down, combine per layer call (the separate
+        # route+gather and the GEMM launch per layer call (the separate
         # activation-prep launch only runs above 4096 slots)
-        "gpu_launches": (4 if c["tokens"] * c["top_k"] <= 4096 else 5) * args.steps,
+        "gpu_launches": (2 if c["tokens"] * c["top_k"] <= 4096 else 3) * args.steps,
         "clocks": clk.summary(),
         "sweep": sweep,
     }
