@@ -51,6 +51,7 @@ SIGNATURES = {
                               vp]),
     "exq_ep_combine": (C.c_int, [vp, C.c_int, vp, vp, C.c_int, i64, i32, i64, vp, vp, vp]),
     "exq_ep_buffer_bytes": (sz, [i32, i64, i64]),
+    "exq_ep_set_wait_timeout": (C.c_int, [C.c_uint64]),
     "exq_ep_buffer_init": (C.c_int, [vp, i32, i64, i64, vp]),
     "exq_ep_ipc_alloc": (C.c_int, [sz, C.POINTER(C.c_void_p), vp]),
     "exq_ep_ipc_free": (C.c_int, [vp]),
@@ -160,6 +161,12 @@ def read_device_status(device: torch.device | None = None, clear: bool = True) -
         check(lib().exq_read_device_status(C.byref(out), int(clear), stream_of(device)),
               "read_device_status")
     return int(out.value)
+
+
+def set_ep_wait_timeout(ns: int = 0) -> None:
+    """Limit of the expert-parallel kernels' waits on other ranks, in
+    nanoseconds, for launches made after this call (0: the 5 s default)."""
+    check(lib().exq_ep_set_wait_timeout(int(ns)), "ep_set_wait_timeout")
 
 
 def exported_symbols() -> list[str]:

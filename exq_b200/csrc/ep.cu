@@ -57,9 +57,11 @@ constexpr int kEpFlagReturn = 64;
 constexpr int kEpStep = 128;
 constexpr int kEpTicketDispatch = 129;
 constexpr int kEpTicketReturn = 130;
+constexpr int kEpFailed = 131;  // nonzero once a wait of this rank's kernels ran out
 constexpr int64_t kEpHeaderBytes = 1024;
-// a wait on another rank gives up after this long
-constexpr unsigned long long kEpWaitNs = 5000000000ull;
+// a wait on another rank gives up after this long (exq_ep_set_wait_timeout)
+constexpr unsigned long long kEpWaitNsDefault = 5000000000ull;
+unsigned long long g_ep_wait_ns = kEpWaitNsDefault;
 
 struct EpLayout {
   int64_t ids, ones, recv, back, bytes;
@@ -91,13 +93,19 @@ __device__ __forceinline__ unsigned long long global_ns() {
   return t;
 }
 
-// Waits until *flag has reached `step` (wrap-safe).  Bounded by time and by
-// iterations; on expiry sets EXQ_DEV_TIMEOUT and returns false.
-__device__ bool ep_wait_flag(const uint32_t* flag, uint32_t step, uint32_t* status) {
+// Waits until *flag has reached `step` (wrap-safe).  Bounded by time
+// (wait_ns) and by iterations; on expiry sets EXQ_DEV_TIMEOUT, marks the
+// rank's buffer as failed (hdr[kEpFailed]) and returns false.  After that the
+// exchange is out of step: the kernels of this rank stop reading and writing
+// peer data, the peers' own waits run out in turn, and every rank must
+// re-initialise its buffer (exq_ep_buffer_init) before the next step.
+__device__ bool ep_wait_flag(const uint32_t* flag, uint32_t step, uint32_t* status,
+                             uint32_t* hdr, unsigned long long wait_ns) {
   const unsigned long long t0 = global_ns();
   for (uint32_t it = 0; static_cast<int32_t>(ld_acquire_sys(flag) - step) < 0; ++it) {
-    if (it > (1u << 27) || global_ns() - t0 > kEpWaitNs) {
+    if (it > (1u << 27) || global_ns() - t0 > wait_ns) {
       atomicOr(status, EXQ_DEV_TIMEOUT);
+      atomicExch(hdr + kEpFailed, 1u);
       return false;
     }
     __nanosleep(100);
@@ -269,12 +277,15 @@ template <typename T>
 __global__ void ep_combine_kernel(const T* __restrict__ rows, const int32_t* __restrict__ slot_row,
                                   const void* __restrict__ w, int w_dtype, int64_t n_tokens,
                                   int top_k, int64_t H, const T* __restrict__ base,
-                                  T* __restrict__ out, const uint32_t* wait_hdr, int n_ranks,
-                                  uint32_t* status) {
+                                  T* __restrict__ out, uint32_t* wait_hdr, int n_ranks,
+                                  uint32_t* status, unsigned long long wait_ns) {
   if (wait_hdr) {  // peer exchange: every expert rank has returned this step's rows
     const uint32_t step = *reinterpret_cast<const volatile uint32_t*>(wait_hdr + kEpStep);
-    if (threadIdx.x < n_ranks) ep_wait_flag(wait_hdr + kEpFlagReturn + threadIdx.x, step, status);
-    __syncthreads();
+    bool ok = true;
+    if (threadIdx.x < n_ranks)
+      ok = ep_wait_flag(wait_hdr + kEpFlagReturn + threadIdx.x, step, status, wait_hdr, wait_ns);
+    // a return that never came: the rows are not this step's, leave out untouched
+    if (__syncthreads_or(!ok)) return;
   }
   for (int64_t t = blockIdx.x; t < n_tokens; t += gridDim.x) {
     for (int64_t h = threadIdx.x; h < H; h += blockDim.x) {
@@ -293,9 +304,11 @@ __global__ void ep_combine_kernel(const T* __restrict__ rows, const int32_t* __r
 }
 
 // One thread per source rank waits for its arrival flag of the current step.
-__global__ void ep_wait_arrivals_kernel(const uint32_t* hdr, int n_ranks, uint32_t* status) {
+__global__ void ep_wait_arrivals_kernel(uint32_t* hdr, int n_ranks, uint32_t* status,
+                                        unsigned long long wait_ns) {
   const uint32_t step = *reinterpret_cast<const volatile uint32_t*>(hdr + kEpStep);
-  if (threadIdx.x < n_ranks) ep_wait_flag(hdr + kEpFlagArrive + threadIdx.x, step, status);
+  if (threadIdx.x < n_ranks)
+    ep_wait_flag(hdr + kEpFlagArrive + threadIdx.x, step, status, hdr, wait_ns);
 }
 
 template <typename T>
@@ -324,6 +337,10 @@ __global__ void __launch_bounds__(kEpThreads) ep_return_kernel(
   __shared__ uint8_t* peer[kEpMaxRanks];
   for (int d = threadIdx.x; d < n_ranks; d += kEpThreads) peer[d] = peers[d];
   __syncthreads();
+  // an arrival that never came (this step's rows are incomplete): send
+  // nothing back and raise no return flag
+  if (*reinterpret_cast<const volatile uint32_t*>(reinterpret_cast<uint32_t*>(peer[rank]) + kEpFailed))
+    return;
   const int64_t oct = H / 8;
   for (int q = blockIdx.x; q < rows; q += gridDim.x) {
     const int pos = pos_of_slot[q];
@@ -444,12 +461,12 @@ extern "C" int exq_ep_combine(const void* rows, int dtype, const int32_t* slot_r
     ep_combine_kernel<__half><<<grid, threads, 0, s>>>(
         static_cast<const __half*>(rows), slot_row, weights, w_dtype, n_tokens, top_k,
         hidden_size, static_cast<const __half*>(base), static_cast<__half*>(out), nullptr, 0,
-        nullptr);
+        nullptr, 0ull);
   else
     ep_combine_kernel<__nv_bfloat16><<<grid, threads, 0, s>>>(
         static_cast<const __nv_bfloat16*>(rows), slot_row, weights, w_dtype, n_tokens, top_k,
         hidden_size, static_cast<const __nv_bfloat16*>(base), static_cast<__nv_bfloat16*>(out),
-        nullptr, 0, nullptr);
+        nullptr, 0, nullptr, 0ull);
   EXQ_CHECK_LAUNCH("ep_combine_kernel");
   return EXQ_OK;
 }
@@ -464,6 +481,11 @@ static bool ep_sizes_ok(int32_t n_ranks, int64_t capacity, int64_t hidden_size) 
 extern "C" size_t exq_ep_buffer_bytes(int32_t n_ranks, int64_t capacity, int64_t hidden_size) {
   if (!ep_sizes_ok(n_ranks, capacity, hidden_size)) return 0;
   return static_cast<size_t>(ep_layout(n_ranks, capacity, 2 * hidden_size).bytes);
+}
+
+extern "C" int exq_ep_set_wait_timeout(uint64_t ns) {
+  g_ep_wait_ns = ns == 0 ? kEpWaitNsDefault : static_cast<unsigned long long>(ns);
+  return EXQ_OK;
 }
 
 extern "C" int exq_ep_buffer_init(void* buffer, int32_t n_ranks, int64_t capacity,
@@ -601,7 +623,8 @@ extern "C" int exq_ep_expert_forward(const exq_moe_weights* weights, int dtype, 
   uint8_t* b = static_cast<uint8_t*>(buffer);
   const EpLayout l = ep_layout(n_ranks, capacity, 2 * H);
   const int64_t rows = static_cast<int64_t>(n_ranks) * capacity;
-  ep_wait_arrivals_kernel<<<1, kEpMaxRanks, 0, s>>>(reinterpret_cast<const uint32_t*>(b), n_ranks, st);
+  ep_wait_arrivals_kernel<<<1, kEpMaxRanks, 0, s>>>(reinterpret_cast<uint32_t*>(b), n_ranks, st,
+                                                     g_ep_wait_ns);
   EXQ_CHECK_LAUNCH("ep_wait_arrivals_kernel");
   int r = exq_moe_layer_forward_range(weights, b + l.recv, dtype, rows, b + l.ids, EXQ_I32,
                                       b + l.ones, EXQ_F32, 1, b + l.back, workspace,
@@ -638,7 +661,7 @@ extern "C" int exq_ep_combine_peer(const void* buffer, int32_t n_ranks, int64_t 
   auto s = static_cast<cudaStream_t>(stream);
   const uint8_t* b = static_cast<const uint8_t*>(buffer);
   const EpLayout l = ep_layout(n_ranks, capacity, 2 * hidden_size);
-  const uint32_t* hdr = reinterpret_cast<const uint32_t*>(b);
+  uint32_t* hdr = reinterpret_cast<uint32_t*>(const_cast<uint8_t*>(b));
   // with no tokens one CTA still waits, so that the step ends with every return
   const int threads = static_cast<int>(hidden_size < 256 ? (hidden_size < kEpMaxRanks ? kEpMaxRanks : hidden_size) : 256);
   const int grid = static_cast<int>(n_tokens == 0 ? 1 : (n_tokens < 65535 ? n_tokens : 65535));
@@ -646,12 +669,12 @@ extern "C" int exq_ep_combine_peer(const void* buffer, int32_t n_ranks, int64_t 
     ep_combine_kernel<__half><<<grid, threads, 0, s>>>(
         reinterpret_cast<const __half*>(b + l.back), slot_row, weights, w_dtype, n_tokens, top_k,
         hidden_size, static_cast<const __half*>(base), static_cast<__half*>(out), hdr, n_ranks,
-        st);
+        st, g_ep_wait_ns);
   else
     ep_combine_kernel<__nv_bfloat16><<<grid, threads, 0, s>>>(
         reinterpret_cast<const __nv_bfloat16*>(b + l.back), slot_row, weights, w_dtype, n_tokens,
         top_k, hidden_size, static_cast<const __nv_bfloat16*>(base),
-        static_cast<__nv_bfloat16*>(out), hdr, n_ranks, st);
+        static_cast<__nv_bfloat16*>(out), hdr, n_ranks, st, g_ep_wait_ns);
   EXQ_CHECK_LAUNCH("ep_combine_kernel");
   return EXQ_OK;
 }

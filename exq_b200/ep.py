@@ -200,18 +200,53 @@ class ExpertParallelLayer:
         self.shared_fn = shared_fn or self._shared_rows
         self.pack_fn = pack_fn or _cuda_pack
         self.peer = None
+        self._ws = None
         if max_tokens is not None:
             if top_k is None or top_k <= 0 or max_tokens <= 0 or local_bank is None:
                 raise ValueError("the peer exchange needs max_tokens > 0, top_k > 0 and a bank")
+            if local_bank.n_shared:
+                raise ValueError("the peer exchange's local bank holds routed experts only; "
+                                 "pass the shared experts as shared_bank")
             self.peer = PeerExchange(group, max_tokens * top_k, local_bank.hidden,
                                      local_bank.device)
-            self.local_bank.reserve(self.world * self.peer.capacity, 1)
+            # the layer's own workspace, sized once: a captured step keeps
+            # pointing at it whatever else the bank is called on
+            self._ws = L.workspace(local_bank.device,
+                                   local_bank.workspace_bytes(self.world * self.peer.capacity, 1))
 
     def close(self) -> None:
         """Release the peer buffers (collective)."""
         if self.peer is not None:
             self.peer.close()
             self.peer = None
+
+    def check_status(self) -> None:
+        """Synchronise and raise if a kernel of this rank flagged an error since
+        the last check; a wait on another rank that ran out (EXQ_DEV_TIMEOUT)
+        means the peer exchange is out of step until ``reset`` (collective)."""
+        st = L.read_device_status(self.local_bank.device if self.local_bank is not None
+                                  else None, clear=True)
+        if st & L.DEV_TIMEOUT:
+            raise RuntimeError(f"rank {self.rank}: an expert-parallel wait on another rank ran "
+                               f"out (device status {st:#x}); call reset() on every rank")
+        if st:
+            raise RuntimeError(f"rank {self.rank}: device status {st:#x}")
+
+    def reset(self) -> None:
+        """Re-initialise this rank's peer buffer after a timed-out step
+        (collective: every rank calls it, and no rank's step is in flight)."""
+        if self.peer is None:
+            return
+        px, dev = self.peer, self.peer.device
+        torch.cuda.synchronize(dev)
+        flag = torch.zeros(1, device=dev)
+        dist.all_reduce(flag, group=self.group)   # every rank's kernels have drained
+        torch.cuda.synchronize(dev)
+        L.check(L.lib().exq_ep_buffer_init(px.ptr, self.world, px.capacity, px.hidden,
+                                           L.stream_of(dev)), "ep_buffer_init")
+        torch.cuda.synchronize(dev)
+        dist.all_reduce(flag, group=self.group)   # every buffer is clear before any dispatch
+        torch.cuda.synchronize(dev)
 
     def _host_counts(self, device) -> torch.Tensor:
         """[2 * world] int64 host buffer for the send / receive counts (pinned
@@ -237,17 +272,21 @@ class ExpertParallelLayer:
         return self.shared_bank(hidden, ids.contiguous(), w)
 
     def forward(self, hidden: torch.Tensor, topk_ids: torch.Tensor,
-                topk_weights: torch.Tensor) -> torch.Tensor:
+                topk_weights: torch.Tensor, check: bool = False) -> torch.Tensor:
         """[T, H] output for this rank's T tokens (same dtype as ``hidden``).
 
         Expert ids out of range are dropped and flagged in the device status,
         as in the single-GPU layer.  Every rank passes the same activation
         dtype: a rank runs its experts on the rows it receives in the dtype of
-        its own ``hidden``."""
+        its own ``hidden``.  ``check``: synchronise after the step and raise if
+        a kernel flagged an error (``check_status``)."""
         if topk_ids.shape != topk_weights.shape or topk_ids.shape[0] != hidden.shape[0]:
             raise ValueError("topk_ids / topk_weights must be [T, k] for hidden [T, H]")
         if self.peer is not None:
-            return self._forward_peer(hidden, topk_ids, topk_weights)
+            y = self._forward_peer(hidden, topk_ids, topk_weights)
+            if check:
+                self.check_status()
+            return y
         t, k = topk_ids.shape
         h = hidden.shape[1]
         send_rows, send_ids, slot_row, send_counts = self.pack_fn(hidden.contiguous(), topk_ids,
@@ -278,7 +317,10 @@ class ExpertParallelLayer:
         out_rows = self.local_fn(recv_rows, recv_ids).contiguous()
         back = hidden.new_empty(max(n_send, 1), h)
         dist.all_to_all_single(back[:n_send], out_rows, sc, rc, group=self.group)
-        return self.combine_fn(back, slot_row, topk_weights, shared)
+        y = self.combine_fn(back, slot_row, topk_weights, shared)
+        if check and y.is_cuda:
+            self.check_status()
+        return y
 
     def _forward_peer(self, hidden, topk_ids, topk_weights):
         px, bank, lib = self.peer, self.local_bank, L.lib()
@@ -289,13 +331,23 @@ class ExpertParallelLayer:
         dev = L.require_cuda(hidden, topk_ids, topk_weights)
         x, ids, w = hidden.contiguous(), topk_ids.contiguous(), topk_weights.contiguous()
         h = x.shape[1]
+        # everything the three launches check, before the dispatch raises this
+        # rank's flags on its peers (a later refusal would leave them waiting)
+        if x.dtype not in (torch.float16, torch.bfloat16):
+            raise ValueError("hidden must be fp16 or bf16")
+        if w.dtype not in (torch.float32, torch.float16, torch.bfloat16):
+            raise ValueError("topk_weights must be fp32, fp16 or bf16")
+        if ids.dtype not in (torch.int32, torch.int64):
+            raise ValueError("topk_ids must be int32 or int64")
+        if h != px.hidden or h != bank.hidden:
+            raise ValueError(f"hidden size {h} differs from the exchange's {px.hidden}")
         s = L.stream_of(dev)
         slot_row = torch.empty(t * k, dtype=torch.int32, device=dev)
         L.check(lib.exq_ep_dispatch(L.ptr(ids), L.tag(ids), t, k, self.per_rank, self.world,
                                     self.rank, L.ptr(x), L.tag(x), h, px.capacity,
                                     L.ptr(px.peers), L.ptr(slot_row), s), "ep_dispatch")
         shared = self.shared_fn(x)
-        ws = bank._ws
+        ws = self._ws
         L.check(lib.exq_ep_expert_forward(C.byref(bank.cstruct), L.tag(x), self.world, self.rank,
                                           px.capacity, px.ptr, L.ptr(px.peers), L.ptr(ws),
                                           ws.numel(), s), "ep_expert_forward")

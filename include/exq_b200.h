@@ -293,16 +293,28 @@ EXQ_API int exq_moe_layer_forward_range(const exq_moe_weights* weights,
  * `capacity` rows belongs to source rank s.  A step is, in stream order on
  * every rank: exq_ep_dispatch -> (shared experts) -> exq_ep_expert_forward
  * -> exq_ep_combine_peer.  Every rank must make the same calls in the same
- * order.  Waits on other ranks are bounded (about 5 s): on expiry the kernel
- * sets EXQ_DEV_TIMEOUT in the device status and returns. */
+ * order.  Waits on other ranks are bounded (5 s unless exq_ep_set_wait_timeout
+ * says otherwise): on expiry the kernel sets EXQ_DEV_TIMEOUT in the device
+ * status and marks the buffer failed, after which this rank's kernels neither
+ * read the rows of that step nor send any back, so the peers' waits run out
+ * too.  The caller reads the status (exq_read_device_status) and, after a
+ * timeout, re-initialises every rank's buffer (exq_ep_buffer_init, with the
+ * same barrier as at set-up) before the next step. */
 #define EXQ_IPC_HANDLE_BYTES 64
+
+/* The limit of every wait on another rank in the EP kernels launched after
+ * this call, in nanoseconds (0: the default of 5 s).  Process-wide; a CUDA
+ * graph keeps the limit it was captured with.  No counterpart in the
+ * reference (its layer has no expert parallelism). */
+EXQ_API int exq_ep_set_wait_timeout(uint64_t ns);
 
 /* Bytes of one rank's EP buffer; 0 for invalid sizes. */
 EXQ_API size_t exq_ep_buffer_bytes(int32_t n_ranks, int64_t capacity, int64_t hidden_size);
 
-/* Clears the flags and ids and writes the 1.0f column of a fresh buffer.
+/* Clears the flags, the step counter, the failed mark and the ids and writes
+ * the 1.0f column of a fresh buffer (or of one whose exchange timed out).
  * Every rank must finish it (stream synchronised, then a group barrier)
- * before any rank's first exq_ep_dispatch. */
+ * before any rank's next exq_ep_dispatch. */
 EXQ_API int exq_ep_buffer_init(void* buffer, int32_t n_ranks, int64_t capacity,
                                int64_t hidden_size, void* stream);
 

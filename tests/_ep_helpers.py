@@ -230,3 +230,70 @@ def agree_worker(rank, world, port):
             raise AssertionError(f"rank {rank} went on although rank 0 failed")
     finally:
         dist.destroy_process_group()
+
+
+def gpu_timeout_worker(rank, world, port):
+    """A device-side wait that runs out, on a one-rank peer exchange: a step
+    whose expert stage never runs leaves the combine waiting for a return flag
+    that nothing raises.  With a 2 ms limit the combine returns, the device
+    status carries EXQ_DEV_TIMEOUT, the layer's status check raises, a step
+    before the collective reset times out again (the buffer is marked failed),
+    and after reset() a correct step matches the whole layer on one GPU."""
+    from exq_b200 import ExpertBank
+    from exq_b200 import _lib as L
+    from exq_b200.ep import ExpertParallelLayer, build_rank_banks
+    from exq_b200.synth import expert_weights
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    _init(rank, world, port, "nccl")
+    try:
+        e, h, inter, k, t = 8, 512, 256, 2, 24
+        w13, w2 = expert_weights(e, inter, h, seed=0, device=dev)
+        local, _ = build_rank_banks(w13, w2, world, rank, act_dtype=torch.bfloat16)
+        full = ExpertBank.from_dense(w13, w2, None, act_dtype=torch.bfloat16)
+        layer = ExpertParallelLayer(local, e, max_tokens=64, top_k=k)
+        x, ids, w = _gpu_step_inputs(0, rank, world, t, "spread", e, h, k, dev)
+        L.read_device_status(dev, clear=True)
+        y = layer(x, ids, w, check=True)
+        assert OM.rel_l2(y.float().cpu(), full(x, ids, w).float().cpu()) < 5e-3
+
+        L.set_ep_wait_timeout(2_000_000)
+        try:
+            px, lib, s = layer.peer, L.lib(), L.stream_of(dev)
+            ids32 = ids.to(torch.int32).contiguous()
+            slot_row = torch.empty(t * k, dtype=torch.int32, device=dev)
+            L.check(lib.exq_ep_dispatch(L.ptr(ids32), L.tag(ids32), t, k, e // world, world, rank,
+                                        L.ptr(x), L.tag(x), h, px.capacity, L.ptr(px.peers),
+                                        L.ptr(slot_row), s), "ep_dispatch")
+            # no exq_ep_expert_forward: this step's return flag is never raised
+            out = torch.full((t, h), 7.0, dtype=x.dtype, device=dev)
+            wc = w.contiguous()
+            L.check(lib.exq_ep_combine_peer(px.ptr, world, px.capacity, h, L.tag(x),
+                                            L.ptr(slot_row), L.ptr(wc), L.tag(wc), t, k, None,
+                                            L.ptr(out), s), "ep_combine_peer")
+            torch.cuda.synchronize(dev)          # the kernel returned
+            assert bool((out == 7.0).all()), "a timed-out combine must not write its output"
+            try:
+                layer.check_status()
+            except RuntimeError as err:
+                assert "ran out" in str(err), str(err)
+            else:
+                raise AssertionError("the timed-out wait was not reported")
+            # out of step until reset: the next step's return is withheld
+            layer(x, ids, w)
+            torch.cuda.synchronize(dev)
+            assert L.read_device_status(dev, clear=True) & L.DEV_TIMEOUT
+        finally:
+            L.set_ep_wait_timeout(0)
+        layer.reset()
+        x2, ids2, w2_ = _gpu_step_inputs(1, rank, world, t, "spread", e, h, k, dev)
+        y2 = layer(x2, ids2, w2_, check=True)
+        assert OM.rel_l2(y2.float().cpu(), full(x2, ids2, w2_).float().cpu()) < 5e-3
+        layer.close()
+        dist.barrier()
+    except BaseException:
+        traceback.print_exc()
+        sys.stderr.flush()
+        raise
+    finally:
+        dist.destroy_process_group()

@@ -65,3 +65,11 @@ def test_ep_peer_two_gpus_matches_nccl_and_single_gpu():
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
     mp.spawn(EH.gpu_worker, args=(2, _free_port(), "peer"), nprocs=2, join=True)
+
+
+@pytest.mark.gpu
+def test_ep_peer_wait_runs_out_and_recovers():
+    """A wait on another rank that runs out (2 ms limit, a return flag that
+    nothing raises) returns with EXQ_DEV_TIMEOUT, is reported by the layer's
+    status check, and the exchange works again after reset() (one GPU)."""
+    mp.spawn(EH.gpu_timeout_worker, args=(1, _free_port()), nprocs=1, join=True)
