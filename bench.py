@@ -60,6 +60,11 @@ def parse():
                     help="skip the expert-parallel configs (C4, C5; one GPU = whole layer)")
     ap.add_argument("--profile", action="store_true",
                     help="small case for ncu: one layer of the bench workload, 3 eager calls")
+    ap.add_argument("--no-ref-gpu", action="store_true",
+                    help="skip the reference's own GPU path (Triton GEMMs + exq_dispatch_cuda)")
+    ap.add_argument("--setup-reference", action="store_true",
+                    help="copy the reference's GPU modules (checkout at $EXQ_REFERENCE) into "
+                         "baseline/_ref and build its dispatch extension from source")
     return ap.parse_args()
 
 
@@ -244,6 +249,157 @@ def reference_arm(args):
     }
     print(json.dumps(line), flush=True)
     return 0
+
+
+# ----------------------------------------------------- reference GPU path
+REF_DIR = ROOT / "baseline" / "_ref" / "exq_src"
+REF_FILES = ("exq/kernels/moe_int4_kernel.py", "exq/kernels/moe_grouped_gemm.py",
+             "exq/kernels/cuda_src/exq_dispatch.cu")
+
+
+def setup_reference():
+    """Install the reference's GPU path for this layer into baseline/_ref.
+
+    The reference package does not pip-install here (its build backend is
+    maturin, for a Rust extension module, and no Rust toolchain is present).
+    Its layer path needs only two pure-Python Triton modules and one CUDA
+    extension source; they are copied unmodified and the extension is built
+    from source with torch's extension builder for sm_100, as the
+    reference's own setup_cuda.py builds it (for sm_86)."""
+    import shutil
+    src = os.environ.get("EXQ_REFERENCE")
+    if not src or not Path(src, REF_FILES[0]).exists():
+        print("set EXQ_REFERENCE to the reference checkout", file=sys.stderr)
+        return 1
+    REF_DIR.mkdir(parents=True, exist_ok=True)
+    for f in REF_FILES:
+        shutil.copy2(Path(src, f), REF_DIR / Path(f).name)
+    os.environ["TORCH_CUDA_ARCH_LIST"] = "10.0"
+    from torch.utils.cpp_extension import load
+    build = REF_DIR / "build"
+    build.mkdir(exist_ok=True)
+    load(name="exq_dispatch_cuda", sources=[str(REF_DIR / "exq_dispatch.cu")],
+         build_directory=str(build), extra_cflags=["-O3"],
+         extra_cuda_cflags=["-O3", "--use_fast_math", "-lineinfo", "--expt-relaxed-constexpr"],
+         verbose=False)
+    print(f"reference GPU path installed in {REF_DIR}")
+    return 0
+
+
+def load_reference_gpu():
+    """(triton module, exq_dispatch_cuda) from baseline/_ref, or a reason string."""
+    import importlib.util
+    so = sorted((REF_DIR / "build").glob("exq_dispatch_cuda*.so"))
+    if not (REF_DIR / "moe_int4_kernel.py").exists() or not so:
+        return None, "reference GPU path not installed (bench.py --setup-reference)"
+    try:
+        spec = importlib.util.spec_from_file_location("exq_ref_moe_int4", REF_DIR / "moe_int4_kernel.py")
+        tri = importlib.util.module_from_spec(spec)
+        spec.loader.exec_module(tri)
+        spec = importlib.util.spec_from_file_location("exq_dispatch_cuda", so[0])
+        disp = importlib.util.module_from_spec(spec)
+        spec.loader.exec_module(disp)
+    except Exception as e:  # noqa: BLE001 - reported in the bench line
+        return None, f"{type(e).__name__}: {e}"
+    return (tri, disp), None
+
+
+def ref_align(topk_ids, n_buckets, block, max_padded):
+    """sgl_kernel.moe_align_block_size's contract in torch ops (sgl_kernel is
+    not installed): slots of each of n_buckets experts in ascending slot
+    order, each expert's run padded to a multiple of `block` with the pad
+    value T*k.  Only sorted_token_ids feeds the rest of the path."""
+    import torch
+    flat = topk_ids.reshape(-1).long()
+    n = flat.numel()
+    counts = torch.bincount(flat, minlength=n_buckets)
+    padded = (counts + block - 1) // block * block
+    starts = torch.cumsum(padded, 0) - padded
+    order = torch.argsort(flat, stable=True)
+    rank = torch.arange(n, device=flat.device) - (torch.cumsum(counts, 0) - counts)[flat[order]]
+    out = torch.full((max_padded,), n, dtype=torch.int32, device=flat.device)
+    out[starts[flat[order]] + rank] = order.to(torch.int32)
+    return out
+
+
+def ref_layer(ref, w1p, w1s, w2p, w2s, x, ids, w, n_experts):
+    """The body of the reference's _exq_forward_cuda (exq/runtime/
+    sglang_backend.py:99-156) on its own kernels: align (torch stand-in),
+    build_ends_from_slots, gather_hidden, the Triton INT4 GEMM, SiLU*mul
+    (torch stand-in for sgl_kernel), the Triton GEMM again and combine."""
+    import torch
+    import torch.nn.functional as F
+    tri, disp = ref
+    n_tokens, hidden = x.shape
+    top_k = ids.shape[1]
+    n_active = n_tokens * top_k
+    inter2 = w1p.shape[1]
+    inter = inter2 // 2
+    max_padded = n_active + (n_experts + 1) * 15
+    sorted_ids = ref_align(ids, n_experts + 1, 16, max_padded)
+    flat_router = ids.reshape(-1).int().contiguous()
+    sort_order = torch.empty(n_active, dtype=torch.int64, device=x.device)
+    expert_ends = torch.zeros(n_experts + 1, dtype=torch.int32, device=x.device)
+    disp.build_ends_from_slots(sorted_ids, flat_router, expert_ends, sort_order, n_active,
+                               n_experts)
+    sorted_hidden = torch.empty(n_active, hidden, dtype=torch.float16, device=x.device)
+    disp.gather_hidden(x, sort_order, sorted_hidden, top_k)
+    max_tok = int((expert_ends[1:] - expert_ends[:-1]).max().item())
+    nm = max((max_tok + 63) // 64, 1)
+    gate_up = torch.zeros(n_active, inter2, dtype=torch.float16, device=x.device)
+    tri._moe_gemm_int4_kernel[(n_experts, nm, (inter2 + 127) // 128)](
+        sorted_hidden, w1p, w1s, gate_up, expert_ends, N=inter2, K=hidden,
+        stride_am=sorted_hidden.stride(0), stride_be=w1p.stride(0), stride_bn=w1p.stride(1),
+        stride_se=w1s.stride(0), stride_sn=w1s.stride(1), stride_cm=gate_up.stride(0),
+        BLOCK_M=64, BLOCK_N=128, BLOCK_K=32, GROUP_SIZE=128)
+    mid = (F.silu(gate_up[:, :inter].float()) * gate_up[:, inter:].float()).half()
+    down = torch.zeros(n_active, hidden, dtype=torch.float16, device=x.device)
+    tri._moe_gemm_int4_kernel[(n_experts, nm, (hidden + 127) // 128)](
+        mid, w2p, w2s, down, expert_ends, N=hidden, K=inter,
+        stride_am=mid.stride(0), stride_be=w2p.stride(0), stride_bn=w2p.stride(1),
+        stride_se=w2s.stride(0), stride_sn=w2s.stride(1), stride_cm=down.stride(0),
+        BLOCK_M=64, BLOCK_N=128, BLOCK_K=32, GROUP_SIZE=128)
+    result = torch.empty(n_tokens, hidden, dtype=torch.float16, device=x.device)
+    disp.combine(down, sort_order, w.half().contiguous(), result)
+    return result
+
+
+def reference_gpu_measure(dev, banks, sweep_t=SWEEP_T, reps=30):
+    """The reference's own B200 path timed on the same layers and routings as
+    the sweep (eager calls: it synchronises on the host for max_tok each call),
+    with its output checked against this repo's layer."""
+    import torch
+    ref, why = load_reference_gpu()
+    if ref is None:
+        return {"unavailable": why}
+    c = CFG
+    L = len(banks)
+    packed = []
+    for bank in banks:
+        _, a13, a2 = zip(*[bank.expert_reference_format(e) for e in range(c["n_experts"])])
+        packed.append((torch.stack([a[0] for a in a13]), torch.stack([a[1] for a in a13]).contiguous(),
+                       torch.stack([a[0] for a in a2]), torch.stack([a[1] for a in a2]).contiguous()))
+    out = {"path": "reference _exq_forward_cuda body: Triton _moe_gemm_int4_kernel (JIT for "
+                   "sm_100) + exq_dispatch_cuda built from source; align and silu_and_mul are "
+                   "torch stand-ins (sgl_kernel absent)", "per_T": {}}
+    for t in sweep_t:
+        inp = layer_inputs(dev, t, L, seed0=7)
+        for i in range(L):   # warm (Triton JIT) and parity
+            x, ids, w, _ = inp[i]
+            y_ref = ref_layer(ref, *packed[i], x, ids, w, c["n_experts"])
+        y_ours = banks[L - 1](x, ids, w)
+        rel = float((y_ref.float() - y_ours.float()).norm() / y_ours.float().norm())
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for r in range(reps):
+            x, ids, w, _ = inp[r % L]
+            ref_layer(ref, *packed[r % L], x, ids, w, c["n_experts"])
+        e1.record()
+        torch.cuda.synchronize(dev)
+        us = e0.elapsed_time(e1) / reps * 1e3
+        out["per_T"][str(t)] = {"us": round(us, 1), "rel_l2_vs_ours": float(f"{rel:.2e}")}
+    return out
 
 
 # ----------------------------------------------------------------- GPU arm
@@ -571,6 +727,8 @@ def profile_case():
 
 def main():
     args = parse()
+    if args.setup_reference:
+        return setup_reference()
     if args.impl == "reference":
         return reference_arm(args)
     if args.profile:
@@ -656,6 +814,14 @@ def main():
                                  len(set(ci.reshape(-1).tolist())) for (_, _, _, ci) in inp), 1)}
             del gs
 
+    ref_gpu = None
+    if world == 1 and not args.no_ref_gpu:
+        ref_gpu = reference_gpu_measure(dev, banks)
+        for t, r in ref_gpu.get("per_T", {}).items():
+            if t in sweep:
+                r["ours_us"] = sweep[t]["us"]
+                r["speedup"] = round(r["us"] / sweep[t]["us"], 2)
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         cpu = cpu_baseline()
@@ -698,6 +864,8 @@ def main():
         "clocks": clk.summary(),
         "sweep": sweep,
     }
+    if ref_gpu is not None:
+        line["reference_gpu"] = ref_gpu
     if ep:
         line["ep"] = ep
     print(json.dumps(line), flush=True)
