@@ -52,11 +52,11 @@
 namespace exq {
 namespace tc {
 
-constexpr int kWarps = 20;
+constexpr int kWarps = 21;
 constexpr int kThreads = kWarps * 32;
 constexpr int kWarpW = 0, kWarpB = 1, kWarpMma = 2;
-constexpr int kWarpCmb = 19;    // fused top-k combine
-constexpr int kCmbRing = 4;     // down items the epilogue may run ahead of the combine warp
+constexpr int kWarpCmb0 = 19, kNumCmb = 2;  // fused top-k combine: warp i takes down items i, i+2, ..
+constexpr int kCmbRing = 4;     // down items the epilogue may run ahead of the combine warps
 constexpr int kCmbMaxSpt = 16;  // slots per token the fused combine handles
 constexpr int kEpiWarp0 = 3, kNumEpiWarps = 4;
 constexpr int kDqWarp0 = 7, kDqGroups = 3, kDqGroupWarps = 4;  // 3 groups x 4 lane quarters
@@ -82,12 +82,16 @@ constexpr int kOffItems = kOffMisc + 64;
 constexpr int kItemBytes = 48;  // sizeof(Item)
 constexpr int kHistBuckets = 1024;  // experts the in-kernel tile list handles
 constexpr int kOffHist = kOffItems + kItemTab * kItemBytes;  // 3 x (kHistBuckets + 1) ints
-// The histogram region is free once the item table is built; the combine
-// warp then keeps the slot positions and router weights of an item's rows
-// there: [kMaxN rows][kCmbMaxSpt] ints + floats.
+// The histogram region is free once the item table is built; each combine
+// warp then keeps the slot positions and router weights of an item's
+// finishing rows there: [kMaxN rows][kCmbMaxSpt] ints + floats per warp.
 constexpr int kOffCmb = kOffHist;
-static_assert(2 * kMaxN * kCmbMaxSpt * 4 <= 3 * (kHistBuckets + 1) * 4, "combine staging size");
-constexpr int kSmemBytes = kOffHist + 3 * (kHistBuckets + 1) * 4 + 1024;  // + slack to align the base to 1024 B
+constexpr int kCmbWarpBytes = 2 * kMaxN * kCmbMaxSpt * 4;
+constexpr int kHistRegion = 3 * (kHistBuckets + 1) * 4 > kNumCmb * kCmbWarpBytes
+                                ? 3 * (kHistBuckets + 1) * 4
+                                : kNumCmb * kCmbWarpBytes;
+constexpr int kSmemBytes = kOffHist + kHistRegion + 1024;  // + slack to align the base to 1024 B
+static_assert(kSmemBytes <= 232448, "shared memory per CTA");
 constexpr int kEpiBar = 1;  // named barrier of the four epilogue warps
 
 enum : int { kTierBF16 = EXQ_TIER_BF16, kTierINT8 = EXQ_TIER_INT8, kTierINT4 = EXQ_TIER_INT4 };
@@ -833,20 +837,22 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
         if (lane == 0) mbar_arrive(Cmb_full(ci));
       }
     }
-  } else if (warp == kWarpCmb) {
+  } else if (warp >= kWarpCmb0 && warp < kWarpCmb0 + kNumCmb) {
     // ---------------------------------------------------------- fused top-k combine
     // For every down item, once the epilogue has stored its rows' fp32
-    // partials: one arrival per row on the (token, 128-column block) counter;
-    // a row whose arrival completes its token's valid slots makes this warp
-    // sum the token's partials in slot order (the other items' rows come from
-    // L2) and write y for the block.  The sums run off the GEMM pipeline: the
-    // epilogue only waits for a free entry of the kCmbRing-deep hand-off.
+    // partials: one arrival per row on the (token, 128-column block) counter,
+    // which the routing stage set to minus the token's valid slots; the row
+    // whose arrival brings it to zero makes this warp sum the token's
+    // partials in slot order (the other items' rows come from L2) and write y
+    // for the block.  Two warps take alternate down items, off the GEMM
+    // pipeline: the epilogue only waits for a free kCmbRing hand-off entry.
     if (p.fuse_combine) {
+      const int cw = warp - kWarpCmb0;
       pdl_wait();  // pos_of_slot / sorted_slot come from the routing kernel
       // a token none of whose slots has an expert gets no arrival: zero row
       const int64_t n_tok = p.n_slots / p.spt;
-      for (int64_t t = static_cast<int64_t>(blockIdx.x) * 32 + lane; t < n_tok;
-           t += static_cast<int64_t>(gridDim.x) * 32) {
+      for (int64_t t = (static_cast<int64_t>(blockIdx.x) * kNumCmb + cw) * 32 + lane; t < n_tok;
+           t += static_cast<int64_t>(gridDim.x) * kNumCmb * 32) {
         int need = 0;
         for (int j = 0; j < p.spt; ++j) need += __ldcg(p.pos_of_slot + t * p.spt + j) >= 0;
         if (need == 0) {
@@ -854,35 +860,25 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
           for (int64_t c = 0; c < p.hidden / 8; ++c) yrow[c] = make_uint4(0, 0, 0, 0);
         }
       }
-      int* spos = reinterpret_cast<int*>(gbase + kOffCmb);     // [kMaxN][kCmbMaxSpt]
+      int* spos = reinterpret_cast<int*>(gbase + kOffCmb + cw * kCmbWarpBytes);  // [kMaxN][kCmbMaxSpt]
       float* sw = reinterpret_cast<float*>(spos + kMaxN * kCmbMaxSpt);
       const int nhb = static_cast<int>(p.hidden >> 7);
       const int spt = p.spt;
+      const float* part = static_cast<const float*>(p.pj[1].out);
+      const int64_t stride = p.pj[1].out_stride;
       int dc = 0;
       for (int item = blockIdx.x, li = 0; item < n_items; item += gridDim.x, ++li) {
         Item it;
         if (!decode_item(p, items_tab, li, item, n_tiles, it) || it.prj != 1) continue;
-        const uint32_t ci = dc % kCmbRing, ph = (dc / kCmbRing) & 1;
-        ++dc;
-        // rows lane and lane + 32: token, valid slots, positions and weights
-        // (loaded before the wait; the routing kernel wrote them)
-        int tok[2], need[2] = {0, 0};
+        const int d = dc++;
+        if (d % kNumCmb != cw) continue;
+        const uint32_t ci = d % kCmbRing, ph = (d / kCmbRing) & 1;
+        // rows lane and lane + 32: their tokens (loaded before the wait)
+        int tok[2];
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
           const int c = lane + 32 * h;
-          tok[h] = -1;
-          if (c < it.mc) {
-            tok[h] = __ldcg(p.sorted_slot + it.m0 + c) / spt;
-            for (int j = 0; j < spt; ++j) {
-              const int r = __ldcg(p.pos_of_slot + tok[h] * spt + j);
-              need[h] += r >= 0;
-              spos[c * kCmbMaxSpt + j] = r;
-              sw[c * kCmbMaxSpt + j] =
-                  j < p.top_k ? load_as_f32(p.topk_w, p.w_dtype,
-                                            static_cast<int64_t>(tok[h]) * p.top_k + j)
-                              : 1.0f;
-            }
-          }
+          tok[h] = c < it.mc ? __ldcg(p.sorted_slot + it.m0 + c) / spt : -1;
         }
         const bool got = !aborted() && mbar_wait(Cmb_full(ci), ph, p.status);
         if (!__all_sync(0xffffffffu, got)) {
@@ -894,26 +890,42 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
         __threadfence();
         __syncwarp();
         if (lane == 0) mbar_arrive(Cmb_empty(ci));
-        bool fin[2];
+        int old[2];
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          fin[h] = false;
-          if (tok[h] >= 0) {
-            const int old = atomicAdd(p.comb_cnt + tok[h] * nhb + it.nb, 1);
-            fin[h] = old + 1 == need[h];
-          }
-        }
-        uint64_t mask = static_cast<uint64_t>(__ballot_sync(0xffffffffu, fin[0])) |
-                        (static_cast<uint64_t>(__ballot_sync(0xffffffffu, fin[1])) << 32);
+        for (int h = 0; h < 2; ++h)
+          old[h] = tok[h] >= 0 ? atomicAdd(p.comb_cnt + tok[h] * nhb + it.nb, 1) : 0;
+        const uint64_t mask = static_cast<uint64_t>(__ballot_sync(0xffffffffu, old[0] == -1)) |
+                              (static_cast<uint64_t>(__ballot_sync(0xffffffffu, old[1] == -1)) << 32);
         if (!mask) continue;
         __threadfence();  // acquire the other items' partial rows of these tokens
+        // slot positions and router weights of the finishing rows, all loads in flight
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          if (old[h] != -1) continue;
+          const int c = lane + 32 * h;
+          int r[kCmbMaxSpt];
+          float wv[kCmbMaxSpt];
+#pragma unroll
+          for (int j = 0; j < kCmbMaxSpt; ++j) {
+            r[j] = j < spt ? __ldcg(p.pos_of_slot + tok[h] * spt + j) : -1;
+            wv[j] = j < spt ? (j < p.top_k ? load_as_f32(p.topk_w, p.w_dtype,
+                                                         static_cast<int64_t>(tok[h]) * p.top_k + j)
+                                           : 1.0f)
+                            : 0.f;
+          }
+#pragma unroll
+          for (int j = 0; j < kCmbMaxSpt; ++j) {
+            spos[c * kCmbMaxSpt + j] = r[j];
+            sw[c * kCmbMaxSpt + j] = wv[j];
+          }
+        }
+        __syncwarp();
         // lane: 4 consecutive columns of the 128-column block
         const int col = it.r0 + 4 * lane;
-        const float* part = static_cast<const float*>(p.pj[1].out);
-        const int64_t stride = p.pj[1].out_stride;
-        while (mask) {
-          const int c = __ffsll(static_cast<long long>(mask)) - 1;
-          mask &= mask - 1;
+        uint64_t left = mask;
+        while (left) {
+          const int c = __ffsll(static_cast<long long>(left)) - 1;
+          left &= left - 1;
           const int t = __shfl_sync(0xffffffffu, c < 32 ? tok[0] : tok[1], c & 31);
           float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
           // the sum of combine_partials_kernel: slot order, product and sum
@@ -949,6 +961,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
           }
           *reinterpret_cast<uint2*>(static_cast<__half*>(p.y) + yo) = packed;
         }
+        __syncwarp();  // the staging rows are read before the next item rewrites them
       }
     }
   } else {
@@ -1301,7 +1314,7 @@ struct TcWs {
   int32_t* tile_info;
   int32_t* n_tiles;
   int32_t* tile_done;  // [max_tiles] gate_up row blocks stored per tile
-  int32_t* comb_cnt;   // [n_tokens * hidden/128] fused-combine arrivals
+  int32_t* comb_cnt;   // [n_tokens * hidden/128] fused-combine arrivals (start: -valid slots)
   __half* act;
   __half* mid;
   float* partial;
@@ -1453,7 +1466,8 @@ extern "C" int exq_moe_layer_forward_range(const exq_moe_weights* w, const void*
     rg.max_tiles = ws.max_tiles;
     rg.sorted_slot = ws.sorted_slot;
     rg.counters = ws.tile_done;
-    rg.n_counters = ws.n_counters;
+    rg.n_tile_counters = ws.max_tiles;
+    rg.comb_blocks = static_cast<int>(H / 128);
     st = launch_route_gather(rg, s, chained);
     if (st != EXQ_OK) return st;
     chained = true;
@@ -1478,7 +1492,8 @@ extern "C" int exq_moe_layer_forward_range(const exq_moe_weights* w, const void*
     rp.n_tiles = ws.n_tiles;
     rp.max_tiles = ws.max_tiles;
     rp.counters = ws.tile_done;
-    rp.n_counters = ws.n_counters;
+    rp.n_tile_counters = ws.max_tiles;
+    rp.comb_blocks = static_cast<int>(H / 128);
     st = launch_route(rp, kRouteLayer, s, chained);
     if (st != EXQ_OK) return st;
     chained = true;
