@@ -75,9 +75,8 @@ struct RouteParams {
   int32_t* tile_info;          // LAYER: [max_tiles][3] = expert, first row, rows
   int32_t* n_tiles;            // LAYER: [1]
   int64_t max_tiles;
-  int32_t* counters;           // LAYER: [n_tile_counters] zeroed, then [T][comb_blocks] set
-  int64_t n_tile_counters;     //   to minus the token's valid slots (the GEMM's counters)
-  int comb_blocks;
+  int32_t* counters;           // LAYER: zeroed (the GEMM's tile and work counters)
+  int64_t n_counters;
   uint32_t* status;
 };
 
@@ -108,9 +107,8 @@ struct RouteGatherParams {
   int32_t* n_tiles;     // [1]
   int64_t max_tiles;
   int32_t* sorted_slot; // [n] slot at every sorted position (or null)
-  int32_t* counters;    // [n_tile_counters] zeroed, then [T][comb_blocks] set to minus
-  int64_t n_tile_counters;  // the token's valid slots (the GEMM's tile and combine counters)
-  int comb_blocks;
+  int32_t* counters;    // [n_counters] zeroed (the GEMM's tile and work counters)
+  int64_t n_counters;
   uint32_t* status;
 };
 

@@ -55,8 +55,10 @@ namespace tc {
 constexpr int kWarps = 21;
 constexpr int kThreads = kWarps * 32;
 constexpr int kWarpW = 0, kWarpB = 1, kWarpMma = 2;
-constexpr int kWarpCmb0 = 19, kNumCmb = 2;  // fused top-k combine: warp i takes down items i, i+2, ..
-constexpr int kCmbRing = 4;     // down items the epilogue may run ahead of the combine warps
+constexpr int kWarpCmb0 = 19, kNumCmb = 2;  // wait for the down items, then join the combine
+constexpr int kItemRing = 8;    // claimed items handed from the weight producer to the other roles
+constexpr int kItemConsumers = 18;  // activation producer, MMA, 4 epilogue, 12 dequant warps
+constexpr int kTailWarp0 = 3, kTailWarps = kWarps - 3;  // epilogue, dequant, combine warps
 constexpr int kCmbMaxSpt = 16;  // slots per token the fused combine handles
 constexpr int kEpiWarp0 = 3, kNumEpiWarps = 4;
 constexpr int kDqWarp0 = 7, kDqGroups = 3, kDqGroupWarps = 4;  // 3 groups x 4 lane quarters
@@ -75,24 +77,21 @@ constexpr int kOffB = 0;
 constexpr int kOffW = kOffB + kBStages * kBSlot;
 constexpr int kOffS = kOffW + kWStages * kWSlot;
 constexpr int kOffBar = kOffS + kWStages * kSSlot;
-constexpr int kNumBars = 2 * kWStages + 2 * kABufs + 2 * kBStages + 4 + 2 * kCmbRing;
+constexpr int kNumBars = 2 * kWStages + 2 * kABufs + 2 * kBStages + 4 + 2 * kItemRing;
 constexpr int kOffMisc = kOffBar + kNumBars * 8;
-constexpr int kItemTab = 128;  // work items of this CTA decoded into shared memory up front
+constexpr int kItemTab = 128;  // region of 48-byte entries: the item ring, then the combine staging
 constexpr int kOffItems = kOffMisc + 64;
 constexpr int kItemBytes = 48;  // sizeof(Item)
 constexpr int kHistBuckets = 1024;  // experts the in-kernel tile list handles
 constexpr int kOffHist = kOffItems + kItemTab * kItemBytes;  // 3 x (kHistBuckets + 1) ints
-// The histogram region is free once the item table is built; each combine
-// warp then keeps the slot positions and router weights of an item's
-// finishing rows there: [kMaxN rows][kCmbMaxSpt] ints + floats per warp.
-constexpr int kOffCmb = kOffHist;
-constexpr int kCmbWarpBytes = 2 * kMaxN * kCmbMaxSpt * 4;
-constexpr int kHistRegion = 3 * (kHistBuckets + 1) * 4 > kNumCmb * kCmbWarpBytes
-                                ? 3 * (kHistBuckets + 1) * 4
-                                : kNumCmb * kCmbWarpBytes;
-constexpr int kSmemBytes = kOffHist + kHistRegion + 1024;  // + slack to align the base to 1024 B
+// After the item ring: the slot positions and router weights of this CTA's
+// share of the tokens, for the combine at the end of the launch.
+constexpr int kOffCmb = kOffItems + kItemRing * kItemBytes;
+constexpr int kCmbEntries = (kItemTab - kItemRing) * kItemBytes / 8;
+constexpr int kSmemBytes = kOffHist + 3 * (kHistBuckets + 1) * 4 + 1024;  // + slack to align the base to 1024 B
 static_assert(kSmemBytes <= 232448, "shared memory per CTA");
-constexpr int kEpiBar = 1;  // named barrier of the four epilogue warps
+constexpr int kEpiBar = 1;   // named barrier of the four epilogue warps
+constexpr int kTailBar = 2;  // named barrier of the combine at the end (kTailWarps warps)
 
 enum : int { kTierBF16 = EXQ_TIER_BF16, kTierINT8 = EXQ_TIER_INT8, kTierINT4 = EXQ_TIER_INT4 };
 
@@ -122,13 +121,17 @@ struct TcParams {
   // producer waits until all nb_gu row blocks of its tile have done so.
   int link;
   int* tile_done;
-  // fuse_combine (down items): y[t] = sum_j w[t, j] * partial[pos(t, j)] is
-  // computed by the combine warp of the CTA that stores a token's last partial
-  // row of a 128-column block, counted in comb_cnt[t * (H/128) + block]
-  // (zeroed by the route stage).  Same order and rounding as
-  // combine_partials_kernel.
+  // Items are claimed in order from *claim by the CTAs as they go (one
+  // failing claim per CTA ends its stream); the last CTA to finish resets
+  // claim, exit_cnt and dn_done to zero for the next launch.
+  int* claim;
+  int* exit_cnt;
+  // fuse_combine: every down item adds 1 to *dn_done once its partial rows
+  // are stored; when all are, the CTAs sum y[t] = sum_j w[t, j] *
+  // partial[pos(t, j)] for their share of the tokens, in slot order with the
+  // rounding of combine_partials_kernel.
   int fuse_combine;
-  int* comb_cnt;
+  int* dn_done;
   const int32_t* sorted_slot;  // slot at every sorted position
   const int32_t* pos_of_slot;  // sorted position of every slot (-1: dropped)
   const void* topk_w;
@@ -233,12 +236,27 @@ __device__ __forceinline__ void fence_proxy_async_global() {
   asm volatile("fence.proxy.async.global;\n" ::: "memory");
 }
 
-// The CTA's li-th work item (global index `item`): from the shared table for
-// the first kItemTab, else from global memory.  False for an unknown tier.
-__device__ __forceinline__ bool decode_item(const TcParams& p, const Item* tab, int li, int item,
-                                            int n_tiles, Item& it) {
-  it = li < kItemTab ? tab[li] : make_item(p, item, n_tiles);
-  return it.tier == kTierINT4 || it.tier == kTierINT8 || it.tier == kTierBF16;
+__device__ __forceinline__ bool tier_ok(int tier) {
+  return tier == kTierINT4 || tier == kTierINT8 || tier == kTierBF16;
+}
+
+// Bounded acquire-spin until *ctr >= target that gives up only after about
+// 2 s without progress (the counter grows while other CTAs work).
+__device__ __forceinline__ bool wait_progress(const int* ctr, int target, uint32_t* status) {
+  int v, last = -1;
+  long long t0 = clock64();
+  for (;;) {
+    asm volatile("ld.acquire.gpu.global.b32 %0, [%1];\n" : "=r"(v) : "l"(ctr) : "memory");
+    if (v >= target) return true;
+    if (v != last) {
+      last = v;
+      t0 = clock64();
+    } else if (clock64() - t0 > 4000000000LL) {
+      atomicOr(status, EXQ_DEV_TIMEOUT);
+      return false;
+    }
+    __nanosleep(256);
+  }
 }
 
 struct Ring {
@@ -421,9 +439,9 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
   auto B_empty = [&](int i) { return bar0 + 8u * (kBarB + kBStages + i); };
   auto Acc_full = [&](int i) { return bar0 + 8u * (kBarAcc + i); };
   auto Acc_empty = [&](int i) { return bar0 + 8u * (kBarAcc + 2 + i); };
-  constexpr int kBarCmb = kBarAcc + 4;
-  auto Cmb_full = [&](int i) { return bar0 + 8u * (kBarCmb + i); };
-  auto Cmb_empty = [&](int i) { return bar0 + 8u * (kBarCmb + kCmbRing + i); };
+  constexpr int kBarIr = kBarAcc + 4;
+  auto IR_full = [&](int i) { return bar0 + 8u * (kBarIr + i); };
+  auto IR_empty = [&](int i) { return bar0 + 8u * (kBarIr + kItemRing + i); };
   volatile uint32_t* misc = reinterpret_cast<volatile uint32_t*>(gbase + kOffMisc);
   // misc[0] = TMEM base address, misc[1] = abort flag
 
@@ -446,9 +464,9 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
       mbar_init(Acc_full(i), 1);
       mbar_init(Acc_empty(i), kNumEpiWarps);
     }
-    for (int i = 0; i < kCmbRing; ++i) {
-      mbar_init(Cmb_full(i), kNumEpiWarps);
-      mbar_init(Cmb_empty(i), 1);
+    for (int i = 0; i < kItemRing; ++i) {
+      mbar_init(IR_full(i), 1);
+      mbar_init(IR_empty(i), kItemConsumers);
     }
     misc[1] = 0;
     mbar_fence_init();
@@ -483,16 +501,17 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
   const bool early = p.weights_early || p.tiles_from_ids;
   if (!early) pdl_wait();
   pdl_trigger();
-  Item* items_tab = reinterpret_cast<Item*>(gbase + kOffItems);
+  Item* iring = reinterpret_cast<Item*>(gbase + kOffItems);  // [kItemRing]
+  // per-expert tables of the tile list built from the ids (tiles_from_ids)
+  int* cnt = reinterpret_cast<int*>(gbase + kOffHist);
+  int* rbase = cnt + kHistBuckets + 1;
+  int* tstart = rbase + kHistBuckets + 1;
+  const int nbk = p.n_buckets;
   int n_tiles;
   if (p.tiles_from_ids) {
     // The same tile list the routing kernel writes: experts in order, rows in
     // tiles of kMaxN from each expert's first sorted position.  Per-expert
     // counts (an order-independent histogram), then two exclusive scans.
-    int* cnt = reinterpret_cast<int*>(gbase + kOffHist);
-    int* rbase = cnt + kHistBuckets + 1;
-    int* tstart = rbase + kHistBuckets + 1;
-    const int nbk = p.n_buckets;
     for (int i = threadIdx.x; i < nbk; i += kThreads) cnt[i] = 0;
     __syncthreads();
     for (int i = threadIdx.x; i < p.n_slots; i += kThreads) {
@@ -535,11 +554,18 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
     }
     __syncthreads();
     n_tiles = min(tstart[nbk], p.max_tiles);
-    const int n_items0 = num_items(p, n_tiles);
-    for (int t = threadIdx.x; t < kItemTab; t += kThreads) {
-      const int item = static_cast<int>(blockIdx.x) + t * static_cast<int>(gridDim.x);
-      if (item >= n_items0) continue;
-      Item it;
+  } else {
+    n_tiles = min(__ldcg(p.n_tiles_ptr), p.max_tiles);
+  }
+  const int n_items = num_items(p, n_tiles);
+  __syncthreads();
+  auto aborted = [&]() { return misc[1] != 0; };
+  auto do_abort = [&]() { misc[1] = 1; };
+  // Global item `item`: from the shared tables (tiles_from_ids) or the
+  // routing kernel's tile list.
+  auto decode = [&](int item) {
+    Item it;
+    if (p.tiles_from_ids) {
       item_coords(p, item, n_tiles, it.prj, it.tile, it.nb);
       int lo = 0, hi = nbk - 1;  // last expert whose first tile is <= tile
       while (lo < hi) {
@@ -552,34 +578,59 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
       it.m0 = rbase[lo] + lt * kMaxN;
       it.mc = min(kMaxN, cnt[lo] - lt * kMaxN);
       finish_item(p, it);
-      items_tab[t] = it;
+    } else {
+      it = make_item(p, item, n_tiles);
     }
-  } else {
-    n_tiles = min(__ldcg(p.n_tiles_ptr), p.max_tiles);
-    // decode this CTA's items once, so no role waits on global loads at an item boundary
-    const int n_items0 = num_items(p, n_tiles);
-    for (int t = threadIdx.x; t < kItemTab; t += kThreads) {
-      const int item = static_cast<int>(blockIdx.x) + t * static_cast<int>(gridDim.x);
-      if (item < n_items0) items_tab[t] = make_item(p, item, n_tiles);
+    return it;
+  };
+  // The next item of this CTA from the item ring (whole warp): 0 an item,
+  // 1 the end of the stream, 2 a wait that ran out.
+  auto next_item = [&](Ring& q, Item& it) -> int {
+    const bool got = __all_sync(0xffffffffu, mbar_wait(IR_full(q.idx), q.phase, p.status));
+    int st = 2;
+    if (got) {
+      it = iring[q.idx];
+      st = it.prj < 0 ? 1 : 0;
     }
-  }
-  const int n_items = num_items(p, n_tiles);
-  __syncthreads();
-  auto aborted = [&]() { return misc[1] != 0; };
-  auto do_abort = [&]() { misc[1] = 1; };
+    __syncwarp();
+    if (lane == 0 && got) mbar_arrive(IR_empty(q.idx));
+    q.next(kItemRing);
+    return st;
+  };
 
   if (warp == kWarpW) {
     // ---------------------------------------------------------- weights
-    // The whole warp walks the loop (waits are uniform); one elected lane
-    // issues, which keeps the issue path on the warp-uniform datapath.
-    Ring r;
+    // Claims the CTA's items one at a time from the global counter (so the
+    // CTAs share the work as they go), hands each to the other roles through
+    // the item ring and streams its weights.  The whole warp walks the loop
+    // (waits are uniform); one elected lane issues.
+    Ring r, qi;
     int issued = 0;
-    for (int item = blockIdx.x, li = 0; item < n_items && !aborted(); item += gridDim.x, ++li) {
+    for (;;) {
+      int item = 0;
+      if (lane == 0) item = atomicAdd(p.claim, 1);
+      item = __shfl_sync(0xffffffffu, item, 0);
+      const bool more = item < n_items && !aborted();
       Item it;
-      if (!decode_item(p, items_tab, li, item, n_tiles, it)) {
-        if (lane == 0) atomicOr(p.status, EXQ_DEV_BAD_TIER);
-        continue;
+      it.prj = -1;  // the end of the stream
+      if (more) {
+        it = decode(item);
+        if (!tier_ok(it.tier)) {
+          if (lane == 0) atomicOr(p.status, EXQ_DEV_BAD_TIER);
+          continue;
+        }
       }
+      if (!__all_sync(0xffffffffu, mbar_wait(IR_empty(qi.idx), qi.phase ^ 1, p.status))) {
+        do_abort();
+        break;
+      }
+      if (lane == 0) {
+        iring[qi.idx] = it;
+        mbar_arrive(IR_full(qi.idx));
+      }
+      __syncwarp();
+      qi.next(kItemRing);
+      if (!more) break;
       const ProjParams& pj = p.pj[it.prj];
       const int G = pj.k >> 7;
       const int nk = pj.k / kKS;
@@ -632,11 +683,13 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
   } else if (warp == kWarpB) {
     // ---------------------------------------------------------- activations
     if (early) pdl_wait();
-    Ring r;
+    Ring r, qi;
     int issued = 0;
-    for (int item = blockIdx.x, li = 0; item < n_items && !aborted(); item += gridDim.x, ++li) {
+    for (;;) {
       Item it;
-      if (!decode_item(p, items_tab, li, item, n_tiles, it)) continue;
+      const int st = next_item(qi, it);
+      if (st == 2) do_abort();
+      if (st != 0 || aborted()) break;
       const ProjParams& pj = p.pj[it.prj];
       const int nk = pj.k / kKS;
       const int per_slot = it.per_slot;
@@ -690,12 +743,14 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
     // ---------------------------------------------------------- MMA issue
     // Converged warp; the elected lane issues each group of 4 MMAs (K = 64)
     // and the commits.  The k-stages of one weight slot are unrolled per tier.
-    Ring ra, rb;
+    Ring ra, rb, qi;
     int count = 0;
     const uint64_t bdesc0 = smem_desc_sw128(sB);
-    for (int item = blockIdx.x, li = 0; item < n_items && !aborted(); item += gridDim.x, ++li) {
+    for (;;) {
       Item it;
-      if (!decode_item(p, items_tab, li, item, n_tiles, it)) continue;
+      const int st = next_item(qi, it);
+      if (st == 2) do_abort();
+      if (st != 0 || aborted()) break;
       const int ab = count & 1;
       const uint32_t acc_phase = (count >> 1) & 1;
       ++count;
@@ -744,15 +799,17 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
     const int quarter = warp & 3;  // TMEM lanes 32*quarter .. +31
     const int row = 32 * quarter + lane;
     const int et = static_cast<int>(threadIdx.x) - 32 * kEpiWarp0;  // 0..127
-    int count = 0, dcount = 0;
+    int count = 0;
+    Ring qi;
     // The four warps take every decision together (the named barriers below
-    // need all 128 threads): the loop bound and the abort test are agreed at
-    // the barrier after each accumulator wait.
-    for (int item = blockIdx.x, li = 0; item < n_items; item += gridDim.x, ++li, ++count) {
+    // need all 128 threads): the end of the stream and the abort test are
+    // agreed at a barrier after each item-ring and accumulator wait.
+    for (;; ++count) {
       Item it;
-      if (!decode_item(p, items_tab, li, item, n_tiles, it)) {
-        --count;
-        continue;
+      const int st = next_item(qi, it);
+      if (named_barrier_or(kEpiBar, 128, st != 0)) {
+        if (st == 2) do_abort();
+        break;
       }
       const ProjParams& pj = p.pj[it.prj];
       const int ab = count & 1;
@@ -818,152 +875,20 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(Acc_empty(ab));
-      if (pj.gate_up && p.link) {
-        // this row block of the tile's mid rows is stored: count it for the
-        // down items of the tile (their TMA loads read mid)
-        fence_proxy_async_global();
+      if (pj.gate_up ? p.link : p.fuse_combine) {
+        // gate_up: this row block of the tile's mid rows is stored, for the
+        // down items of the tile (their TMA loads read mid); down: one more
+        // item's partial rows are stored, for the combine
+        if (pj.gate_up) fence_proxy_async_global();
         named_barrier(kEpiBar, 128);
         if (et == 0) {
           __threadfence();
-          atomicAdd(p.tile_done + it.tile, 1);
+          atomicAdd(pj.gate_up ? p.tile_done + it.tile : p.dn_done, 1);
         }
-      } else if (!pj.gate_up && p.fuse_combine) {
-        // hand the item to the combine warp once its partial rows are stored
-        const uint32_t ci = dcount % kCmbRing, ph = (dcount / kCmbRing) & 1;
-        ++dcount;
-        const bool free_slot = mbar_wait(Cmb_empty(ci), ph ^ 1, p.status);
-        if (!__all_sync(0xffffffffu, free_slot)) do_abort();  // agreed at the next item's barrier
-        __syncwarp();
-        if (lane == 0) mbar_arrive(Cmb_full(ci));
       }
     }
   } else if (warp >= kWarpCmb0 && warp < kWarpCmb0 + kNumCmb) {
-    // ---------------------------------------------------------- fused top-k combine
-    // For every down item, once the epilogue has stored its rows' fp32
-    // partials: one arrival per row on the (token, 128-column block) counter,
-    // which the routing stage set to minus the token's valid slots; the row
-    // whose arrival brings it to zero makes this warp sum the token's
-    // partials in slot order (the other items' rows come from L2) and write y
-    // for the block.  Two warps take alternate down items, off the GEMM
-    // pipeline: the epilogue only waits for a free kCmbRing hand-off entry.
-    if (p.fuse_combine) {
-      const int cw = warp - kWarpCmb0;
-      pdl_wait();  // pos_of_slot / sorted_slot come from the routing kernel
-      // a token none of whose slots has an expert gets no arrival: zero row
-      const int64_t n_tok = p.n_slots / p.spt;
-      for (int64_t t = (static_cast<int64_t>(blockIdx.x) * kNumCmb + cw) * 32 + lane; t < n_tok;
-           t += static_cast<int64_t>(gridDim.x) * kNumCmb * 32) {
-        int need = 0;
-        for (int j = 0; j < p.spt; ++j) need += __ldcg(p.pos_of_slot + t * p.spt + j) >= 0;
-        if (need == 0) {
-          uint4* yrow = reinterpret_cast<uint4*>(static_cast<__half*>(p.y) + t * p.hidden);
-          for (int64_t c = 0; c < p.hidden / 8; ++c) yrow[c] = make_uint4(0, 0, 0, 0);
-        }
-      }
-      int* spos = reinterpret_cast<int*>(gbase + kOffCmb + cw * kCmbWarpBytes);  // [kMaxN][kCmbMaxSpt]
-      float* sw = reinterpret_cast<float*>(spos + kMaxN * kCmbMaxSpt);
-      const int nhb = static_cast<int>(p.hidden >> 7);
-      const int spt = p.spt;
-      const float* part = static_cast<const float*>(p.pj[1].out);
-      const int64_t stride = p.pj[1].out_stride;
-      int dc = 0;
-      for (int item = blockIdx.x, li = 0; item < n_items; item += gridDim.x, ++li) {
-        Item it;
-        if (!decode_item(p, items_tab, li, item, n_tiles, it) || it.prj != 1) continue;
-        const int d = dc++;
-        if (d % kNumCmb != cw) continue;
-        const uint32_t ci = d % kCmbRing, ph = (d / kCmbRing) & 1;
-        // rows lane and lane + 32: their tokens (loaded before the wait)
-        int tok[2];
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          const int c = lane + 32 * h;
-          tok[h] = c < it.mc ? __ldcg(p.sorted_slot + it.m0 + c) / spt : -1;
-        }
-        const bool got = !aborted() && mbar_wait(Cmb_full(ci), ph, p.status);
-        if (!__all_sync(0xffffffffu, got)) {
-          do_abort();
-          break;
-        }
-        // the epilogue's partial stores (ordered before its arrivals) become
-        // visible device-wide before this warp's counter arrivals
-        __threadfence();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(Cmb_empty(ci));
-        int old[2];
-#pragma unroll
-        for (int h = 0; h < 2; ++h)
-          old[h] = tok[h] >= 0 ? atomicAdd(p.comb_cnt + tok[h] * nhb + it.nb, 1) : 0;
-        const uint64_t mask = static_cast<uint64_t>(__ballot_sync(0xffffffffu, old[0] == -1)) |
-                              (static_cast<uint64_t>(__ballot_sync(0xffffffffu, old[1] == -1)) << 32);
-        if (!mask) continue;
-        __threadfence();  // acquire the other items' partial rows of these tokens
-        // slot positions and router weights of the finishing rows, all loads in flight
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          if (old[h] != -1) continue;
-          const int c = lane + 32 * h;
-          int r[kCmbMaxSpt];
-          float wv[kCmbMaxSpt];
-#pragma unroll
-          for (int j = 0; j < kCmbMaxSpt; ++j) {
-            r[j] = j < spt ? __ldcg(p.pos_of_slot + tok[h] * spt + j) : -1;
-            wv[j] = j < spt ? (j < p.top_k ? load_as_f32(p.topk_w, p.w_dtype,
-                                                         static_cast<int64_t>(tok[h]) * p.top_k + j)
-                                           : 1.0f)
-                            : 0.f;
-          }
-#pragma unroll
-          for (int j = 0; j < kCmbMaxSpt; ++j) {
-            spos[c * kCmbMaxSpt + j] = r[j];
-            sw[c * kCmbMaxSpt + j] = wv[j];
-          }
-        }
-        __syncwarp();
-        // lane: 4 consecutive columns of the 128-column block
-        const int col = it.r0 + 4 * lane;
-        uint64_t left = mask;
-        while (left) {
-          const int c = __ffsll(static_cast<long long>(left)) - 1;
-          left &= left - 1;
-          const int t = __shfl_sync(0xffffffffu, c < 32 ? tok[0] : tok[1], c & 31);
-          float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-          // the sum of combine_partials_kernel: slot order, product and sum
-          // rounded separately, padded to a multiple of 8 slots with 0 * 0
-          for (int j0 = 0; j0 < spt; j0 += 8) {
-            float4 v[8];
-            float wj[8];
-#pragma unroll
-            for (int u = 0; u < 8; ++u) {
-              const int j = j0 + u;
-              const int r = j < spt ? spos[c * kCmbMaxSpt + j] : -1;
-              wj[u] = j < spt ? sw[c * kCmbMaxSpt + j] : 0.f;
-              v[u] = r >= 0 ? __ldcg(reinterpret_cast<const float4*>(part + r * stride + col))
-                            : make_float4(0.f, 0.f, 0.f, 0.f);
-            }
-#pragma unroll
-            for (int u = 0; u < 8; ++u) {
-              acc.x = __fadd_rn(acc.x, __fmul_rn(wj[u], v[u].x));
-              acc.y = __fadd_rn(acc.y, __fmul_rn(wj[u], v[u].y));
-              acc.z = __fadd_rn(acc.z, __fmul_rn(wj[u], v[u].z));
-              acc.w = __fadd_rn(acc.w, __fmul_rn(wj[u], v[u].w));
-            }
-          }
-          const int64_t yo = static_cast<int64_t>(t) * p.hidden + col;
-          uint2 packed;
-          if (p.y_dtype == EXQ_F16) {
-            __half2 lo = __floats2half2_rn(acc.x, acc.y), hi = __floats2half2_rn(acc.z, acc.w);
-            packed = make_uint2(*reinterpret_cast<uint32_t*>(&lo), *reinterpret_cast<uint32_t*>(&hi));
-          } else {
-            __nv_bfloat162 lo = __floats2bfloat162_rn(acc.x, acc.y),
-                           hi = __floats2bfloat162_rn(acc.z, acc.w);
-            packed = make_uint2(*reinterpret_cast<uint32_t*>(&lo), *reinterpret_cast<uint32_t*>(&hi));
-          }
-          *reinterpret_cast<uint2*>(static_cast<__half*>(p.y) + yo) = packed;
-        }
-        __syncwarp();  // the staging rows are read before the next item rewrites them
-      }
-    }
+    // combine warps: nothing during the items (the combine below)
   } else {
     // ---------------------------------------------------------- dequant
     // Group g = (warp - kDqWarp0) / 4 converts weight slots gs = g, g+3, ...
@@ -975,9 +900,12 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
     const uint32_t abuf = tmem + tlane + kTmemA + grp * kACols;
     const uint32_t a_empty = A_empty(grp), a_full = A_full(grp);
     uint32_t gs = 0;  // global slot counter of this CTA
-    for (int item = blockIdx.x, li = 0; item < n_items && !aborted(); item += gridDim.x, ++li) {
+    Ring qi;
+    for (;;) {
       Item it;
-      if (!decode_item(p, items_tab, li, item, n_tiles, it)) continue;
+      const int st = next_item(qi, it);
+      if (st == 2) do_abort();
+      if (st != 0 || aborted()) break;
       const int nk = p.pj[it.prj].k / kKS;
       const int sps = it.sps;
       // gate_up interleaves gate/up rows in blocks of 8 (the epilogue pairs lanes m, m^8)
@@ -1047,12 +975,97 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
     }
   }
 
+  if (p.fuse_combine && warp >= kTailWarp0) {
+    // ---------------------------------------------------------- top-k combine
+    // Once every down item of the launch has stored its partial rows, the
+    // epilogue, dequant and combine warps of every CTA sum this CTA's share
+    // of the tokens: y[t] = sum_j w[t, j] * partial[pos(t, j)], slot order,
+    // product and sum rounded separately (a dropped slot adds 0 * w), exactly
+    // as combine_partials_kernel.  Warp kWarpCmb0 waits; the others agree at
+    // a barrier.
+    const int tt = static_cast<int>(threadIdx.x) - 32 * kTailWarp0;
+    const int wk = warp - kTailWarp0;
+    bool ok = true;
+    if (warp == kWarpCmb0) {
+      const int n_down = p.run_dn ? n_tiles * p.pj[1].nblocks : 0;
+      if (lane == 0) ok = wait_progress(p.dn_done, n_down, p.status);
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+    }
+    if (!named_barrier_or(kTailBar, 32 * kTailWarps, !ok || aborted())) {
+      pdl_wait();  // pos_of_slot comes from the routing kernel
+      int seen;    // the other CTAs' partial rows (their counts were acquired above)
+      asm volatile("ld.acquire.gpu.global.b32 %0, [%1];\n" : "=r"(seen) : "l"(p.dn_done) : "memory");
+      (void)seen;
+      const int spt = p.spt;
+      const int n_tok = static_cast<int>(p.n_slots / spt);
+      const int tpc = (n_tok + static_cast<int>(gridDim.x) - 1) / static_cast<int>(gridDim.x);
+      const int t0 = min(n_tok, static_cast<int>(blockIdx.x) * tpc), t1 = min(n_tok, t0 + tpc);
+      int* spos = reinterpret_cast<int*>(gbase + kOffCmb);  // [tokens of this CTA][spt]
+      float* sw = reinterpret_cast<float*>(spos + kCmbEntries);
+      for (int i = tt; i < (t1 - t0) * spt; i += 32 * kTailWarps) {
+        const int t = t0 + i / spt, j = i - (i / spt) * spt;
+        spos[i] = __ldcg(p.pos_of_slot + static_cast<int64_t>(t) * spt + j);
+        sw[i] = j < p.top_k ? load_as_f32(p.topk_w, p.w_dtype, static_cast<int64_t>(t) * p.top_k + j)
+                            : 1.0f;
+      }
+      named_barrier(kTailBar, 32 * kTailWarps);
+      const int nhb = static_cast<int>(p.hidden >> 7);
+      const float* part = static_cast<const float*>(p.pj[1].out);
+      const int64_t stride = p.pj[1].out_stride;
+      for (int q = wk; q < (t1 - t0) * nhb; q += kTailWarps) {
+        const int tl = q / nhb, col = (q - tl * nhb) * 128 + 4 * lane;
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int j0 = 0; j0 < spt; j0 += 8) {
+          float4 v[8];
+          float wj[8];
+#pragma unroll
+          for (int u = 0; u < 8; ++u) {
+            const int j = j0 + u;
+            const int r = j < spt ? spos[tl * spt + j] : -1;
+            wj[u] = j < spt ? sw[tl * spt + j] : 0.f;
+            v[u] = r >= 0 ? __ldcg(reinterpret_cast<const float4*>(part + r * stride + col))
+                          : make_float4(0.f, 0.f, 0.f, 0.f);
+          }
+#pragma unroll
+          for (int u = 0; u < 8; ++u) {
+            acc.x = __fadd_rn(acc.x, __fmul_rn(wj[u], v[u].x));
+            acc.y = __fadd_rn(acc.y, __fmul_rn(wj[u], v[u].y));
+            acc.z = __fadd_rn(acc.z, __fmul_rn(wj[u], v[u].z));
+            acc.w = __fadd_rn(acc.w, __fmul_rn(wj[u], v[u].w));
+          }
+        }
+        const int64_t yo = static_cast<int64_t>(t0 + tl) * p.hidden + col;
+        uint2 packed;
+        if (p.y_dtype == EXQ_F16) {
+          __half2 lo = __floats2half2_rn(acc.x, acc.y), hi = __floats2half2_rn(acc.z, acc.w);
+          packed = make_uint2(*reinterpret_cast<uint32_t*>(&lo), *reinterpret_cast<uint32_t*>(&hi));
+        } else {
+          __nv_bfloat162 lo = __floats2bfloat162_rn(acc.x, acc.y),
+                         hi = __floats2bfloat162_rn(acc.z, acc.w);
+          packed = make_uint2(*reinterpret_cast<uint32_t*>(&lo), *reinterpret_cast<uint32_t*>(&hi));
+        }
+        *reinterpret_cast<uint2*>(static_cast<__half*>(p.y) + yo) = packed;
+      }
+    }
+  }
+
   // producer / MMA warps arrive here diverged (only lane 0 worked)
   cta_barrier_unaligned();
   if (warp == kWarpMma) {
     __syncwarp();
     tc_fence_after();
     tmem_dealloc(tmem, kTmemCols);
+  }
+  if (threadIdx.x == 0) {
+    // the last CTA to finish leaves the claim and combine counters at zero
+    // for the next launch on this workspace
+    __threadfence();
+    if (atomicAdd(p.exit_cnt, 1) == static_cast<int>(gridDim.x) - 1) {
+      *reinterpret_cast<volatile int*>(p.claim) = 0;
+      *reinterpret_cast<volatile int*>(p.dn_done) = 0;
+      __threadfence();
+      *reinterpret_cast<volatile int*>(p.exit_cnt) = 0;
+    }
   }
 }
 
@@ -1313,13 +1326,13 @@ struct TcWs {
   int32_t* ends;
   int32_t* tile_info;
   int32_t* n_tiles;
-  int32_t* tile_done;  // [max_tiles] gate_up row blocks stored per tile
-  int32_t* comb_cnt;   // [n_tokens * hidden/128] fused-combine arrivals (start: -valid slots)
+  int32_t* tile_done;  // [max_tiles] gate_up row blocks stored per tile, then the claim,
+                       // exit and stored-down-item counters (all zeroed by the route stage)
   __half* act;
   __half* mid;
   float* partial;
   int64_t max_tiles;
-  int64_t n_counters;  // ints in tile_done + comb_cnt (one contiguous run)
+  int64_t n_counters;  // ints from tile_done on (one contiguous run)
   size_t bytes;
 };
 
@@ -1339,9 +1352,9 @@ TcWs carve_tc(void* base, int64_t n_slots, int64_t n_tokens, int n_buckets, int6
   w.ends = reinterpret_cast<int32_t*>(take(4 * (n_buckets + 1)));
   w.tile_info = reinterpret_cast<int32_t*>(take(12 * w.max_tiles));
   w.n_tiles = reinterpret_cast<int32_t*>(take(16));
-  w.n_counters = w.max_tiles + n_tokens * (hidden / 128);
+  (void)n_tokens;
+  w.n_counters = w.max_tiles + 3;
   w.tile_done = reinterpret_cast<int32_t*>(take(4 * w.n_counters));
-  w.comb_cnt = w.tile_done ? w.tile_done + w.max_tiles : nullptr;
   w.act = reinterpret_cast<__half*>(take(2 * n_slots * hidden));
   w.mid = reinterpret_cast<__half*>(take(2 * n_slots * inter));
   w.partial = reinterpret_cast<float*>(take(4 * n_slots * hidden));
@@ -1438,10 +1451,13 @@ extern "C" int exq_moe_layer_forward_range(const exq_moe_weights* w, const void*
   // combine too, the down items sum each token's slots (no separate combine)
   const bool do_gu = first_stage <= 2 && end_stage > 2;
   const bool do_dn = first_stage <= 3 && end_stage > 3;
-  const bool fuse_combine =
-      do_dn && first_stage <= 4 && end_stage > 4 && spt <= tc::kCmbMaxSpt;
   // decode-sized calls route and gather in one kernel (stage 0; stage 1 is empty)
   const bool fused = n_slots <= kRouteGatherMaxSlots && n_total <= kRouteGatherMaxBuckets;
+  // decode-sized calls: the GEMM launch also does the combine (its CTAs split
+  // the tokens once every down item is stored); larger ones launch it apart
+  const bool fuse_combine = do_dn && first_stage <= 4 && end_stage > 4 && fused &&
+                            spt <= tc::kCmbMaxSpt &&
+                            ((n_tokens + num_sms() - 1) / num_sms() + 1) * spt <= tc::kCmbEntries;
   if (fused && first_stage <= 0 && end_stage > 0) {
     RouteGatherParams rg{};
     rg.ids = topk_ids;
@@ -1466,8 +1482,7 @@ extern "C" int exq_moe_layer_forward_range(const exq_moe_weights* w, const void*
     rg.max_tiles = ws.max_tiles;
     rg.sorted_slot = ws.sorted_slot;
     rg.counters = ws.tile_done;
-    rg.n_tile_counters = ws.max_tiles;
-    rg.comb_blocks = static_cast<int>(H / 128);
+    rg.n_counters = ws.n_counters;
     st = launch_route_gather(rg, s, chained);
     if (st != EXQ_OK) return st;
     chained = true;
@@ -1492,8 +1507,7 @@ extern "C" int exq_moe_layer_forward_range(const exq_moe_weights* w, const void*
     rp.n_tiles = ws.n_tiles;
     rp.max_tiles = ws.max_tiles;
     rp.counters = ws.tile_done;
-    rp.n_tile_counters = ws.max_tiles;
-    rp.comb_blocks = static_cast<int>(H / 128);
+    rp.n_counters = ws.n_counters;
     st = launch_route(rp, kRouteLayer, s, chained);
     if (st != EXQ_OK) return st;
     chained = true;
@@ -1521,8 +1535,10 @@ extern "C" int exq_moe_layer_forward_range(const exq_moe_weights* w, const void*
     p.run_dn = do_dn;
     p.link = do_gu && do_dn;
     p.tile_done = ws.tile_done;
+    p.claim = ws.tile_done + ws.max_tiles;
+    p.exit_cnt = ws.tile_done + ws.max_tiles + 1;
     p.fuse_combine = fuse_combine;
-    p.comb_cnt = ws.comb_cnt;
+    p.dn_done = ws.tile_done + ws.max_tiles + 2;
     p.sorted_slot = ws.sorted_slot;
     p.pos_of_slot = ws.pos_of_slot;
     p.topk_w = topk_weights;
@@ -1540,10 +1556,9 @@ extern "C" int exq_moe_layer_forward_range(const exq_moe_weights* w, const void*
     const int64_t per_tile = (do_gu ? I / 64 : 0) + (do_dn ? H / 128 : 0);
     const int64_t max_items = ws.max_tiles * per_tile;
     const int64_t grid = max_items < num_sms() ? max_items : num_sms();
-    // a CTA can build its items from the ids: the experts fit the histogram and
-    // every CTA's items fit its shared table
-    const bool ids_ok = n_total <= tc::kHistBuckets &&
-                        max_items <= static_cast<int64_t>(tc::kItemTab) * (grid > 0 ? grid : 1);
+    // a CTA can build its items from the ids: the experts fit the histogram
+    const bool ids_ok = n_total <= tc::kHistBuckets;
+    (void)grid;
     if (fused && first_stage == 0) {
       // right after the fused routing of this call: build the tiles from the
       // ids (complete before routing started) and stream weights at once;

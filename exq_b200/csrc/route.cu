@@ -186,21 +186,8 @@ __global__ void __launch_bounds__(kRouteThreads, 1) route_kernel(RouteParams p, 
     }
   }
   if (mode == kRouteLayer) {
-    // the GEMM's tile counters start at zero, its combine counters at minus
-    // the token's valid slots (the last arrival brings one to zero)
-    for (int64_t i = threadIdx.x; i < p.n_tile_counters; i += kRouteThreads) p.counters[i] = 0;
-    if (p.comb_blocks > 0) {
-      const int64_t n_tok = p.n / p.slots_per_token;
-      int32_t* comb = p.counters + p.n_tile_counters;
-      for (int64_t t = threadIdx.x; t < n_tok; t += kRouteThreads) {
-        int need = p.slots_per_token - p.top_k;  // shared experts
-        for (int j = 0; j < p.top_k; ++j) {
-          const int64_t e = load_index(p.ids, p.ids_dtype, t * p.top_k + j);
-          need += (e >= 0 && e < p.n_routed);
-        }
-        for (int b = 0; b < p.comb_blocks; ++b) comb[t * p.comb_blocks + b] = -need;
-      }
-    }
+    // the GEMM's tile and work counters start at zero
+    for (int64_t i = threadIdx.x; i < p.n_counters; i += kRouteThreads) p.counters[i] = 0;
     // positions past the routed total (slots dropped for a bad expert id) hold -1
     for (int64_t i = carry + threadIdx.x; i < p.n; i += kRouteThreads) {
       p.sorted_i32[i] = -1;

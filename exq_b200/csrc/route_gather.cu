@@ -210,20 +210,10 @@ __global__ void __launch_bounds__(kRgThreads) route_gather_kernel(const RouteGat
       if (p.sorted_slot) p.sorted_slot[pos] = i;
     }
   }
-  // the GEMM's tile counters start at zero, its combine counters at minus
-  // the token's valid slots (the last arrival brings one to zero)
-  for (int64_t i = static_cast<int64_t>(blockIdx.x) * kRgThreads + threadIdx.x;
-       i < p.n_tile_counters; i += static_cast<int64_t>(gridDim.x) * kRgThreads)
+  // the GEMM's tile and work counters start at zero
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * kRgThreads + threadIdx.x; i < p.n_counters;
+       i += static_cast<int64_t>(gridDim.x) * kRgThreads)
     p.counters[i] = 0;
-  if (p.comb_blocks > 0) {
-    const int n_tok = n / p.spt;
-    int32_t* comb = p.counters + p.n_tile_counters;
-    for (int t = blockIdx.x * kRgThreads + threadIdx.x; t < n_tok; t += gridDim.x * kRgThreads) {
-      int need = 0;
-      for (int j = 0; j < p.spt; ++j) need += bkt[t * p.spt + j] >= 0;
-      for (int b = 0; b < p.comb_blocks; ++b) comb[static_cast<int64_t>(t) * p.comb_blocks + b] = -need;
-    }
-  }
   // row copies, slot by slot: each thread issues 8 independent 16-byte loads
   // before storing
   const int octs = static_cast<int>(p.hidden_size / 8);
