@@ -1320,14 +1320,16 @@ namespace {
 constexpr int kLayerMT = tc::kMaxN;  // tokens per GEMM tile (the MMA's N)
 
 struct TcWs {
+  int32_t* gemm_ctr;   // [2] item claims and exited CTAs of the GEMM launch: at offset 0,
+                       // zero before a call and after it (the launch's last CTA resets them)
   int32_t* sorted_slot;
   int32_t* pos_of_slot;
   float* sorted_w;
   int32_t* ends;
   int32_t* tile_info;
   int32_t* n_tiles;
-  int32_t* tile_done;  // [max_tiles] gate_up row blocks stored per tile, then the claim,
-                       // exit and stored-down-item counters (all zeroed by the route stage)
+  int32_t* tile_done;  // [max_tiles] gate_up row blocks stored per tile, then the count
+                       // of stored down items (zeroed by the route stage)
   __half* act;
   __half* mid;
   float* partial;
@@ -1346,6 +1348,7 @@ TcWs carve_tc(void* base, int64_t n_slots, int64_t n_tokens, int n_buckets, int6
     return base ? static_cast<char*>(base) + o : nullptr;
   };
   w.max_tiles = n_slots / kLayerMT + (n_slots < n_buckets ? n_slots : n_buckets) + 1;
+  w.gemm_ctr = reinterpret_cast<int32_t*>(take(8));
   w.sorted_slot = reinterpret_cast<int32_t*>(take(4 * n_slots));
   w.pos_of_slot = reinterpret_cast<int32_t*>(take(4 * n_slots));
   w.sorted_w = reinterpret_cast<float*>(take(4 * n_slots));
@@ -1353,7 +1356,7 @@ TcWs carve_tc(void* base, int64_t n_slots, int64_t n_tokens, int n_buckets, int6
   w.tile_info = reinterpret_cast<int32_t*>(take(12 * w.max_tiles));
   w.n_tiles = reinterpret_cast<int32_t*>(take(16));
   (void)n_tokens;
-  w.n_counters = w.max_tiles + 3;
+  w.n_counters = w.max_tiles + 1;
   w.tile_done = reinterpret_cast<int32_t*>(take(4 * w.n_counters));
   w.act = reinterpret_cast<__half*>(take(2 * n_slots * hidden));
   w.mid = reinterpret_cast<__half*>(take(2 * n_slots * inter));
@@ -1535,10 +1538,10 @@ extern "C" int exq_moe_layer_forward_range(const exq_moe_weights* w, const void*
     p.run_dn = do_dn;
     p.link = do_gu && do_dn;
     p.tile_done = ws.tile_done;
-    p.claim = ws.tile_done + ws.max_tiles;
-    p.exit_cnt = ws.tile_done + ws.max_tiles + 1;
+    p.claim = ws.gemm_ctr;
+    p.exit_cnt = ws.gemm_ctr + 1;
     p.fuse_combine = fuse_combine;
-    p.dn_done = ws.tile_done + ws.max_tiles + 2;
+    p.dn_done = ws.tile_done + ws.max_tiles;
     p.sorted_slot = ws.sorted_slot;
     p.pos_of_slot = ws.pos_of_slot;
     p.topk_w = topk_weights;

@@ -249,16 +249,21 @@ typedef struct exq_moe_weights {
 
 /* The whole MoE layer of exq/runtime/sglang_backend.py:65-158 (and
  * moe_int4_full_forward, moe_int4_kernel.py:330-426): route -> activation
- * prep (gather + fp16 + octet permutation) -> gate_up tcgen05 grouped GEMM with
- * fused SiLU*mul -> down tcgen05 grouped GEMM writing fp32 partials -> the
- * deterministic router-weighted top-k combine.  The experts may mix the three
- * tiers.  hidden_states/out: [n_tokens, hidden] (fp16 or bf16; the matrix
- * products run on fp16 operands with fp32 accumulation, as the reference's
- * kernel does); topk_ids [n_tokens, top_k] int32/int64, where a negative id
- * marks an unused slot (no expert) and an id >= n_routed is dropped and
- * flagged (EXQ_DEV_BAD_EXPERT_ID); topk_weights [n_tokens, top_k]
- * f32/f16/bf16.  Four launches up to 4096 slots (route and prep fused), five
- * above; no host synchronisation. */
+ * prep (gather + fp16 + octet permutation) -> one tcgen05 grouped-GEMM launch
+ * that runs gate_up with fused SiLU*mul, then down (each down tile starts when
+ * its gate_up row blocks are stored), and the deterministic router-weighted
+ * top-k combine.  The experts may mix the three tiers.
+ * hidden_states/out: [n_tokens, hidden] (fp16 or bf16; the matrix products
+ * run on fp16 operands with fp32 accumulation, as the reference's kernel
+ * does); topk_ids [n_tokens, top_k] int32/int64, where a negative id marks an
+ * unused slot (no expert) and an id >= n_routed is dropped and flagged
+ * (EXQ_DEV_BAD_EXPERT_ID); topk_weights [n_tokens, top_k] f32/f16/bf16.  Up
+ * to 4096 slots: two launches (route fused with prep; the GEMM launch with
+ * the combine at its end); above: route, prep, GEMM, combine.  No host
+ * synchronisation.  The workspace must be zero-filled before its first use
+ * and belongs to the library between calls on one stream: its first 256
+ * bytes hold the GEMM launch's work counters, which every call leaves at
+ * zero. */
 EXQ_API size_t exq_moe_layer_workspace_bytes(int64_t n_tokens, int32_t top_k, int32_t n_shared,
                                              int32_t n_experts_total, int64_t hidden,
                                              int64_t inter);
@@ -272,7 +277,9 @@ EXQ_API int exq_moe_layer_forward(const exq_moe_weights* weights, const void* hi
  * 0 = route (sort + tile list), 1 = activation prep, 2 = gate_up GEMM,
  * 3 = down GEMM, 4 = top-k combine.  Stages communicate through `workspace`,
  * so a caller may run them separately on one stream (per-kernel timing) with
- * identical arguments; exq_moe_layer_forward = stages [0, 5). */
+ * identical arguments, each stage once and in order after stage 0;
+ * exq_moe_layer_forward = stages [0, 5).  Stages 2 and 3 in one range are one
+ * launch; with stage 4 too (up to 4096 slots), the combine runs in it. */
 #define EXQ_LAYER_STAGES 5
 EXQ_API int exq_moe_layer_forward_range(const exq_moe_weights* weights,
                                         const void* hidden_states, int act_dtype,
