@@ -987,6 +987,9 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
     const int wk = warp - kTailWarp0;
     bool ok = true;
     if (warp == kWarpCmb0) {
+      // the count lives in this call's workspace layout: zeroed by the routing
+      // kernel, which may still be running (the location held other data)
+      pdl_wait();
       const int n_down = p.run_dn ? n_tiles * p.pj[1].nblocks : 0;
       if (lane == 0) ok = wait_progress(p.dn_done, n_down, p.status);
       ok = __shfl_sync(0xffffffffu, ok, 0);
