@@ -121,9 +121,10 @@ struct TcParams {
   // producer waits until all nb_gu row blocks of its tile have done so.
   int link;
   int* tile_done;
-  // Items are claimed in order from *claim by the CTAs as they go (one
-  // failing claim per CTA ends its stream); the last CTA to finish resets
-  // claim, exit_cnt and dn_done to zero for the next launch.
+  // A CTA's first item is blockIdx.x, its later ones gridDim.x + a value
+  // claimed from *claim as it goes (claims only grow, so every down item is
+  // claimed after the gate_up items it waits for); the last CTA to finish
+  // resets claim and exit_cnt to zero for the next launch.
   int* claim;
   int* exit_cnt;
   // fuse_combine: every down item adds 1 to *dn_done once its partial rows
@@ -219,8 +220,8 @@ __device__ __forceinline__ bool wait_count(const int* ctr, int target, uint32_t*
   asm volatile("ld.acquire.gpu.global.b32 %0, [%1];\n" : "=r"(v) : "l"(ctr) : "memory");
   if (v >= target) return true;
   const long long t0 = clock64();
-  for (;;) {
-    __nanosleep(128);
+  for (unsigned ns = 64;; ns = ns < 1024 ? 2 * ns : ns) {
+    __nanosleep(ns);  // backing off: every CTA polls one L2 line
     asm volatile("ld.acquire.gpu.global.b32 %0, [%1];\n" : "=r"(v) : "l"(ctr) : "memory");
     if (v >= target) return true;
     if (clock64() - t0 > 4000000000LL) {
@@ -255,7 +256,7 @@ __device__ __forceinline__ bool wait_progress(const int* ctr, int target, uint32
       atomicOr(status, EXQ_DEV_TIMEOUT);
       return false;
     }
-    __nanosleep(256);
+    __nanosleep(2048);  // a long wait, polled by every CTA: one L2 line
   }
 }
 
@@ -600,16 +601,23 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
 
   if (warp == kWarpW) {
     // ---------------------------------------------------------- weights
-    // Claims the CTA's items one at a time from the global counter (so the
-    // CTAs share the work as they go), hands each to the other roles through
-    // the item ring and streams its weights.  The whole warp walks the loop
+    // The CTA's first item is blockIdx.x; the next ones are claimed from the
+    // global counter (items gridDim.x + claim), so the CTAs share the work as
+    // they go.  Each claim is issued one item ahead, its result used only
+    // after the current item's weights are streamed.  Every item goes to the
+    // other roles through the item ring.  The whole warp walks the loop
     // (waits are uniform); one elected lane issues.
     Ring r, qi;
     int issued = 0;
+    int item = static_cast<int>(blockIdx.x);
+    int pend = 0;
+    if (lane == 0) pend = atomicAdd(p.claim, 1);
+    auto next_claim = [&]() {
+      const int c = __shfl_sync(0xffffffffu, pend, 0);
+      if (lane == 0) pend = atomicAdd(p.claim, 1);
+      return static_cast<int>(gridDim.x) + c;
+    };
     for (;;) {
-      int item = 0;
-      if (lane == 0) item = atomicAdd(p.claim, 1);
-      item = __shfl_sync(0xffffffffu, item, 0);
       const bool more = item < n_items && !aborted();
       Item it;
       it.prj = -1;  // the end of the stream
@@ -617,6 +625,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
         it = decode(item);
         if (!tier_ok(it.tier)) {
           if (lane == 0) atomicOr(p.status, EXQ_DEV_BAD_TIER);
+          item = next_claim();
           continue;
         }
       }
@@ -671,6 +680,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
         do_abort();
         break;
       }
+      item = next_claim();
     }
     if (aborted()) {  // let in-flight copies land before the CTA exits
       Ring q = r;
