@@ -256,7 +256,7 @@ __device__ __forceinline__ bool wait_progress(const int* ctr, int target, uint32
       atomicOr(status, EXQ_DEV_TIMEOUT);
       return false;
     }
-    __nanosleep(2048);  // a long wait, polled by every CTA: one L2 line
+    __nanosleep(512);  // a long wait, polled by one thread of every CTA: one L2 line
   }
 }
 
@@ -812,23 +812,20 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
     int count = 0;
     Ring qi;
     // The four warps take every decision together (the named barriers below
-    // need all 128 threads): the end of the stream and the abort test are
-    // agreed at a barrier after each item-ring and accumulator wait.
+    // need all 128 threads): the end of the stream (the same ring entry for
+    // all four) and the abort test are agreed at one barrier per item, after
+    // the accumulator wait.
     for (;; ++count) {
       Item it;
       const int st = next_item(qi, it);
-      if (named_barrier_or(kEpiBar, 128, st != 0)) {
-        if (st == 2) do_abort();
+      const int ab = count & 1;
+      const uint32_t acc_phase = (count >> 1) & 1;
+      const bool got = st == 0 && !aborted() && mbar_wait(Acc_full(ab), acc_phase, p.status);
+      if (named_barrier_or(kEpiBar, 128, !got)) {
+        if (st != 1) do_abort();
         break;
       }
       const ProjParams& pj = p.pj[it.prj];
-      const int ab = count & 1;
-      const uint32_t acc_phase = (count >> 1) & 1;
-      const bool got = !aborted() && mbar_wait(Acc_full(ab), acc_phase, p.status);
-      if (named_barrier_or(kEpiBar, 128, !got)) {
-        do_abort();
-        break;
-      }
       tc_fence_after();
       const uint32_t taddr = tmem + (static_cast<uint32_t>(32 * quarter) << 16) + ab * kMaxN;
       if (pj.gate_up) {
