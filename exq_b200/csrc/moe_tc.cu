@@ -123,8 +123,8 @@ struct TcParams {
   int* tile_done;
   // A CTA's first item is blockIdx.x, its later ones gridDim.x + a value
   // claimed from *claim as it goes (claims only grow, so every down item is
-  // claimed after the gate_up items it waits for); the last CTA to finish
-  // resets claim and exit_cnt to zero for the next launch.
+  // claimed after the gate_up items it waits for); the last CTA to stop
+  // claiming resets claim and exit_cnt to zero for the next launch.
   int* claim;
   int* exit_cnt;
   // fuse_combine: every down item adds 1 to *dn_done once its partial rows
@@ -682,6 +682,18 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
       }
       item = next_claim();
     }
+    if (lane == 0) {
+      // this CTA claims nothing more (its last claim has returned, the fence
+      // orders it before the count): the last CTA to get here leaves the
+      // claim counter at zero for the next launch on this workspace
+      (void)*reinterpret_cast<volatile int*>(&pend);
+      __threadfence();
+      if (atomicAdd(p.exit_cnt, 1) == static_cast<int>(gridDim.x) - 1) {
+        *reinterpret_cast<volatile int*>(p.claim) = 0;
+        __threadfence();
+        *reinterpret_cast<volatile int*>(p.exit_cnt) = 0;
+      }
+    }
     if (aborted()) {  // let in-flight copies land before the CTA exits
       Ring q = r;
       for (int i = 0; i < min(issued, kWStages); ++i) {
@@ -1065,17 +1077,6 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
     __syncwarp();
     tc_fence_after();
     tmem_dealloc(tmem, kTmemCols);
-  }
-  if (threadIdx.x == 0) {
-    // the last CTA to finish leaves the claim and combine counters at zero
-    // for the next launch on this workspace
-    __threadfence();
-    if (atomicAdd(p.exit_cnt, 1) == static_cast<int>(gridDim.x) - 1) {
-      *reinterpret_cast<volatile int*>(p.claim) = 0;
-      *reinterpret_cast<volatile int*>(p.dn_done) = 0;
-      __threadfence();
-      *reinterpret_cast<volatile int*>(p.exit_cnt) = 0;
-    }
   }
 }
 
