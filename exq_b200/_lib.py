@@ -149,10 +149,8 @@ def require_cuda(*tensors: torch.Tensor) -> torch.device:
 
 
 def workspace(device: torch.device, nbytes: int) -> torch.Tensor:
-    """Scratch from torch's caching allocator (never on the library's side),
-    zero-filled: the layer keeps counters in its first bytes that must start
-    at zero (every call leaves them at zero)."""
-    return torch.zeros(max(int(nbytes), 1), dtype=torch.uint8, device=device)
+    """Scratch from torch's caching allocator (never on the library's side)."""
+    return torch.empty(max(int(nbytes), 1), dtype=torch.uint8, device=device)
 
 
 def read_device_status(device: torch.device | None = None, clear: bool = True) -> int:

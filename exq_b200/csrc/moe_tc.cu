@@ -56,9 +56,7 @@ constexpr int kWarps = 21;
 constexpr int kThreads = kWarps * 32;
 constexpr int kWarpW = 0, kWarpB = 1, kWarpMma = 2;
 constexpr int kWarpCmb0 = 19, kNumCmb = 2;  // wait for the down items, then join the combine
-constexpr int kItemRing = 8;    // claimed items handed from the weight producer to the other roles
-constexpr int kItemConsumers = 18;  // activation producer, MMA, 4 epilogue, 12 dequant warps
-constexpr int kTailWarp0 = 3, kTailWarps = kWarps - 3;  // epilogue, dequant, combine warps
+constexpr int kTailWarp0 = 3, kTailWarps = kWarps - 3;  // epilogue, dequant and combine warps
 constexpr int kCmbMaxSpt = 16;  // slots per token the fused combine handles
 constexpr int kEpiWarp0 = 3, kNumEpiWarps = 4;
 constexpr int kDqWarp0 = 7, kDqGroups = 3, kDqGroupWarps = 4;  // 3 groups x 4 lane quarters
@@ -77,18 +75,20 @@ constexpr int kOffB = 0;
 constexpr int kOffW = kOffB + kBStages * kBSlot;
 constexpr int kOffS = kOffW + kWStages * kWSlot;
 constexpr int kOffBar = kOffS + kWStages * kSSlot;
-constexpr int kNumBars = 2 * kWStages + 2 * kABufs + 2 * kBStages + 4 + 2 * kItemRing;
+constexpr int kNumBars = 2 * kWStages + 2 * kABufs + 2 * kBStages + 4;
 constexpr int kOffMisc = kOffBar + kNumBars * 8;
-constexpr int kItemTab = 128;  // region of 48-byte entries: the item ring, then the combine staging
+constexpr int kItemTab = 128;  // work items of this CTA decoded into shared memory up front
 constexpr int kOffItems = kOffMisc + 64;
 constexpr int kItemBytes = 48;  // sizeof(Item)
 constexpr int kHistBuckets = 1024;  // experts the in-kernel tile list handles
 constexpr int kOffHist = kOffItems + kItemTab * kItemBytes;  // 3 x (kHistBuckets + 1) ints
-// After the item ring: the slot positions and router weights of this CTA's
-// share of the tokens, for the combine at the end of the launch.
-constexpr int kOffCmb = kOffItems + kItemRing * kItemBytes;
-constexpr int kCmbEntries = (kItemTab - kItemRing) * kItemBytes / 8;
-constexpr int kSmemBytes = kOffHist + 3 * (kHistBuckets + 1) * 4 + 1024;  // + slack to align the base to 1024 B
+// The histogram region is free once the item table is built; the combine at
+// the end of the launch then keeps there the slot positions and router
+// weights of this CTA's share of the tokens (kCmbEntries ints + floats).
+constexpr int kOffCmb = kOffHist;
+constexpr int kHistRegion = 3 * (kHistBuckets + 1) * 4;
+constexpr int kCmbEntries = kHistRegion / 8;
+constexpr int kSmemBytes = kOffHist + kHistRegion + 1024;  // + slack to align the base to 1024 B
 static_assert(kSmemBytes <= 232448, "shared memory per CTA");
 constexpr int kEpiBar = 1;   // named barrier of the four epilogue warps
 constexpr int kTailBar = 2;  // named barrier of the combine at the end (kTailWarps warps)
@@ -121,16 +121,10 @@ struct TcParams {
   // producer waits until all nb_gu row blocks of its tile have done so.
   int link;
   int* tile_done;
-  // A CTA's first item is blockIdx.x, its later ones gridDim.x + a value
-  // claimed from *claim as it goes (claims only grow, so every down item is
-  // claimed after the gate_up items it waits for); the last CTA to stop
-  // claiming resets claim and exit_cnt to zero for the next launch.
-  int* claim;
-  int* exit_cnt;
-  // fuse_combine: every down item adds 1 to *dn_done once its partial rows
-  // are stored; when all are, the CTAs sum y[t] = sum_j w[t, j] *
-  // partial[pos(t, j)] for their share of the tokens, in slot order with the
-  // rounding of combine_partials_kernel.
+  // fuse_combine: every CTA adds 1 to *dn_done (zeroed by the route stage)
+  // once its epilogue has stored all its items; when all have, the CTAs sum
+  // y[t] = sum_j w[t, j] * partial[pos(t, j)] for their share of the tokens,
+  // in slot order with the rounding of combine_partials_kernel.
   int fuse_combine;
   int* dn_done;
   const int32_t* sorted_slot;  // slot at every sorted position
@@ -220,8 +214,8 @@ __device__ __forceinline__ bool wait_count(const int* ctr, int target, uint32_t*
   asm volatile("ld.acquire.gpu.global.b32 %0, [%1];\n" : "=r"(v) : "l"(ctr) : "memory");
   if (v >= target) return true;
   const long long t0 = clock64();
-  for (unsigned ns = 64;; ns = ns < 1024 ? 2 * ns : ns) {
-    __nanosleep(ns);  // backing off: every CTA polls one L2 line
+  for (;;) {
+    __nanosleep(128);
     asm volatile("ld.acquire.gpu.global.b32 %0, [%1];\n" : "=r"(v) : "l"(ctr) : "memory");
     if (v >= target) return true;
     if (clock64() - t0 > 4000000000LL) {
@@ -235,10 +229,6 @@ __device__ __forceinline__ bool wait_count(const int* ctr, int target, uint32_t*
 // async-proxy (TMA) accesses.
 __device__ __forceinline__ void fence_proxy_async_global() {
   asm volatile("fence.proxy.async.global;\n" ::: "memory");
-}
-
-__device__ __forceinline__ bool tier_ok(int tier) {
-  return tier == kTierINT4 || tier == kTierINT8 || tier == kTierBF16;
 }
 
 // Bounded acquire-spin until *ctr >= target that gives up only after about
@@ -256,8 +246,16 @@ __device__ __forceinline__ bool wait_progress(const int* ctr, int target, uint32
       atomicOr(status, EXQ_DEV_TIMEOUT);
       return false;
     }
-    __nanosleep(512);  // a long wait, polled by one thread of every CTA: one L2 line
+    __nanosleep(128);  // one thread of every CTA polls this line
   }
+}
+
+// The CTA's li-th work item (global index `item`): from the shared table for
+// the first kItemTab, else from global memory.  False for an unknown tier.
+__device__ __forceinline__ bool decode_item(const TcParams& p, const Item* tab, int li, int item,
+                                            int n_tiles, Item& it) {
+  it = li < kItemTab ? tab[li] : make_item(p, item, n_tiles);
+  return it.tier == kTierINT4 || it.tier == kTierINT8 || it.tier == kTierBF16;
 }
 
 struct Ring {
@@ -440,9 +438,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
   auto B_empty = [&](int i) { return bar0 + 8u * (kBarB + kBStages + i); };
   auto Acc_full = [&](int i) { return bar0 + 8u * (kBarAcc + i); };
   auto Acc_empty = [&](int i) { return bar0 + 8u * (kBarAcc + 2 + i); };
-  constexpr int kBarIr = kBarAcc + 4;
-  auto IR_full = [&](int i) { return bar0 + 8u * (kBarIr + i); };
-  auto IR_empty = [&](int i) { return bar0 + 8u * (kBarIr + kItemRing + i); };
+
   volatile uint32_t* misc = reinterpret_cast<volatile uint32_t*>(gbase + kOffMisc);
   // misc[0] = TMEM base address, misc[1] = abort flag
 
@@ -465,10 +461,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
       mbar_init(Acc_full(i), 1);
       mbar_init(Acc_empty(i), kNumEpiWarps);
     }
-    for (int i = 0; i < kItemRing; ++i) {
-      mbar_init(IR_full(i), 1);
-      mbar_init(IR_empty(i), kItemConsumers);
-    }
+
     misc[1] = 0;
     mbar_fence_init();
   }
@@ -502,17 +495,16 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
   const bool early = p.weights_early || p.tiles_from_ids;
   if (!early) pdl_wait();
   pdl_trigger();
-  Item* iring = reinterpret_cast<Item*>(gbase + kOffItems);  // [kItemRing]
-  // per-expert tables of the tile list built from the ids (tiles_from_ids)
-  int* cnt = reinterpret_cast<int*>(gbase + kOffHist);
-  int* rbase = cnt + kHistBuckets + 1;
-  int* tstart = rbase + kHistBuckets + 1;
-  const int nbk = p.n_buckets;
+  Item* items_tab = reinterpret_cast<Item*>(gbase + kOffItems);
   int n_tiles;
   if (p.tiles_from_ids) {
     // The same tile list the routing kernel writes: experts in order, rows in
     // tiles of kMaxN from each expert's first sorted position.  Per-expert
     // counts (an order-independent histogram), then two exclusive scans.
+    int* cnt = reinterpret_cast<int*>(gbase + kOffHist);
+    int* rbase = cnt + kHistBuckets + 1;
+    int* tstart = rbase + kHistBuckets + 1;
+    const int nbk = p.n_buckets;
     for (int i = threadIdx.x; i < nbk; i += kThreads) cnt[i] = 0;
     __syncthreads();
     for (int i = threadIdx.x; i < p.n_slots; i += kThreads) {
@@ -555,18 +547,11 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
     }
     __syncthreads();
     n_tiles = min(tstart[nbk], p.max_tiles);
-  } else {
-    n_tiles = min(__ldcg(p.n_tiles_ptr), p.max_tiles);
-  }
-  const int n_items = num_items(p, n_tiles);
-  __syncthreads();
-  auto aborted = [&]() { return misc[1] != 0; };
-  auto do_abort = [&]() { misc[1] = 1; };
-  // Global item `item`: from the shared tables (tiles_from_ids) or the
-  // routing kernel's tile list.
-  auto decode = [&](int item) {
-    Item it;
-    if (p.tiles_from_ids) {
+    const int n_items0 = num_items(p, n_tiles);
+    for (int t = threadIdx.x; t < kItemTab; t += kThreads) {
+      const int item = static_cast<int>(blockIdx.x) + t * static_cast<int>(gridDim.x);
+      if (item >= n_items0) continue;
+      Item it;
       item_coords(p, item, n_tiles, it.prj, it.tile, it.nb);
       int lo = 0, hi = nbk - 1;  // last expert whose first tile is <= tile
       while (lo < hi) {
@@ -579,67 +564,34 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
       it.m0 = rbase[lo] + lt * kMaxN;
       it.mc = min(kMaxN, cnt[lo] - lt * kMaxN);
       finish_item(p, it);
-    } else {
-      it = make_item(p, item, n_tiles);
+      items_tab[t] = it;
     }
-    return it;
-  };
-  // The next item of this CTA from the item ring (whole warp): 0 an item,
-  // 1 the end of the stream, 2 a wait that ran out.
-  auto next_item = [&](Ring& q, Item& it) -> int {
-    const bool got = __all_sync(0xffffffffu, mbar_wait(IR_full(q.idx), q.phase, p.status));
-    int st = 2;
-    if (got) {
-      it = iring[q.idx];
-      st = it.prj < 0 ? 1 : 0;
+  } else {
+    n_tiles = min(__ldcg(p.n_tiles_ptr), p.max_tiles);
+    // decode this CTA's items once, so no role waits on global loads at an item boundary
+    const int n_items0 = num_items(p, n_tiles);
+    for (int t = threadIdx.x; t < kItemTab; t += kThreads) {
+      const int item = static_cast<int>(blockIdx.x) + t * static_cast<int>(gridDim.x);
+      if (item < n_items0) items_tab[t] = make_item(p, item, n_tiles);
     }
-    __syncwarp();
-    if (lane == 0 && got) mbar_arrive(IR_empty(q.idx));
-    q.next(kItemRing);
-    return st;
-  };
+  }
+  const int n_items = num_items(p, n_tiles);
+  __syncthreads();
+  auto aborted = [&]() { return misc[1] != 0; };
+  auto do_abort = [&]() { misc[1] = 1; };
 
   if (warp == kWarpW) {
     // ---------------------------------------------------------- weights
-    // The CTA's first item is blockIdx.x; the next ones are claimed from the
-    // global counter (items gridDim.x + claim), so the CTAs share the work as
-    // they go.  Each claim is issued one item ahead, its result used only
-    // after the current item's weights are streamed.  Every item goes to the
-    // other roles through the item ring.  The whole warp walks the loop
-    // (waits are uniform); one elected lane issues.
-    Ring r, qi;
+    // The whole warp walks the loop (waits are uniform); one elected lane
+    // issues, which keeps the issue path on the warp-uniform datapath.
+    Ring r;
     int issued = 0;
-    int item = static_cast<int>(blockIdx.x);
-    int pend = 0;
-    if (lane == 0) pend = atomicAdd(p.claim, 1);
-    auto next_claim = [&]() {
-      const int c = __shfl_sync(0xffffffffu, pend, 0);
-      if (lane == 0) pend = atomicAdd(p.claim, 1);
-      return static_cast<int>(gridDim.x) + c;
-    };
-    for (;;) {
-      const bool more = item < n_items && !aborted();
+    for (int item = blockIdx.x, li = 0; item < n_items && !aborted(); item += gridDim.x, ++li) {
       Item it;
-      it.prj = -1;  // the end of the stream
-      if (more) {
-        it = decode(item);
-        if (!tier_ok(it.tier)) {
-          if (lane == 0) atomicOr(p.status, EXQ_DEV_BAD_TIER);
-          item = next_claim();
-          continue;
-        }
+      if (!decode_item(p, items_tab, li, item, n_tiles, it)) {
+        if (lane == 0) atomicOr(p.status, EXQ_DEV_BAD_TIER);
+        continue;
       }
-      if (!__all_sync(0xffffffffu, mbar_wait(IR_empty(qi.idx), qi.phase ^ 1, p.status))) {
-        do_abort();
-        break;
-      }
-      if (lane == 0) {
-        iring[qi.idx] = it;
-        mbar_arrive(IR_full(qi.idx));
-      }
-      __syncwarp();
-      qi.next(kItemRing);
-      if (!more) break;
       const ProjParams& pj = p.pj[it.prj];
       const int G = pj.k >> 7;
       const int nk = pj.k / kKS;
@@ -680,19 +632,6 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
         do_abort();
         break;
       }
-      item = next_claim();
-    }
-    if (lane == 0) {
-      // this CTA claims nothing more (its last claim has returned, the fence
-      // orders it before the count): the last CTA to get here leaves the
-      // claim counter at zero for the next launch on this workspace
-      (void)*reinterpret_cast<volatile int*>(&pend);
-      __threadfence();
-      if (atomicAdd(p.exit_cnt, 1) == static_cast<int>(gridDim.x) - 1) {
-        *reinterpret_cast<volatile int*>(p.claim) = 0;
-        __threadfence();
-        *reinterpret_cast<volatile int*>(p.exit_cnt) = 0;
-      }
     }
     if (aborted()) {  // let in-flight copies land before the CTA exits
       Ring q = r;
@@ -705,13 +644,11 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
   } else if (warp == kWarpB) {
     // ---------------------------------------------------------- activations
     if (early) pdl_wait();
-    Ring r, qi;
+    Ring r;
     int issued = 0;
-    for (;;) {
+    for (int item = blockIdx.x, li = 0; item < n_items && !aborted(); item += gridDim.x, ++li) {
       Item it;
-      const int st = next_item(qi, it);
-      if (st == 2) do_abort();
-      if (st != 0 || aborted()) break;
+      if (!decode_item(p, items_tab, li, item, n_tiles, it)) continue;
       const ProjParams& pj = p.pj[it.prj];
       const int nk = pj.k / kKS;
       const int per_slot = it.per_slot;
@@ -765,14 +702,12 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
     // ---------------------------------------------------------- MMA issue
     // Converged warp; the elected lane issues each group of 4 MMAs (K = 64)
     // and the commits.  The k-stages of one weight slot are unrolled per tier.
-    Ring ra, rb, qi;
+    Ring ra, rb;
     int count = 0;
     const uint64_t bdesc0 = smem_desc_sw128(sB);
-    for (;;) {
+    for (int item = blockIdx.x, li = 0; item < n_items && !aborted(); item += gridDim.x, ++li) {
       Item it;
-      const int st = next_item(qi, it);
-      if (st == 2) do_abort();
-      if (st != 0 || aborted()) break;
+      if (!decode_item(p, items_tab, li, item, n_tiles, it)) continue;
       const int ab = count & 1;
       const uint32_t acc_phase = (count >> 1) & 1;
       ++count;
@@ -822,22 +757,23 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
     const int row = 32 * quarter + lane;
     const int et = static_cast<int>(threadIdx.x) - 32 * kEpiWarp0;  // 0..127
     int count = 0;
-    Ring qi;
     // The four warps take every decision together (the named barriers below
-    // need all 128 threads): the end of the stream (the same ring entry for
-    // all four) and the abort test are agreed at one barrier per item, after
-    // the accumulator wait.
-    for (;; ++count) {
+    // need all 128 threads): the loop bound and the abort test are agreed at
+    // the barrier after each accumulator wait.
+    for (int item = blockIdx.x, li = 0; item < n_items; item += gridDim.x, ++li, ++count) {
       Item it;
-      const int st = next_item(qi, it);
-      const int ab = count & 1;
-      const uint32_t acc_phase = (count >> 1) & 1;
-      const bool got = st == 0 && !aborted() && mbar_wait(Acc_full(ab), acc_phase, p.status);
-      if (named_barrier_or(kEpiBar, 128, !got)) {
-        if (st != 1) do_abort();
-        break;
+      if (!decode_item(p, items_tab, li, item, n_tiles, it)) {
+        --count;
+        continue;
       }
       const ProjParams& pj = p.pj[it.prj];
+      const int ab = count & 1;
+      const uint32_t acc_phase = (count >> 1) & 1;
+      const bool got = !aborted() && mbar_wait(Acc_full(ab), acc_phase, p.status);
+      if (named_barrier_or(kEpiBar, 128, !got)) {
+        do_abort();
+        break;
+      }
       tc_fence_after();
       const uint32_t taddr = tmem + (static_cast<uint32_t>(32 * quarter) << 16) + ab * kMaxN;
       if (pj.gate_up) {
@@ -894,16 +830,23 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(Acc_empty(ab));
-      if (pj.gate_up ? p.link : p.fuse_combine) {
-        // gate_up: this row block of the tile's mid rows is stored, for the
-        // down items of the tile (their TMA loads read mid); down: one more
-        // item's partial rows are stored, for the combine
-        if (pj.gate_up) fence_proxy_async_global();
+      if (pj.gate_up && p.link) {
+        // this row block of the tile's mid rows is stored: count it for the
+        // down items of the tile (their TMA loads read mid)
+        fence_proxy_async_global();
         named_barrier(kEpiBar, 128);
         if (et == 0) {
           __threadfence();
-          atomicAdd(pj.gate_up ? p.tile_done + it.tile : p.dn_done, 1);
+          atomicAdd(p.tile_done + it.tile, 1);
         }
+      }
+    }
+    if (p.fuse_combine) {
+      // every partial row of this CTA's items is stored: count the CTA
+      named_barrier(kEpiBar, 128);
+      if (et == 0) {
+        __threadfence();
+        atomicAdd(p.dn_done, 1);
       }
     }
   } else if (warp >= kWarpCmb0 && warp < kWarpCmb0 + kNumCmb) {
@@ -919,12 +862,9 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
     const uint32_t abuf = tmem + tlane + kTmemA + grp * kACols;
     const uint32_t a_empty = A_empty(grp), a_full = A_full(grp);
     uint32_t gs = 0;  // global slot counter of this CTA
-    Ring qi;
-    for (;;) {
+    for (int item = blockIdx.x, li = 0; item < n_items && !aborted(); item += gridDim.x, ++li) {
       Item it;
-      const int st = next_item(qi, it);
-      if (st == 2) do_abort();
-      if (st != 0 || aborted()) break;
+      if (!decode_item(p, items_tab, li, item, n_tiles, it)) continue;
       const int nk = p.pj[it.prj].k / kKS;
       const int sps = it.sps;
       // gate_up interleaves gate/up rows in blocks of 8 (the epilogue pairs lanes m, m^8)
@@ -996,41 +936,36 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
 
   if (p.fuse_combine && warp >= kTailWarp0) {
     // ---------------------------------------------------------- top-k combine
-    // Once every down item of the launch has stored its partial rows, the
-    // epilogue, dequant and combine warps of every CTA sum this CTA's share
-    // of the tokens: y[t] = sum_j w[t, j] * partial[pos(t, j)], slot order,
-    // product and sum rounded separately (a dropped slot adds 0 * w), exactly
-    // as combine_partials_kernel.  Warp kWarpCmb0 waits; the others agree at
-    // a barrier.
+    // Once every CTA has stored its items' partial rows, the epilogue,
+    // dequant and combine warps of every CTA sum this CTA's share of the
+    // tokens: y[t] = sum_j w[t, j] * partial[pos(t, j)], slot order, product
+    // and sum rounded separately (a dropped slot adds 0 * w), exactly as
+    // combine_partials_kernel.  The slot positions and weights are staged
+    // first; warp kWarpCmb0 waits for the count, the others agree at a barrier.
     const int tt = static_cast<int>(threadIdx.x) - 32 * kTailWarp0;
     const int wk = warp - kTailWarp0;
+    pdl_wait();  // pos_of_slot and the count's zero come from the routing kernel
+    const int spt = p.spt;
+    const int n_tok = static_cast<int>(p.n_slots / spt);
+    const int tpc = (n_tok + static_cast<int>(gridDim.x) - 1) / static_cast<int>(gridDim.x);
+    const int t0 = min(n_tok, static_cast<int>(blockIdx.x) * tpc), t1 = min(n_tok, t0 + tpc);
+    int* spos = reinterpret_cast<int*>(gbase + kOffCmb);  // [tokens of this CTA][spt]
+    float* sw = reinterpret_cast<float*>(spos + kCmbEntries);
+    for (int i = tt; i < (t1 - t0) * spt; i += 32 * kTailWarps) {
+      const int t = t0 + i / spt, j = i - (i / spt) * spt;
+      spos[i] = __ldcg(p.pos_of_slot + static_cast<int64_t>(t) * spt + j);
+      sw[i] = j < p.top_k ? load_as_f32(p.topk_w, p.w_dtype, static_cast<int64_t>(t) * p.top_k + j)
+                          : 1.0f;
+    }
     bool ok = true;
     if (warp == kWarpCmb0) {
-      // the count lives in this call's workspace layout: zeroed by the routing
-      // kernel, which may still be running (the location held other data)
-      pdl_wait();
-      const int n_down = p.run_dn ? n_tiles * p.pj[1].nblocks : 0;
-      if (lane == 0) ok = wait_progress(p.dn_done, n_down, p.status);
+      if (lane == 0) ok = wait_progress(p.dn_done, static_cast<int>(gridDim.x), p.status);
       ok = __shfl_sync(0xffffffffu, ok, 0);
     }
     if (!named_barrier_or(kTailBar, 32 * kTailWarps, !ok || aborted())) {
-      pdl_wait();  // pos_of_slot comes from the routing kernel
-      int seen;    // the other CTAs' partial rows (their counts were acquired above)
+      int seen;  // the other CTAs' partial rows (their counts were acquired above)
       asm volatile("ld.acquire.gpu.global.b32 %0, [%1];\n" : "=r"(seen) : "l"(p.dn_done) : "memory");
       (void)seen;
-      const int spt = p.spt;
-      const int n_tok = static_cast<int>(p.n_slots / spt);
-      const int tpc = (n_tok + static_cast<int>(gridDim.x) - 1) / static_cast<int>(gridDim.x);
-      const int t0 = min(n_tok, static_cast<int>(blockIdx.x) * tpc), t1 = min(n_tok, t0 + tpc);
-      int* spos = reinterpret_cast<int*>(gbase + kOffCmb);  // [tokens of this CTA][spt]
-      float* sw = reinterpret_cast<float*>(spos + kCmbEntries);
-      for (int i = tt; i < (t1 - t0) * spt; i += 32 * kTailWarps) {
-        const int t = t0 + i / spt, j = i - (i / spt) * spt;
-        spos[i] = __ldcg(p.pos_of_slot + static_cast<int64_t>(t) * spt + j);
-        sw[i] = j < p.top_k ? load_as_f32(p.topk_w, p.w_dtype, static_cast<int64_t>(t) * p.top_k + j)
-                            : 1.0f;
-      }
-      named_barrier(kTailBar, 32 * kTailWarps);
       const int nhb = static_cast<int>(p.hidden >> 7);
       const float* part = static_cast<const float*>(p.pj[1].out);
       const int64_t stride = p.pj[1].out_stride;
@@ -1331,16 +1266,14 @@ namespace {
 constexpr int kLayerMT = tc::kMaxN;  // tokens per GEMM tile (the MMA's N)
 
 struct TcWs {
-  int32_t* gemm_ctr;   // [2] item claims and exited CTAs of the GEMM launch: at offset 0,
-                       // zero before a call and after it (the launch's last CTA resets them)
   int32_t* sorted_slot;
   int32_t* pos_of_slot;
   float* sorted_w;
   int32_t* ends;
   int32_t* tile_info;
   int32_t* n_tiles;
-  int32_t* tile_done;  // [max_tiles] gate_up row blocks stored per tile, then the count
-                       // of stored down items (zeroed by the route stage)
+  int32_t* tile_done;  // [max_tiles] gate_up row blocks stored per tile, then the count of
+                       // CTAs whose items are all stored (zeroed by the route stage)
   __half* act;
   __half* mid;
   float* partial;
@@ -1359,7 +1292,6 @@ TcWs carve_tc(void* base, int64_t n_slots, int64_t n_tokens, int n_buckets, int6
     return base ? static_cast<char*>(base) + o : nullptr;
   };
   w.max_tiles = n_slots / kLayerMT + (n_slots < n_buckets ? n_slots : n_buckets) + 1;
-  w.gemm_ctr = reinterpret_cast<int32_t*>(take(8));
   w.sorted_slot = reinterpret_cast<int32_t*>(take(4 * n_slots));
   w.pos_of_slot = reinterpret_cast<int32_t*>(take(4 * n_slots));
   w.sorted_w = reinterpret_cast<float*>(take(4 * n_slots));
@@ -1468,7 +1400,7 @@ extern "C" int exq_moe_layer_forward_range(const exq_moe_weights* w, const void*
   // decode-sized calls route and gather in one kernel (stage 0; stage 1 is empty)
   const bool fused = n_slots <= kRouteGatherMaxSlots && n_total <= kRouteGatherMaxBuckets;
   // decode-sized calls: the GEMM launch also does the combine (its CTAs split
-  // the tokens once every down item is stored); larger ones launch it apart
+  // the tokens once every item is stored); larger ones launch it apart
   const bool fuse_combine = do_dn && first_stage <= 4 && end_stage > 4 && fused &&
                             spt <= tc::kCmbMaxSpt &&
                             ((n_tokens + num_sms() - 1) / num_sms() + 1) * spt <= tc::kCmbEntries;
@@ -1549,8 +1481,6 @@ extern "C" int exq_moe_layer_forward_range(const exq_moe_weights* w, const void*
     p.run_dn = do_dn;
     p.link = do_gu && do_dn;
     p.tile_done = ws.tile_done;
-    p.claim = ws.gemm_ctr;
-    p.exit_cnt = ws.gemm_ctr + 1;
     p.fuse_combine = fuse_combine;
     p.dn_done = ws.tile_done + ws.max_tiles;
     p.sorted_slot = ws.sorted_slot;
@@ -1570,9 +1500,10 @@ extern "C" int exq_moe_layer_forward_range(const exq_moe_weights* w, const void*
     const int64_t per_tile = (do_gu ? I / 64 : 0) + (do_dn ? H / 128 : 0);
     const int64_t max_items = ws.max_tiles * per_tile;
     const int64_t grid = max_items < num_sms() ? max_items : num_sms();
-    // a CTA can build its items from the ids: the experts fit the histogram
-    const bool ids_ok = n_total <= tc::kHistBuckets;
-    (void)grid;
+    // a CTA can build its items from the ids: the experts fit the histogram and
+    // every CTA's items fit its shared table
+    const bool ids_ok = n_total <= tc::kHistBuckets &&
+                        max_items <= static_cast<int64_t>(tc::kItemTab) * (grid > 0 ? grid : 1);
     if (fused && first_stage == 0) {
       // right after the fused routing of this call: build the tiles from the
       // ids (complete before routing started) and stream weights at once;

@@ -260,10 +260,7 @@ typedef struct exq_moe_weights {
  * (EXQ_DEV_BAD_EXPERT_ID); topk_weights [n_tokens, top_k] f32/f16/bf16.  Up
  * to 4096 slots: two launches (route fused with prep; the GEMM launch with
  * the combine at its end); above: route, prep, GEMM, combine.  No host
- * synchronisation.  The workspace must be zero-filled before its first use
- * and belongs to the library between calls on one stream: its first 256
- * bytes hold the GEMM launch's work counters, which every call leaves at
- * zero. */
+ * synchronisation. */
 EXQ_API size_t exq_moe_layer_workspace_bytes(int64_t n_tokens, int32_t top_k, int32_t n_shared,
                                              int32_t n_experts_total, int64_t hidden,
                                              int64_t inter);
