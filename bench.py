@@ -322,7 +322,7 @@ def ref_align(topk_ids, n_buckets, block, max_padded):
     return out
 
 
-def ref_layer(ref, w1p, w1s, w2p, w2s, x, ids, w, n_experts):
+def ref_layer(ref, w1p, w1s, w2p, w2s, x, ids, w, n_experts, launch_opts=None):
     """The body of the reference's _exq_forward_cuda (exq/runtime/
     sglang_backend.py:99-156) on its own kernels: align (torch stand-in),
     build_ends_from_slots, gather_hidden, the Triton INT4 GEMM, SiLU*mul
@@ -351,14 +351,14 @@ def ref_layer(ref, w1p, w1s, w2p, w2s, x, ids, w, n_experts):
         sorted_hidden, w1p, w1s, gate_up, expert_ends, N=inter2, K=hidden,
         stride_am=sorted_hidden.stride(0), stride_be=w1p.stride(0), stride_bn=w1p.stride(1),
         stride_se=w1s.stride(0), stride_sn=w1s.stride(1), stride_cm=gate_up.stride(0),
-        BLOCK_M=64, BLOCK_N=128, BLOCK_K=32, GROUP_SIZE=128)
+        BLOCK_M=64, BLOCK_N=128, BLOCK_K=32, GROUP_SIZE=128, **(launch_opts or {}))
     mid = (F.silu(gate_up[:, :inter].float()) * gate_up[:, inter:].float()).half()
     down = torch.zeros(n_active, hidden, dtype=torch.float16, device=x.device)
     tri._moe_gemm_int4_kernel[(n_experts, nm, (hidden + 127) // 128)](
         mid, w2p, w2s, down, expert_ends, N=hidden, K=inter,
         stride_am=mid.stride(0), stride_be=w2p.stride(0), stride_bn=w2p.stride(1),
         stride_se=w2s.stride(0), stride_sn=w2s.stride(1), stride_cm=down.stride(0),
-        BLOCK_M=64, BLOCK_N=128, BLOCK_K=32, GROUP_SIZE=128)
+        BLOCK_M=64, BLOCK_N=128, BLOCK_K=32, GROUP_SIZE=128, **(launch_opts or {}))
     result = torch.empty(n_tokens, hidden, dtype=torch.float16, device=x.device)
     disp.combine(down, sort_order, w.half().contiguous(), result)
     return result
@@ -382,11 +382,29 @@ def reference_gpu_measure(dev, banks, sweep_t=SWEEP_T, reps=30):
     out = {"path": "reference _exq_forward_cuda body: Triton _moe_gemm_int4_kernel (JIT for "
                    "sm_100) + exq_dispatch_cuda built from source; align and silu_and_mul are "
                    "torch stand-ins (sgl_kernel absent)", "per_T": {}}
+    # The reference's own launch first; Triton's pipeline for sm_100 may fail on
+    # this kernel, in which case the one change is the num_stages=1 launch option.
+    opts = None
+    x, ids, w, _ = layer_inputs(dev, 8, 1, seed0=7)[0]
+    for cand in (None, {"num_stages": 1}):
+        try:
+            ref_layer(ref, *packed[0], x, ids, w, c["n_experts"], cand)
+            torch.cuda.synchronize(dev)
+            opts = cand
+            break
+        except Exception as e:  # noqa: BLE001 - a compiler failure is the finding
+            msg = f"{type(e).__name__}: {str(e).strip().splitlines()[-1][:160]}"
+            out.setdefault("compile_failures", []).append(
+                {"launch_options": cand or "reference default", "error": msg})
+    else:
+        out["unavailable"] = "the reference's Triton GEMM does not compile for sm_100 here"
+        return out
+    out["launch_options"] = opts or "reference default"
     for t in sweep_t:
         inp = layer_inputs(dev, t, L, seed0=7)
         for i in range(L):   # warm (Triton JIT) and parity
             x, ids, w, _ = inp[i]
-            y_ref = ref_layer(ref, *packed[i], x, ids, w, c["n_experts"])
+            y_ref = ref_layer(ref, *packed[i], x, ids, w, c["n_experts"], opts)
         y_ours = banks[L - 1](x, ids, w)
         rel = float((y_ref.float() - y_ours.float()).norm() / y_ours.float().norm())
         torch.cuda.synchronize(dev)
@@ -394,7 +412,7 @@ def reference_gpu_measure(dev, banks, sweep_t=SWEEP_T, reps=30):
         e0.record()
         for r in range(reps):
             x, ids, w, _ = inp[r % L]
-            ref_layer(ref, *packed[r % L], x, ids, w, c["n_experts"])
+            ref_layer(ref, *packed[r % L], x, ids, w, c["n_experts"], opts)
         e1.record()
         torch.cuda.synchronize(dev)
         us = e0.elapsed_time(e1) / reps * 1e3
