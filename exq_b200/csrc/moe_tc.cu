@@ -116,10 +116,6 @@ struct ProjParams {
 struct TcParams {
   ProjParams pj[2];  // [0] gate_up, [1] down
   int run_gu, run_dn;
-  // bpi = 2: CTA pairs (clusters of two) share each item, a 2-row-block item
-  // computed by tcgen05.mma.cta_group::2 (M = 256); CTA rank r of the pair
-  // owns row block 2 * (item's block) + r.  bpi = 1: one CTA per item.
-  int bpi;
   // link (both projections in one launch): a gate_up item adds 1 to
   // tile_done[tile] once its mid rows are stored; a down item's activation
   // producer waits until all nb_gu row blocks of its tile have done so.
@@ -176,20 +172,18 @@ struct Item {
 static_assert(sizeof(Item) == kItemBytes, "item table entry size");
 
 __device__ __forceinline__ int num_items(const TcParams& p, int n_tiles) {
-  return (p.run_gu ? n_tiles * (p.pj[0].nblocks / p.bpi) : 0) +
-         (p.run_dn ? n_tiles * (p.pj[1].nblocks / p.bpi) : 0);
+  return (p.run_gu ? n_tiles * p.pj[0].nblocks : 0) + (p.run_dn ? n_tiles * p.pj[1].nblocks : 0);
 }
 
-// Projection, tile and this CTA's row block of global item `item` (gate_up
-// items first).
-__device__ __forceinline__ void item_coords(const TcParams& p, int item, int n_tiles, int rank,
-                                            int& prj, int& tile, int& nb) {
-  const int ngu = p.run_gu ? n_tiles * (p.pj[0].nblocks / p.bpi) : 0;
+// Projection, tile and row block of global item `item` (gate_up items first).
+__device__ __forceinline__ void item_coords(const TcParams& p, int item, int n_tiles, int& prj,
+                                            int& tile, int& nb) {
+  const int ngu = p.run_gu ? n_tiles * p.pj[0].nblocks : 0;
   prj = (item < ngu) ? 0 : 1;
   const int j = item - (prj ? ngu : 0);
-  const int nbk = p.pj[prj].nblocks / p.bpi;
+  const int nbk = p.pj[prj].nblocks;
   tile = j / nbk;
-  nb = (j - tile * nbk) * p.bpi + rank;
+  nb = j - tile * nbk;
 }
 
 // The fields that follow from (expert, rows, projection, row block).
@@ -197,16 +191,15 @@ __device__ __forceinline__ void finish_item(const TcParams& p, Item& it) {
   const int code = __ldg(p.expert_slot + it.e);
   it.tier = code >> 24;
   it.idx = code & 0xFFFFFF;
-  // a pair's MMA takes N in steps of 32 (16 token rows per CTA)
-  it.n = p.bpi == 2 ? max(32, (it.mc + 31) & ~31) : max(16, (it.mc + 15) & ~15);
+  it.n = max(16, (it.mc + 15) & ~15);
   it.r0 = p.pj[it.prj].gate_up ? it.nb * 64 : it.nb * 128;
   it.sps = stages_per_slot(it.tier);
-  it.per_slot = b_stages_per_slot(it.n / p.bpi);
+  it.per_slot = b_stages_per_slot(it.n);
 }
 
-__device__ __forceinline__ Item make_item(const TcParams& p, int item, int n_tiles, int rank) {
+__device__ __forceinline__ Item make_item(const TcParams& p, int item, int n_tiles) {
   Item it;
-  item_coords(p, item, n_tiles, rank, it.prj, it.tile, it.nb);
+  item_coords(p, item, n_tiles, it.prj, it.tile, it.nb);
   it.e = __ldcg(p.tile_info + 3 * it.tile);
   it.m0 = __ldcg(p.tile_info + 3 * it.tile + 1);
   it.mc = __ldcg(p.tile_info + 3 * it.tile + 2);
@@ -260,8 +253,8 @@ __device__ __forceinline__ bool wait_progress(const int* ctr, int target, uint32
 // The CTA's li-th work item (global index `item`): from the shared table for
 // the first kItemTab, else from global memory.  False for an unknown tier.
 __device__ __forceinline__ bool decode_item(const TcParams& p, const Item* tab, int li, int item,
-                                            int n_tiles, Item& it, int rank) {
-  it = li < kItemTab ? tab[li] : make_item(p, item, n_tiles, rank);
+                                            int n_tiles, Item& it) {
+  it = li < kItemTab ? tab[li] : make_item(p, item, n_tiles);
   return it.tier == kTierINT4 || it.tier == kTierINT8 || it.tier == kTierBF16;
 }
 
@@ -363,24 +356,7 @@ struct MmaItem {
 // MMAs of one weight slot (SPS k-stages of 64, A in tensor memory at `abuf`).
 // B stages are consumed from the activation ring; a ring slot is released
 // once its last stage has been issued.  Runs on the whole (converged) warp.
-template <bool kPair>
-__device__ __forceinline__ void mma_f16_ts(uint32_t d, uint32_t a, uint64_t b, uint32_t idesc,
-                                           uint32_t acc) {
-  if constexpr (kPair) tc_mma_f16_ts_pair(d, a, b, idesc, acc);
-  else tc_mma_f16_ts(d, a, b, idesc, acc);
-}
-template <bool kPair>
-__device__ __forceinline__ void commit(uint32_t bar) {
-  if constexpr (kPair) tc_commit_pair(bar);
-  else tc_commit(bar);
-}
-template <bool kPair>
-__device__ __forceinline__ bool wait_bar(uint32_t bar, uint32_t parity, uint32_t* status) {
-  if constexpr (kPair) return mbar_wait_cluster(bar, parity, status);
-  else return mbar_wait(bar, parity, status);
-}
-
-template <int SPS, bool kPair>
+template <int SPS>
 __device__ __forceinline__ bool mma_slot(const MmaItem& mi, uint32_t abuf, int kc0, Ring& rb,
                                          int& sidx) {
   if (SPS > 1 && sidx + SPS <= mi.per_slot && kc0 + SPS <= mi.nk) {
@@ -388,7 +364,7 @@ __device__ __forceinline__ bool mma_slot(const MmaItem& mi, uint32_t abuf, int k
     // so one wait at most and all 4*SPS MMAs from one elected block, with the
     // descriptors computed by the whole warp beforehand.
     if (sidx == 0) {
-      if (!__all_sync(0xffffffffu, wait_bar<kPair>(mi.bar_bfull + 8u * rb.idx, rb.phase, mi.status)))
+      if (!__all_sync(0xffffffffu, mbar_wait(mi.bar_bfull + 8u * rb.idx, rb.phase, mi.status)))
         return false;
       tc_fence_after();
     }
@@ -402,12 +378,12 @@ __device__ __forceinline__ bool mma_slot(const MmaItem& mi, uint32_t abuf, int k
 #pragma unroll
       for (int sub = 0; sub < SPS; ++sub) {
         const uint32_t a = abuf + 32 * sub;
-        mma_f16_ts<kPair>(mi.d, a, bd[sub], mi.idesc, sub == 0 ? first : 1u);
-        mma_f16_ts<kPair>(mi.d, a + 8, bd[sub] + 2, mi.idesc, 1u);
-        mma_f16_ts<kPair>(mi.d, a + 16, bd[sub] + 4, mi.idesc, 1u);
-        mma_f16_ts<kPair>(mi.d, a + 24, bd[sub] + 6, mi.idesc, 1u);
+        tc_mma_f16_ts(mi.d, a, bd[sub], mi.idesc, sub == 0 ? first : 1u);
+        tc_mma_f16_ts(mi.d, a + 8, bd[sub] + 2, mi.idesc, 1u);
+        tc_mma_f16_ts(mi.d, a + 16, bd[sub] + 4, mi.idesc, 1u);
+        tc_mma_f16_ts(mi.d, a + 24, bd[sub] + 6, mi.idesc, 1u);
       }
-      if (release_b) commit<kPair>(mi.bar_bempty + 8u * rb.idx);
+      if (release_b) tc_commit(mi.bar_bempty + 8u * rb.idx);
     }
     __syncwarp();
     sidx += SPS;
@@ -422,7 +398,7 @@ __device__ __forceinline__ bool mma_slot(const MmaItem& mi, uint32_t abuf, int k
     const int kc = kc0 + sub;
     if (kc >= mi.nk) break;
     if (sidx == 0) {
-      if (!__all_sync(0xffffffffu, wait_bar<kPair>(mi.bar_bfull + 8u * rb.idx, rb.phase, mi.status)))
+      if (!__all_sync(0xffffffffu, mbar_wait(mi.bar_bfull + 8u * rb.idx, rb.phase, mi.status)))
         return false;
       tc_fence_after();
     }
@@ -430,11 +406,11 @@ __device__ __forceinline__ bool mma_slot(const MmaItem& mi, uint32_t abuf, int k
     const uint32_t a = abuf + 32 * sub;
     const bool release_b = (++sidx == mi.per_slot) || kc == mi.nk - 1;
     if (elect_one()) {
-      mma_f16_ts<kPair>(mi.d, a, bd, mi.idesc, kc != 0);
-      mma_f16_ts<kPair>(mi.d, a + 8, bd + 2, mi.idesc, 1u);
-      mma_f16_ts<kPair>(mi.d, a + 16, bd + 4, mi.idesc, 1u);
-      mma_f16_ts<kPair>(mi.d, a + 24, bd + 6, mi.idesc, 1u);
-      if (release_b) commit<kPair>(mi.bar_bempty + 8u * rb.idx);
+      tc_mma_f16_ts(mi.d, a, bd, mi.idesc, kc != 0);
+      tc_mma_f16_ts(mi.d, a + 8, bd + 2, mi.idesc, 1u);
+      tc_mma_f16_ts(mi.d, a + 16, bd + 4, mi.idesc, 1u);
+      tc_mma_f16_ts(mi.d, a + 24, bd + 6, mi.idesc, 1u);
+      if (release_b) tc_commit(mi.bar_bempty + 8u * rb.idx);
     }
     __syncwarp();
     if (release_b) {
@@ -445,7 +421,6 @@ __device__ __forceinline__ bool mma_slot(const MmaItem& mi, uint32_t abuf, int k
   return true;
 }
 
-template <bool kPair>
 __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_constant__ TcParams p) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
@@ -468,10 +443,6 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
   // misc[0] = TMEM base address, misc[1] = abort flag
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  // a pair works on one item sequence: scheduled per cluster, rank picks the rows
-  const int rank = kPair ? static_cast<int>(cluster_ctarank()) : 0;
-  const int sid = kPair ? static_cast<int>(blockIdx.x >> 1) : static_cast<int>(blockIdx.x);
-  const int sn = kPair ? static_cast<int>(gridDim.x >> 1) : static_cast<int>(gridDim.x);
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < kWStages; ++i) {
@@ -479,7 +450,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
       mbar_init(W_empty(i), kDqGroupWarps);
     }
     for (int i = 0; i < kABufs; ++i) {
-      mbar_init(A_full(i), (kPair ? 2 : 1) * kDqGroupWarps);  // pair: both CTAs' dequantisers
+      mbar_init(A_full(i), kDqGroupWarps);
       mbar_init(A_empty(i), 1);
     }
     for (int i = 0; i < kBStages; ++i) {
@@ -488,7 +459,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(Acc_full(i), 1);
-      mbar_init(Acc_empty(i), (kPair ? 2 : 1) * kNumEpiWarps);  // pair: both CTAs' epilogues
+      mbar_init(Acc_empty(i), kNumEpiWarps);
     }
 
     misc[1] = 0;
@@ -507,18 +478,11 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
     }
   }
   if (warp == kWarpMma) {
-    if constexpr (kPair) {
-      tmem_alloc_pair(base + kOffMisc, kTmemCols);
-      tmem_relinquish_pair();
-    } else {
-      tmem_alloc(base + kOffMisc, kTmemCols);
-      tmem_relinquish();
-    }
+    tmem_alloc(base + kOffMisc, kTmemCols);
+    tmem_relinquish();
     tc_fence_before();
   }
   __syncthreads();
-  // a pair: both CTAs' barriers are initialised before either arrives remotely
-  if constexpr (kPair) cluster_sync_all();
   tc_fence_after();
   const uint32_t tmem = misc[0];
   // everything above overlaps the tail of the previous kernel in the stream.
@@ -585,10 +549,10 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
     n_tiles = min(tstart[nbk], p.max_tiles);
     const int n_items0 = num_items(p, n_tiles);
     for (int t = threadIdx.x; t < kItemTab; t += kThreads) {
-      const int item = sid + t * sn;
+      const int item = static_cast<int>(blockIdx.x) + t * static_cast<int>(gridDim.x);
       if (item >= n_items0) continue;
       Item it;
-      item_coords(p, item, n_tiles, rank, it.prj, it.tile, it.nb);
+      item_coords(p, item, n_tiles, it.prj, it.tile, it.nb);
       int lo = 0, hi = nbk - 1;  // last expert whose first tile is <= tile
       while (lo < hi) {
         const int mid = (lo + hi + 1) >> 1;
@@ -607,8 +571,8 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
     // decode this CTA's items once, so no role waits on global loads at an item boundary
     const int n_items0 = num_items(p, n_tiles);
     for (int t = threadIdx.x; t < kItemTab; t += kThreads) {
-      const int item = sid + t * sn;
-      if (item < n_items0) items_tab[t] = make_item(p, item, n_tiles, rank);
+      const int item = static_cast<int>(blockIdx.x) + t * static_cast<int>(gridDim.x);
+      if (item < n_items0) items_tab[t] = make_item(p, item, n_tiles);
     }
   }
   const int n_items = num_items(p, n_tiles);
@@ -622,9 +586,9 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
     // issues, which keeps the issue path on the warp-uniform datapath.
     Ring r;
     int issued = 0;
-    for (int item = sid, li = 0; item < n_items && !aborted(); item += sn, ++li) {
+    for (int item = blockIdx.x, li = 0; item < n_items && !aborted(); item += gridDim.x, ++li) {
       Item it;
-      if (!decode_item(p, items_tab, li, item, n_tiles, it, rank)) {
+      if (!decode_item(p, items_tab, li, item, n_tiles, it)) {
         if (lane == 0) atomicOr(p.status, EXQ_DEV_BAD_TIER);
         continue;
       }
@@ -682,15 +646,13 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
     if (early) pdl_wait();
     Ring r;
     int issued = 0;
-    for (int item = sid, li = 0; item < n_items && !aborted(); item += sn, ++li) {
+    for (int item = blockIdx.x, li = 0; item < n_items && !aborted(); item += gridDim.x, ++li) {
       Item it;
-      if (!decode_item(p, items_tab, li, item, n_tiles, it, rank)) continue;
+      if (!decode_item(p, items_tab, li, item, n_tiles, it)) continue;
       const ProjParams& pj = p.pj[it.prj];
       const int nk = pj.k / kKS;
       const int per_slot = it.per_slot;
-      // a pair: this CTA loads its half of the item's token rows
-      const int nh = kPair ? it.n / 2 : it.n;
-      const uint32_t stage_bytes = static_cast<uint32_t>(nh) * 128u;
+      const uint32_t stage_bytes = static_cast<uint32_t>(it.n) * 128u;
       if (p.link && it.prj == 1) {
         // the tile's mid rows come from nb_gu gate_up items of this launch
         bool ok = true;
@@ -715,16 +677,9 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
         }
         const uint32_t bar = B_full(r.idx);
         if (elect_one()) {
-          // the whole slot in one box: nh rows x per_slot stages (stages past k
-          // read as zeros).  A pair's two halves both count on rank 0's barrier.
-          if constexpr (kPair) {
-            if (rank == 0) mbar_arrive_tx(bar, 2u * static_cast<uint32_t>(per_slot) * stage_bytes);
-            tma_load_3d_pair(sB + r.idx * kBSlot, &pj.tm_b[(nh >> 4) - 1], bar, 0, it.m0 + rank * nh,
-                             kc0);
-          } else {
-            mbar_arrive_tx(bar, static_cast<uint32_t>(per_slot) * stage_bytes);
-            tma_load_3d(sB + r.idx * kBSlot, &pj.tm_b[(nh >> 4) - 1], bar, 0, it.m0, kc0);
-          }
+          // the whole slot in one box: n rows x per_slot stages (stages past k read as zeros)
+          mbar_arrive_tx(bar, static_cast<uint32_t>(per_slot) * stage_bytes);
+          tma_load_3d(sB + r.idx * kBSlot, &pj.tm_b[(it.n >> 4) - 1], bar, 0, it.m0, kc0);
         }
         __syncwarp();
         r.next(kBStages);
@@ -750,25 +705,23 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
     Ring ra, rb;
     int count = 0;
     const uint64_t bdesc0 = smem_desc_sw128(sB);
-    // a pair's MMAs are issued by rank 0 alone
-    for (int item = sid, li = 0; item < n_items && !aborted() && rank == 0; item += sn, ++li) {
+    for (int item = blockIdx.x, li = 0; item < n_items && !aborted(); item += gridDim.x, ++li) {
       Item it;
-      if (!decode_item(p, items_tab, li, item, n_tiles, it, rank)) continue;
+      if (!decode_item(p, items_tab, li, item, n_tiles, it)) continue;
       const int ab = count & 1;
       const uint32_t acc_phase = (count >> 1) & 1;
       ++count;
-      if (!__all_sync(0xffffffffu, wait_bar<kPair>(Acc_empty(ab), acc_phase ^ 1, p.status))) {
+      if (!__all_sync(0xffffffffu, mbar_wait(Acc_empty(ab), acc_phase ^ 1, p.status))) {
         do_abort();
         break;
       }
       tc_fence_after();
       MmaItem mi;
       mi.d = tmem + ab * kMaxN;
-      mi.idesc = kPair ? idesc_f16_m256(it.n) : idesc_f16_m128(it.n);
+      mi.idesc = idesc_f16_m128(it.n);
       mi.nk = p.pj[it.prj].k / kKS;
       mi.per_slot = it.per_slot;
-      // rows of one k-stage in this CTA's B slot x 128 B, in 16 B units
-      mi.stage_desc = static_cast<uint32_t>(kPair ? it.n / 2 : it.n) * 8u;
+      mi.stage_desc = static_cast<uint32_t>(it.n) * 8u;  // n rows x 128 B, in 16 B units
       mi.bdesc0 = bdesc0;
       mi.bar_bfull = B_full(0);
       mi.bar_bempty = B_empty(0);
@@ -777,17 +730,17 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
       int sidx = 0;
       const int sps = it.sps;
       for (int kc0 = 0; kc0 < mi.nk; kc0 += sps) {
-        if (!__all_sync(0xffffffffu, wait_bar<kPair>(A_full(ra.idx), ra.phase, p.status))) {
+        if (!__all_sync(0xffffffffu, mbar_wait(A_full(ra.idx), ra.phase, p.status))) {
           ok = false;
           break;
         }
         tc_fence_after();
         const uint32_t abuf = tmem + kTmemA + ra.idx * kACols;
-        if (sps == 4) ok = mma_slot<4, kPair>(mi, abuf, kc0, rb, sidx);
-        else if (sps == 2) ok = mma_slot<2, kPair>(mi, abuf, kc0, rb, sidx);
-        else ok = mma_slot<1, kPair>(mi, abuf, kc0, rb, sidx);
+        if (sps == 4) ok = mma_slot<4>(mi, abuf, kc0, rb, sidx);
+        else if (sps == 2) ok = mma_slot<2>(mi, abuf, kc0, rb, sidx);
+        else ok = mma_slot<1>(mi, abuf, kc0, rb, sidx);
         if (!ok) break;
-        if (elect_one()) commit<kPair>(A_empty(ra.idx));
+        if (elect_one()) tc_commit(A_empty(ra.idx));
         __syncwarp();
         ra.next(kABufs);
       }
@@ -795,7 +748,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
         do_abort();
         break;
       }
-      if (elect_one()) commit<kPair>(Acc_full(ab));
+      if (elect_one()) tc_commit(Acc_full(ab));
       __syncwarp();
     }
   } else if (warp < kDqWarp0) {
@@ -807,16 +760,16 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
     // The four warps take every decision together (the named barriers below
     // need all 128 threads): the loop bound and the abort test are agreed at
     // the barrier after each accumulator wait.
-    for (int item = sid, li = 0; item < n_items; item += sn, ++li, ++count) {
+    for (int item = blockIdx.x, li = 0; item < n_items; item += gridDim.x, ++li, ++count) {
       Item it;
-      if (!decode_item(p, items_tab, li, item, n_tiles, it, rank)) {
+      if (!decode_item(p, items_tab, li, item, n_tiles, it)) {
         --count;
         continue;
       }
       const ProjParams& pj = p.pj[it.prj];
       const int ab = count & 1;
       const uint32_t acc_phase = (count >> 1) & 1;
-      const bool got = !aborted() && wait_bar<kPair>(Acc_full(ab), acc_phase, p.status);
+      const bool got = !aborted() && mbar_wait(Acc_full(ab), acc_phase, p.status);
       if (named_barrier_or(kEpiBar, 128, !got)) {
         do_abort();
         break;
@@ -876,10 +829,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) {
-        if constexpr (kPair) mbar_arrive_cluster(Acc_empty(ab), 0);  // rank 0's MMA waits on it
-        else mbar_arrive(Acc_empty(ab));
-      }
+      if (lane == 0) mbar_arrive(Acc_empty(ab));
       if (pj.gate_up && p.link) {
         // this row block of the tile's mid rows is stored: count it for the
         // down items of the tile (their TMA loads read mid)
@@ -912,9 +862,9 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
     const uint32_t abuf = tmem + tlane + kTmemA + grp * kACols;
     const uint32_t a_empty = A_empty(grp), a_full = A_full(grp);
     uint32_t gs = 0;  // global slot counter of this CTA
-    for (int item = sid, li = 0; item < n_items && !aborted(); item += sn, ++li) {
+    for (int item = blockIdx.x, li = 0; item < n_items && !aborted(); item += gridDim.x, ++li) {
       Item it;
-      if (!decode_item(p, items_tab, li, item, n_tiles, it, rank)) continue;
+      if (!decode_item(p, items_tab, li, item, n_tiles, it)) continue;
       const int nk = p.pj[it.prj].k / kKS;
       const int sps = it.sps;
       // gate_up interleaves gate/up rows in blocks of 8 (the epilogue pairs lanes m, m^8)
@@ -926,7 +876,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
         const int ns = min(sps, nk - kc0);
         const uint32_t wi = gs % kWStages, wph = (gs / kWStages) & 1;
         const uint32_t aph = (gs / kABufs) & 1;
-        bool got = wait_bar<kPair>(a_empty, aph ^ 1, p.status);
+        bool got = mbar_wait(a_empty, aph ^ 1, p.status);
         if (got) got = mbar_wait(W_full(wi), wph, p.status);
         if (!__all_sync(0xffffffffu, got)) {
           ok = false;
@@ -974,8 +924,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
         __syncwarp();
         if (lane == 0) {
           mbar_arrive(W_empty(wi));
-          if constexpr (kPair) mbar_arrive_cluster(a_full, 0);  // rank 0's MMA waits on it
-          else mbar_arrive(a_full);
+          mbar_arrive(a_full);
         }
       }
       if (!ok) {
@@ -1059,16 +1008,10 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
 
   // producer / MMA warps arrive here diverged (only lane 0 worked)
   cta_barrier_unaligned();
-  if constexpr (kPair) {
-    // neither CTA leaves (or frees tensor memory) while rank 0's MMAs may
-    // still read the other's tensor or shared memory
-    asm volatile("barrier.cluster.arrive;\nbarrier.cluster.wait;\n" ::: "memory");
-  }
   if (warp == kWarpMma) {
     __syncwarp();
     tc_fence_after();
-    if constexpr (kPair) tmem_dealloc_pair(tmem, kTmemCols);
-    else tmem_dealloc(tmem, kTmemCols);
+    tmem_dealloc(tmem, kTmemCols);
   }
 }
 
@@ -1258,8 +1201,6 @@ static int build_maps(const exq_moe_weights* w, int proj, const void* act, int64
   return EXQ_OK;
 }
 
-// `max_items`: items of one CTA each (row blocks x tiles).  With p.bpi == 2 the
-// kernel runs as clusters of two CTAs, one item per pair.
 int launch_tc(const TcParams& p, int max_items, cudaStream_t stream, bool pdl) {
   static int attr_done[64] = {0};
   static int sms[64] = {0};
@@ -1267,46 +1208,21 @@ int launch_tc(const TcParams& p, int max_items, cudaStream_t stream, bool pdl) {
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64) dev = 0;
   if (!attr_done[dev]) {
-    for (auto fn : {moe_tc_kernel<false>, moe_tc_kernel<true>}) {
-      cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
-      if (e != cudaSuccess) {
-        set_error("moe_tc_kernel: cannot reserve %d B of shared memory: %s", kSmemBytes,
-                  cudaGetErrorString(e));
-        return EXQ_ERR_CUDA;
-      }
+    cudaError_t e = cudaFuncSetAttribute(moe_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         kSmemBytes);
+    if (e != cudaSuccess) {
+      set_error("moe_tc_kernel: cannot reserve %d B of shared memory: %s", kSmemBytes,
+                cudaGetErrorString(e));
+      return EXQ_ERR_CUDA;
     }
     sms[dev] = num_sms();
     attr_done[dev] = 1;
   }
-  const bool pair = p.bpi == 2;
   int grid = sms[dev];
-  if (pair) grid &= ~1;
-  if (max_items < grid) grid = max_items;  // a pair covers two row blocks
-  if (pair) grid = (grid + 1) & ~1;
-  if (grid < (pair ? 2 : 1)) grid = pair ? 2 : 1;
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(grid);
-  cfg.blockDim = dim3(kThreads);
-  cfg.dynamicSmemBytes = kSmemBytes;
-  cfg.stream = stream;
-  cudaLaunchAttribute attr[2];
-  int na = 0;
-  if (pdl) {
-    attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[na].val.programmaticStreamSerializationAllowed = 1;
-    ++na;
-  }
-  if (pair) {
-    attr[na].id = cudaLaunchAttributeClusterDimension;
-    attr[na].val.clusterDim.x = 2;
-    attr[na].val.clusterDim.y = 1;
-    attr[na].val.clusterDim.z = 1;
-    ++na;
-  }
-  cfg.attrs = attr;
-  cfg.numAttrs = na;
-  const cudaError_t e = pair ? cudaLaunchKernelEx(&cfg, moe_tc_kernel<true>, p)
-                             : cudaLaunchKernelEx(&cfg, moe_tc_kernel<false>, p);
+  if (max_items < grid) grid = max_items;
+  if (grid < 1) grid = 1;
+  const cudaError_t e =
+      launch_pdl(pdl, moe_tc_kernel, dim3(grid), dim3(kThreads), kSmemBytes, stream, p);
   if (e != cudaSuccess) {
     set_error("moe_tc_kernel: %s", cudaGetErrorString(e));
     return EXQ_ERR_CUDA;
@@ -1563,9 +1479,6 @@ extern "C" int exq_moe_layer_forward_range(const exq_moe_weights* w, const void*
     }
     p.run_gu = do_gu;
     p.run_dn = do_dn;
-    // CTA pairs (M = 256 per MMA) when every projection of the launch has an
-    // even number of row blocks
-    p.bpi = ((!do_gu || p.pj[0].nblocks % 2 == 0) && (!do_dn || p.pj[1].nblocks % 2 == 0)) ? 2 : 1;
     p.link = do_gu && do_dn;
     p.tile_done = ws.tile_done;
     p.fuse_combine = fuse_combine;

@@ -173,99 +173,3 @@ __device__ __forceinline__ uint32_t idesc_f16_m128(int n) {
 
 }  // namespace tc
 }  // namespace exq
-
-// ------------------------------------------------------------------ CTA pairs
-// A cluster of two CTAs that issue tcgen05.mma.cta_group::2 (M = 256: each CTA
-// holds 128 rows of A and of the accumulator in its own tensor memory, and half
-// of B's N columns in its own shared memory).  CTA rank 0 issues the MMAs.
-namespace exq {
-namespace tc {
-
-__device__ __forceinline__ uint32_t cluster_ctarank() {
-  uint32_t r;
-  asm volatile("mov.u32 %0, %%cluster_ctarank;\n" : "=r"(r));
-  return r;
-}
-// Arrive (release, cluster scope) on the mbarrier at the same shared-memory
-// offset in CTA `cta` of the cluster.
-__device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar, uint32_t cta) {
-  asm volatile(
-      "{\n .reg .b32 ra;\n mapa.shared::cluster.u32 ra, %0, %1;\n"
-      " mbarrier.arrive.release.cluster.shared::cluster.b64 _, [ra];\n}\n" ::"r"(bar),
-      "r"(cta)
-      : "memory");
-}
-__device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n .reg .pred p;\n"
-      " mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n"
-      " selp.u32 %0, 1, 0, p;\n}\n"
-      : "=r"(ok)
-      : "r"(bar), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-// Bounded wait (about 2 s) with cluster-scope acquire, for barriers that the
-// peer CTA arrives on.
-__device__ __forceinline__ bool mbar_wait_cluster(uint32_t bar, uint32_t parity, uint32_t* status) {
-  if (mbar_try_wait_cluster(bar, parity)) return true;
-  const long long t0 = clock64();
-  while (!mbar_try_wait_cluster(bar, parity)) {
-    if (clock64() - t0 > 4000000000LL) {
-      atomicOr(status, EXQ_DEV_TIMEOUT);
-      return false;
-    }
-  }
-  return true;
-}
-// TMA load into this CTA's shared memory whose completion (bytes) counts on
-// the mbarrier at `bar`'s offset in CTA rank 0 of the pair (bit 24 of a
-// shared-memory address selects the CTA of a pair).  No multicast.
-__device__ __forceinline__ void tma_load_3d_pair(uint32_t dst, const CUtensorMap* map, uint32_t bar,
-                                                 int c0, int c1, int c2) {
-  asm volatile(
-      "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
-      " [%0], [%1, {%3, %4, %5}], [%2];\n" ::"r"(dst),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar & 0xFEFFFFFFu), "r"(c0), "r"(c1), "r"(c2)
-      : "memory");
-}
-__device__ __forceinline__ void tmem_alloc_pair(uint32_t dst_smem, uint32_t ncols) {
-  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(dst_smem),
-               "r"(ncols));
-}
-__device__ __forceinline__ void tmem_relinquish_pair() {
-  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;\n" ::);
-}
-__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
-  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;\n" ::"r"(taddr), "r"(ncols));
-}
-// Arrive on `bar` (same offset) in both CTAs of the pair once every
-// previously issued tcgen05.mma of this thread completes.
-__device__ __forceinline__ void tc_commit_pair(uint32_t bar) {
-  asm volatile(
-      "{\n .reg .b16 m;\n mov.b16 m, 3;\n"
-      " tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64"
-      " [%0], m;\n}\n" ::"r"(bar)
-      : "memory");
-}
-// D (both CTAs' tensor memory) (+)= A (both CTAs' tensor memory, 256 rows) *
-// B (N columns, half in each CTA's shared memory), fp16 inputs, fp32 accumulate.
-__device__ __forceinline__ void tc_mma_f16_ts_pair(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
-                                                   uint32_t idesc, uint32_t accumulate) {
-  asm volatile(
-      "{\n .reg .pred p;\n"
-      " setp.ne.b32 p, %4, 0;\n"
-      " tcgen05.mma.cta_group::2.kind::f16 [%0], [%1], %2, %3, p;\n}\n" ::"r"(d_tmem),
-      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate));
-}
-__device__ __forceinline__ void cluster_sync_all() {
-  asm volatile("barrier.cluster.arrive.aligned;\nbarrier.cluster.wait.aligned;\n" ::: "memory");
-}
-// Instruction descriptor: kind::f16, fp16 A/B, fp32 D, both K-major, M = 256.
-__device__ __forceinline__ uint32_t idesc_f16_m256(int n) {
-  return (1u << 4) | (static_cast<uint32_t>(n >> 3) << 17) | (static_cast<uint32_t>(256 >> 4) << 24);
-}
-
-}  // namespace tc
-}  // namespace exq
