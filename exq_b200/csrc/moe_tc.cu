@@ -670,19 +670,15 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
       uint32_t acc = 0;  // 0 until this warp's first MMA of the item
       for (int kc0 = 0, sl = 0; kc0 < nk; kc0 += sps, ++sl) {
         const int ns = min(sps, nk - kc0);
-        // Every issuer waits for every B slot to be filled, its own slots or
-        // not, before it commits the slot's release below: an issuer that
-        // released a slot it had not seen filled could arrive twice on one
-        // phase of B_empty while the other issuer had not arrived at all.
-        if (!b_ready) {
-          if (!__all_sync(0xffffffffu, mbar_wait(B_full(rb.idx), rb.phase, p.status))) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          b_ready = true;
-        }
         if (sl % NI == iss) {
+          if (!b_ready) {
+            if (!__all_sync(0xffffffffu, mbar_wait(B_full(rb.idx), rb.phase, p.status))) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            b_ready = true;
+          }
           if (!__all_sync(0xffffffffu, mbar_wait(A_full(ra.idx), ra.phase, p.status))) {
             ok = false;
             break;
