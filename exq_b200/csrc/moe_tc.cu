@@ -52,10 +52,9 @@
 namespace exq {
 namespace tc {
 
-constexpr int kWarps = 22;
+constexpr int kWarps = 21;
 constexpr int kThreads = kWarps * 32;
 constexpr int kWarpW = 0, kWarpB = 1, kWarpMma = 2;
-constexpr int kWarpMma2 = 21;  // second MMA issuer (32-token tiles; sub-partition 1)
 constexpr int kWarpCmb0 = 19, kNumCmb = 2;  // wait for the down items, then join the combine
 constexpr int kTailWarp0 = 3, kTailWarps = kWarps - 3;  // epilogue, dequant and combine warps
 constexpr int kCmbMaxSpt = 16;  // slots per token the fused combine handles
@@ -64,11 +63,9 @@ constexpr int kDqWarp0 = 7, kDqGroups = 3, kDqGroupWarps = 4;  // 3 groups x 4 l
 constexpr int kWStages = 6, kABufs = 3, kBStages = 3;  // weight slots, TMEM A buffers, B slots
 constexpr int kWSlot = 16384, kSSlot = 512, kBSlot = 32768;
 constexpr int kACols = 128;  // tensor-memory columns per A buffer (128 rows x 256 fp16)
-// Tokens per item (the MMA's N), the kernel's template parameter MT: 64 with
-// one MMA-issuing warp (two accumulators of 64 columns), or 32 with two
-// issuers (four accumulators of 32 columns); either way the accumulators take
-// 128 columns and three 128-column A buffers the other 384.
-constexpr int kMaxN = 64;
+constexpr int kMaxN = 64;        // tokens per item (the MMA's N)
+static_assert(kMaxN <= 64, "two accumulators of kMaxN columns and three 128-column A buffers "
+                            "fill the 512 tensor-memory columns");
 constexpr int kBRows = 256;      // activation rows one B slot holds (256 rows x 128 B)
 constexpr int kTmemCols = 512;
 constexpr int kTmemA = 2 * kMaxN;  // first tensor-memory column of the A buffers
@@ -356,10 +353,75 @@ struct MmaItem {
   uint32_t* status;
 };
 
-template <int MT>
+// MMAs of one weight slot (SPS k-stages of 64, A in tensor memory at `abuf`).
+// B stages are consumed from the activation ring; a ring slot is released
+// once its last stage has been issued.  Runs on the whole (converged) warp.
+template <int SPS>
+__device__ __forceinline__ bool mma_slot(const MmaItem& mi, uint32_t abuf, int kc0, Ring& rb,
+                                         int& sidx) {
+  if (SPS > 1 && sidx + SPS <= mi.per_slot && kc0 + SPS <= mi.nk) {
+    // Fast path (N <= 32 for INT4): all SPS stages lie in the current B slot,
+    // so one wait at most and all 4*SPS MMAs from one elected block, with the
+    // descriptors computed by the whole warp beforehand.
+    if (sidx == 0) {
+      if (!__all_sync(0xffffffffu, mbar_wait(mi.bar_bfull + 8u * rb.idx, rb.phase, mi.status)))
+        return false;
+      tc_fence_after();
+    }
+    uint64_t bd[SPS];
+    bd[0] = mi.bdesc0 + rb.idx * (kBSlot >> 4) + sidx * mi.stage_desc;
+#pragma unroll
+    for (int sub = 1; sub < SPS; ++sub) bd[sub] = bd[sub - 1] + mi.stage_desc;
+    const bool release_b = (sidx + SPS == mi.per_slot) || (kc0 + SPS == mi.nk);
+    const uint32_t first = kc0 != 0;
+    if (elect_one()) {
+#pragma unroll
+      for (int sub = 0; sub < SPS; ++sub) {
+        const uint32_t a = abuf + 32 * sub;
+        tc_mma_f16_ts(mi.d, a, bd[sub], mi.idesc, sub == 0 ? first : 1u);
+        tc_mma_f16_ts(mi.d, a + 8, bd[sub] + 2, mi.idesc, 1u);
+        tc_mma_f16_ts(mi.d, a + 16, bd[sub] + 4, mi.idesc, 1u);
+        tc_mma_f16_ts(mi.d, a + 24, bd[sub] + 6, mi.idesc, 1u);
+      }
+      if (release_b) tc_commit(mi.bar_bempty + 8u * rb.idx);
+    }
+    __syncwarp();
+    sidx += SPS;
+    if (release_b) {
+      rb.next(kBStages);
+      sidx = 0;
+    }
+    return true;
+  }
+#pragma unroll
+  for (int sub = 0; sub < SPS; ++sub) {
+    const int kc = kc0 + sub;
+    if (kc >= mi.nk) break;
+    if (sidx == 0) {
+      if (!__all_sync(0xffffffffu, mbar_wait(mi.bar_bfull + 8u * rb.idx, rb.phase, mi.status)))
+        return false;
+      tc_fence_after();
+    }
+    const uint64_t bd = mi.bdesc0 + rb.idx * (kBSlot >> 4) + sidx * mi.stage_desc;
+    const uint32_t a = abuf + 32 * sub;
+    const bool release_b = (++sidx == mi.per_slot) || kc == mi.nk - 1;
+    if (elect_one()) {
+      tc_mma_f16_ts(mi.d, a, bd, mi.idesc, kc != 0);
+      tc_mma_f16_ts(mi.d, a + 8, bd + 2, mi.idesc, 1u);
+      tc_mma_f16_ts(mi.d, a + 16, bd + 4, mi.idesc, 1u);
+      tc_mma_f16_ts(mi.d, a + 24, bd + 6, mi.idesc, 1u);
+      if (release_b) tc_commit(mi.bar_bempty + 8u * rb.idx);
+    }
+    __syncwarp();
+    if (release_b) {
+      rb.next(kBStages);
+      sidx = 0;
+    }
+  }
+  return true;
+}
+
 __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_constant__ TcParams p) {
-  constexpr int NI = MT == 32 ? 2 : 1;  // MMA-issuing warps
-  static_assert(MT == 32 || MT == 64, "tile heights");
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
@@ -393,10 +455,10 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
     }
     for (int i = 0; i < kBStages; ++i) {
       mbar_init(B_full(i), 1);
-      mbar_init(B_empty(i), NI);  // every issuer commits each used-up B slot
+      mbar_init(B_empty(i), 1);
     }
     for (int i = 0; i < 2; ++i) {
-      mbar_init(Acc_full(i), NI);  // every issuer commits its accumulator
+      mbar_init(Acc_full(i), 1);
       mbar_init(Acc_empty(i), kNumEpiWarps);
     }
 
@@ -437,7 +499,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
   int n_tiles;
   if (p.tiles_from_ids) {
     // The same tile list the routing kernel writes: experts in order, rows in
-    // tiles of MT from each expert's first sorted position.  Per-expert
+    // tiles of kMaxN from each expert's first sorted position.  Per-expert
     // counts (an order-independent histogram), then two exclusive scans.
     int* cnt = reinterpret_cast<int*>(gbase + kOffHist);
     int* rbase = cnt + kHistBuckets + 1;
@@ -461,7 +523,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
       int rs = 0, ts = 0;
       for (int e = lo; e < hi; ++e) {
         rs += cnt[e];
-        ts += (cnt[e] + MT - 1) / MT;
+        ts += (cnt[e] + kMaxN - 1) / kMaxN;
       }
       int rx = rs, tx = ts;
 #pragma unroll
@@ -480,7 +542,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
         rbase[e] = rx;
         tstart[e] = tx;
         rx += cnt[e];
-        tx += (cnt[e] + MT - 1) / MT;
+        tx += (cnt[e] + kMaxN - 1) / kMaxN;
       }
     }
     __syncthreads();
@@ -499,8 +561,8 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
       }
       const int lt = it.tile - tstart[lo];
       it.e = lo;
-      it.m0 = rbase[lo] + lt * MT;
-      it.mc = min(MT, cnt[lo] - lt * MT);
+      it.m0 = rbase[lo] + lt * kMaxN;
+      it.mc = min(kMaxN, cnt[lo] - lt * kMaxN);
       finish_item(p, it);
       items_tab[t] = it;
     }
@@ -636,16 +698,10 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
         mbar_wait(B_full(q.idx), q.phase, p.status);
       }
     }
-  } else if (warp == kWarpMma || (NI == 2 && warp == kWarpMma2)) {
+  } else if (warp == kWarpMma) {
     // ---------------------------------------------------------- MMA issue
-    // NI issuing warps.  With two (32-token tiles), each on its own SM
-    // sub-partition takes alternate weight slots of every item into its own
-    // accumulator and the epilogue adds the two.  Both walk every slot, so
-    // their A and B ring positions stay in step; a warp waits for and issues
-    // only its own slots, and both commit each used-up B slot and the item's
-    // accumulator.  A converged warp: the elected lane issues the MMAs (4 per
-    // 64-k stage) and the commits.
-    const int iss = warp == kWarpMma ? 0 : 1;
+    // Converged warp; the elected lane issues each group of 4 MMAs (K = 64)
+    // and the commits.  The k-stages of one weight slot are unrolled per tier.
     Ring ra, rb;
     int count = 0;
     const uint64_t bdesc0 = smem_desc_sw128(sB);
@@ -660,55 +716,33 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
         break;
       }
       tc_fence_after();
-      const uint32_t d = tmem + (ab * NI + iss) * MT;
-      const uint32_t idesc = idesc_f16_m128(it.n);
-      const int nk = p.pj[it.prj].k / kKS;
-      const uint32_t stage_desc = static_cast<uint32_t>(it.n) * 8u;  // n rows x 128 B, in 16 B units
-      const int sps = it.sps, per_slot = it.per_slot;
+      MmaItem mi;
+      mi.d = tmem + ab * kMaxN;
+      mi.idesc = idesc_f16_m128(it.n);
+      mi.nk = p.pj[it.prj].k / kKS;
+      mi.per_slot = it.per_slot;
+      mi.stage_desc = static_cast<uint32_t>(it.n) * 8u;  // n rows x 128 B, in 16 B units
+      mi.bdesc0 = bdesc0;
+      mi.bar_bfull = B_full(0);
+      mi.bar_bempty = B_empty(0);
+      mi.status = p.status;
+      bool ok = true;
       int sidx = 0;
-      bool b_ready = false, ok = true;
-      uint32_t acc = 0;  // 0 until this warp's first MMA of the item
-      for (int kc0 = 0, sl = 0; kc0 < nk; kc0 += sps, ++sl) {
-        const int ns = min(sps, nk - kc0);
-        if (sl % NI == iss) {
-          if (!b_ready) {
-            if (!__all_sync(0xffffffffu, mbar_wait(B_full(rb.idx), rb.phase, p.status))) {
-              ok = false;
-              break;
-            }
-            tc_fence_after();
-            b_ready = true;
-          }
-          if (!__all_sync(0xffffffffu, mbar_wait(A_full(ra.idx), ra.phase, p.status))) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          const uint32_t abuf = tmem + kTmemA + ra.idx * kACols;
-          const uint64_t bd0 = bdesc0 + rb.idx * (kBSlot >> 4) + sidx * stage_desc;
-          if (elect_one()) {
-            for (int j = 0; j < ns; ++j) {
-              const uint32_t a = abuf + 32 * j;
-              const uint64_t bd = bd0 + j * stage_desc;
-              tc_mma_f16_ts(d, a, bd, idesc, j == 0 ? acc : 1u);
-              tc_mma_f16_ts(d, a + 8, bd + 2, idesc, 1u);
-              tc_mma_f16_ts(d, a + 16, bd + 4, idesc, 1u);
-              tc_mma_f16_ts(d, a + 24, bd + 6, idesc, 1u);
-            }
-            tc_commit(A_empty(ra.idx));
-          }
-          __syncwarp();
-          acc = 1u;
+      const int sps = it.sps;
+      for (int kc0 = 0; kc0 < mi.nk; kc0 += sps) {
+        if (!__all_sync(0xffffffffu, mbar_wait(A_full(ra.idx), ra.phase, p.status))) {
+          ok = false;
+          break;
         }
+        tc_fence_after();
+        const uint32_t abuf = tmem + kTmemA + ra.idx * kACols;
+        if (sps == 4) ok = mma_slot<4>(mi, abuf, kc0, rb, sidx);
+        else if (sps == 2) ok = mma_slot<2>(mi, abuf, kc0, rb, sidx);
+        else ok = mma_slot<1>(mi, abuf, kc0, rb, sidx);
+        if (!ok) break;
+        if (elect_one()) tc_commit(A_empty(ra.idx));
+        __syncwarp();
         ra.next(kABufs);
-        sidx += ns;
-        if (sidx >= per_slot || kc0 + sps >= nk) {  // the B slot is used up
-          if (elect_one()) tc_commit(B_empty(rb.idx));
-          __syncwarp();
-          rb.next(kBStages);
-          sidx = 0;
-          b_ready = false;
-        }
       }
       if (!ok) {
         do_abort();
@@ -741,10 +775,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
         break;
       }
       tc_fence_after();
-      const uint32_t taddr = tmem + (static_cast<uint32_t>(32 * quarter) << 16) + ab * NI * MT;
-      // two issuers: the second accumulator (odd weight slots) if the item has any
-      const int nslots = (pj.k / kKS + it.sps - 1) / it.sps;
-      const bool two = NI == 2 && nslots > 1;
+      const uint32_t taddr = tmem + (static_cast<uint32_t>(32 * quarter) << 16) + ab * kMaxN;
       if (pj.gate_up) {
         // rows in blocks of 8: gate rows have bit 3 clear, the matching up row is row ^ 8
         const int g = it.r0 + ((row >> 4) << 3) + (row & 7);
@@ -763,16 +794,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
         for (int c = 0; c < it.n; c += 16) {
           uint32_t v[16];
           tmem_ld16(taddr + c, v);
-          if (two) {
-            uint32_t u[16];
-            tmem_ld16(taddr + MT + c, u);
-            tmem_wait_ld();
-#pragma unroll
-            for (int i = 0; i < 16; ++i)
-              v[i] = __float_as_uint(__uint_as_float(v[i]) + __uint_as_float(u[i]));
-          } else {
-            tmem_wait_ld();
-          }
+          tmem_wait_ld();
           // gate lanes finish tokens c..c+7, up lanes c+8..c+15: each lane sends
           // its partner (lane ^ 8) the value the partner is missing
 #pragma unroll
@@ -797,16 +819,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
         for (int c = 0; c < it.n; c += 16) {
           uint32_t v[16];
           tmem_ld16(taddr + c, v);
-          if (two) {
-            uint32_t u[16];
-            tmem_ld16(taddr + MT + c, u);
-            tmem_wait_ld();
-#pragma unroll
-            for (int i = 0; i < 16; ++i)
-              v[i] = __float_as_uint(__uint_as_float(v[i]) + __uint_as_float(u[i]));
-          } else {
-            tmem_wait_ld();
-          }
+          tmem_wait_ld();
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
             const int tok = c + i;
@@ -838,8 +851,6 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
     }
   } else if (warp >= kWarpCmb0 && warp < kWarpCmb0 + kNumCmb) {
     // combine warps: nothing during the items (the combine below)
-  } else if (warp == kWarpMma2) {
-    // one issuer (64-token tiles): nothing during the items
   } else {
     // ---------------------------------------------------------- dequant
     // Group g = (warp - kDqWarp0) / 4 converts weight slots gs = g, g+3, ...
@@ -1190,21 +1201,19 @@ static int build_maps(const exq_moe_weights* w, int proj, const void* act, int64
   return EXQ_OK;
 }
 
-// mt: tokens per tile, 32 (two MMA issuers) or 64 (one).
-int launch_tc(const TcParams& p, int mt, int max_items, cudaStream_t stream, bool pdl) {
+int launch_tc(const TcParams& p, int max_items, cudaStream_t stream, bool pdl) {
   static int attr_done[64] = {0};
   static int sms[64] = {0};
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64) dev = 0;
   if (!attr_done[dev]) {
-    for (auto fn : {moe_tc_kernel<32>, moe_tc_kernel<64>}) {
-      cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
-      if (e != cudaSuccess) {
-        set_error("moe_tc_kernel: cannot reserve %d B of shared memory: %s", kSmemBytes,
-                  cudaGetErrorString(e));
-        return EXQ_ERR_CUDA;
-      }
+    cudaError_t e = cudaFuncSetAttribute(moe_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         kSmemBytes);
+    if (e != cudaSuccess) {
+      set_error("moe_tc_kernel: cannot reserve %d B of shared memory: %s", kSmemBytes,
+                cudaGetErrorString(e));
+      return EXQ_ERR_CUDA;
     }
     sms[dev] = num_sms();
     attr_done[dev] = 1;
@@ -1213,8 +1222,7 @@ int launch_tc(const TcParams& p, int mt, int max_items, cudaStream_t stream, boo
   if (max_items < grid) grid = max_items;
   if (grid < 1) grid = 1;
   const cudaError_t e =
-      mt == 32 ? launch_pdl(pdl, moe_tc_kernel<32>, dim3(grid), dim3(kThreads), kSmemBytes, stream, p)
-               : launch_pdl(pdl, moe_tc_kernel<64>, dim3(grid), dim3(kThreads), kSmemBytes, stream, p);
+      launch_pdl(pdl, moe_tc_kernel, dim3(grid), dim3(kThreads), kSmemBytes, stream, p);
   if (e != cudaSuccess) {
     set_error("moe_tc_kernel: %s", cudaGetErrorString(e));
     return EXQ_ERR_CUDA;
@@ -1255,11 +1263,7 @@ using namespace exq;
 
 namespace {
 
-// Tokens per GEMM tile (the MMA's N): 32 (two MMA issuers) for calls whose
-// routing runs fused with the gather, 64 (one issuer, fewer re-streams of a
-// heavy expert's weights) above.  A function of the call's shape only, so
-// every stage of a call agrees on it.
-constexpr int kLayerMTSmall = 32, kLayerMTLarge = tc::kMaxN;
+constexpr int kLayerMT = tc::kMaxN;  // tokens per GEMM tile (the MMA's N)
 
 struct TcWs {
   int32_t* sorted_slot;
@@ -1287,7 +1291,7 @@ TcWs carve_tc(void* base, int64_t n_slots, int64_t n_tokens, int n_buckets, int6
     off = align_up(off + bytes, 256);
     return base ? static_cast<char*>(base) + o : nullptr;
   };
-  w.max_tiles = n_slots / kLayerMTSmall + (n_slots < n_buckets ? n_slots : n_buckets) + 1;
+  w.max_tiles = n_slots / kLayerMT + (n_slots < n_buckets ? n_slots : n_buckets) + 1;
   w.sorted_slot = reinterpret_cast<int32_t*>(take(4 * n_slots));
   w.pos_of_slot = reinterpret_cast<int32_t*>(take(4 * n_slots));
   w.sorted_w = reinterpret_cast<float*>(take(4 * n_slots));
@@ -1395,7 +1399,6 @@ extern "C" int exq_moe_layer_forward_range(const exq_moe_weights* w, const void*
   const bool do_dn = first_stage <= 3 && end_stage > 3;
   // decode-sized calls route and gather in one kernel (stage 0; stage 1 is empty)
   const bool fused = n_slots <= kRouteGatherMaxSlots && n_total <= kRouteGatherMaxBuckets;
-  const int mt = fused ? kLayerMTSmall : kLayerMTLarge;
   // decode-sized calls: the GEMM launch also does the combine (its CTAs split
   // the tokens once every item is stored); larger ones launch it apart
   const bool fuse_combine = do_dn && first_stage <= 4 && end_stage > 4 && fused &&
@@ -1414,7 +1417,7 @@ extern "C" int exq_moe_layer_forward_range(const exq_moe_weights* w, const void*
     rg.spt = spt;
     rg.n_routed = w->n_routed;
     rg.n_buckets = n_total;
-    rg.mt = mt;
+    rg.mt = kLayerMT;
     rg.n = n_slots;
     rg.act = ws.act;
     rg.pos_of_slot = ws.pos_of_slot;
@@ -1439,7 +1442,7 @@ extern "C" int exq_moe_layer_forward_range(const exq_moe_weights* w, const void*
     rp.n_routed = w->n_routed;
     rp.top_k = top_k;
     rp.slots_per_token = spt;
-    rp.mt = mt;
+    rp.mt = kLayerMT;
     rp.sorted_i32 = ws.sorted_slot;
     rp.pos_of_slot = ws.pos_of_slot;
     rp.sorted_w = ws.sorted_w;
@@ -1457,7 +1460,7 @@ extern "C" int exq_moe_layer_forward_range(const exq_moe_weights* w, const void*
   }
   if (!fused && first_stage <= 1 && end_stage > 1) {
     st = tc::launch_prep(hidden_states, act_dtype, H, n_tokens, ws.sorted_slot, spt, n_slots,
-                         ws.ends + n_total, mt, ws.act, s, chained);
+                         ws.ends + n_total, kLayerMT, ws.act, s, chained);
     if (st != EXQ_OK) return st;
     chained = true;
   }
@@ -1519,7 +1522,7 @@ extern "C" int exq_moe_layer_forward_range(const exq_moe_weights* w, const void*
     p.n_routed = w->n_routed;
     p.n_buckets = n_total;
     p.n_slots = n_slots;
-    st = tc::launch_tc(p, mt, static_cast<int>(max_items < INT32_MAX ? max_items : INT32_MAX), s,
+    st = tc::launch_tc(p, static_cast<int>(max_items < INT32_MAX ? max_items : INT32_MAX), s,
                        chained);
     if (st != EXQ_OK) return st;
     chained = true;
