@@ -348,3 +348,24 @@ def test_layer_qwen3_decode_sizes_in_full(cuda, t):
     y = bank(x.to(cuda), ids.to(cuda), w.to(cuda))
     ref = oracle_layer(bank, x, ids, w)
     assert OM.rel_l2(y, ref) < TOL
+
+
+def test_layer_mixtral_prefill_4096(cuda):
+    """BASELINE config 4 prefill (E8 top-2 H4096 I14336, bf16, T=4096): 8192
+    rows, 210 to 3109 per expert (Zipf), so every expert runs several token
+    tiles in the large-call path.  A sample of tokens run as a call of their own must give the same
+    rows bit for bit (a token's result does not depend on the other tokens in
+    its tiles), and that small call is checked against the oracle."""
+    from exq_b200.synth import hidden_states, zipf_router
+    bank, c = _bank("mixtral", cuda)
+    t = 4096
+    ids, w = zipf_router(t, c.n_experts, c.top_k, seed=40)
+    x = hidden_states(t, c.hidden, seed=40, dtype=torch.bfloat16)
+    xd, idd, wd = x.to(cuda), ids.to(cuda), w.to(cuda)
+    y = bank(xd, idd, wd)
+    assert torch.bincount(ids.reshape(-1).long(), minlength=8).min() > 192   # 4+ tiles each
+    sample = torch.tensor([0, 1, 2, 511, 1024, 2047, 2048, 3000, 4000, 4094, 4095])
+    ys = bank(xd[sample.to(cuda)], idd[sample.to(cuda)], wd[sample.to(cuda)])
+    assert torch.equal(ys, y[sample.to(cuda)])
+    ref = oracle_layer(bank, x, ids, w, tokens=sample)
+    assert OM.rel_l2(ys, ref) < TOL
