@@ -58,6 +58,8 @@ def parse():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-ep", action="store_true",
                     help="skip the expert-parallel configs (C4, C5; one GPU = whole layer)")
+    ap.add_argument("--no-configs", action="store_true",
+                    help="skip the C1 / C3 / C5 lines beside the headline")
     ap.add_argument("--profile", action="store_true",
                     help="small case for ncu: one layer of the bench workload, 3 eager calls")
     ap.add_argument("--no-ref-gpu", action="store_true",
@@ -728,6 +730,94 @@ def prefill_measure(bank, c, dev, tokens=4096, steps=5):
             "peak_kind": "measured bf16 burst" if peak else None}
 
 
+def tier_expert_bytes(tier, hidden, inter):
+    """Stored bytes of one expert (gate_up + down) in a tier: INT4 nibbles +
+    group-128 fp16 scales, INT8 bytes + per-output-row fp16 scales, or BF16."""
+    from exq_b200.synth import int4_expert_bytes
+    if tier == "INT4":
+        return int4_expert_bytes(hidden, inter)
+    if tier == "INT8":
+        return 3 * inter * hidden + 2 * (2 * inter + hidden)
+    return 3 * inter * hidden * 2
+
+
+def stack_measure(dev, name, tokens, n_layers, tiers_fn=None, reps=20, warmup=3):
+    """A stack of ``n_layers`` independently seeded MoE layers of config
+    ``name`` at ``tokens`` decode tokens, each layer's output the next one's
+    input, captured as one CUDA graph and replayed (the stack's weights are
+    far above L2).  Reports µs per stack and per layer, and the stack's
+    algorithmic bytes (touched experts' stored bytes by tier, shared experts,
+    activations in/out, routing metadata) over that time against the measured
+    HBM copy bandwidth."""
+    import torch
+    from exq_b200 import ExpertBank
+    from exq_b200.synth import CONFIGS, expert_weights, hidden_states, zipf_router
+    c = CONFIGS[name]
+    banks, routes, nbytes = [], [], 0
+    act = 2
+    for li in range(n_layers):
+        w13, w2 = expert_weights(c.n_experts, c.inter, c.hidden, seed=500 + li, device=dev)
+        sw13 = sw2 = None
+        if c.n_shared:
+            sw13, sw2 = expert_weights(c.n_shared, c.inter, c.hidden, seed=900 + li, device=dev)
+        tiers = tiers_fn(li) if tiers_fn else None
+        banks.append(ExpertBank.from_dense(w13, w2, tiers, act_dtype=c.act_dtype,
+                                           shared_w13=sw13, shared_w2=sw2))
+        del w13, w2, sw13, sw2
+        ids, w = zipf_router(tokens, c.n_experts, c.top_k, seed=700 + li)
+        touched = set(ids.reshape(-1).tolist())
+        tl = tiers or ["INT4"] * c.n_experts
+        nbytes += sum(tier_expert_bytes(tl[e], c.hidden, c.inter) for e in touched)
+        nbytes += c.n_shared * tier_expert_bytes("BF16", c.hidden, c.inter)
+        nbytes += 2 * tokens * c.hidden * act + tokens * c.top_k * 8
+        routes.append((ids.to(dev), w.to(dev)))
+    torch.cuda.synchronize(dev)
+    x0 = hidden_states(tokens, c.hidden, seed=77).to(dev, c.act_dtype)
+    s = torch.cuda.Stream(dev)
+    s.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(s):
+        for bank, (ids, w) in zip(banks, routes):
+            bank.reserve(tokens, c.top_k)
+        y = x0
+        for bank, (ids, w) in zip(banks, routes):
+            y = bank(y, ids, w)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            y = x0
+            for bank, (ids, w) in zip(banks, routes):
+                y = bank(y, ids, w)
+    torch.cuda.current_stream(dev).wait_stream(s)
+    sec = time_graphs([g], reps, warmup, dev) / reps
+    peak, peak_kind = measured_peak()
+    gbps = nbytes / sec / 1e9
+    ok = bool(torch.isfinite(y).all())
+    del g, banks
+    torch.cuda.empty_cache()
+    return {"model": c.name, "layers": n_layers, "tokens": tokens,
+            "tiers": "per layer: top 10% BF16, next 20% INT8, rest INT4 (Zipf rank)"
+                     if tiers_fn else "INT4 g128" + (" + BF16 shared" if c.n_shared else ""),
+            "us_per_stack": round(sec * 1e6, 1), "us_per_layer": round(sec * 1e6 / n_layers, 2),
+            "bytes_per_stack": int(nbytes), "gbps": round(gbps, 1),
+            "frac": round(gbps / peak, 3), "peak_kind": peak_kind, "finite": ok,
+            "gpu_launches_per_stack": 2 * n_layers}
+
+
+def configs_measure(dev):
+    """The BASELINE configs beside the headline (C2): C1 (OLMoE layer, 16
+    tokens), C3 (16-layer mixed BF16/INT8/INT4 stack, 64 tokens, one grouped
+    GEMM launch per layer), C5 (26-layer DeepSeek-V2-Lite stack with two BF16
+    shared experts, 64 and 256 tokens).  C1 chains 8 independently seeded
+    layers (1.7 GB of weights, above L2) and reports the per-layer time."""
+    from exq_b200.synth import tier_plan
+    return {
+        "C1_olmoe_T16": stack_measure(dev, "olmoe", 16, 8, reps=50),
+        "C3_olmoe_mixed_16L_T64": stack_measure(
+            dev, "olmoe_mixed", 64, 16, tiers_fn=lambda li: tier_plan(64, seed=li)),
+        "C5_dsv2_lite_26L_T64": stack_measure(dev, "dsv2_lite", 64, 26),
+        "C5_dsv2_lite_26L_T256": stack_measure(dev, "dsv2_lite", 256, 26),
+    }
+
+
 def profile_case():
     """One layer of the bench workload (311 MB of INT4 weights, > L2) called
     three times eagerly: the capture target for ``ncu --set full`` on the GEMM
@@ -844,6 +934,10 @@ def main():
     if rank == 0 and world == 1 and not args.no_cpu:
         cpu = cpu_baseline()
 
+    cfgs = None
+    if world == 1 and not args.no_configs:
+        cfgs = configs_measure(dev)
+
     ep = {}
     if not args.no_ep:
         for name in EP_CASES:
@@ -882,6 +976,8 @@ def main():
         "clocks": clk.summary(),
         "sweep": sweep,
     }
+    if cfgs is not None:
+        line["configs"] = cfgs
     if ref_gpu is not None:
         line["reference_gpu"] = ref_gpu
     if ep:
