@@ -62,6 +62,8 @@ def parse():
                     help="skip the C1 / C3 / C5 lines beside the headline")
     ap.add_argument("--profile", action="store_true",
                     help="small case for ncu: one layer of the bench workload, 3 eager calls")
+    ap.add_argument("--profile-prefill", action="store_true",
+                    help="small case for ncu: the C4 prefill layer (T=4096), 3 eager calls")
     ap.add_argument("--no-ref-gpu", action="store_true",
                     help="skip the reference's own GPU path (Triton GEMMs + exq_dispatch_cuda)")
     ap.add_argument("--setup-reference", action="store_true",
@@ -821,7 +823,7 @@ def configs_measure(dev):
 def profile_case():
     """One layer of the bench workload (311 MB of INT4 weights, > L2) called
     three times eagerly: the capture target for ``ncu --set full`` on the GEMM
-    (route_gather, gate_up, down, combine: 4 launches per call)."""
+    (route_gather, then one moe_tc_kernel launch per call)."""
     import torch
     dev = torch.device("cuda", 0)
     bank = build_layers(dev, 1)[0]
@@ -833,8 +835,36 @@ def profile_case():
     return 0
 
 
+def profile_prefill_case(tokens=4096):
+    """The C4 prefill layer (Mixtral shape, INT4 g128, bf16, T=4096: 733 MB of
+    packed weights, 8192 slots) called three times eagerly: the capture target
+    for the tensor-pipe counters of the prefill GEMM launch.  The dense weights
+    are freed before the calls, so the device holds under 1 GB."""
+    import torch
+    from exq_b200 import ExpertBank
+    from exq_b200.synth import CONFIGS, expert_weights, hidden_states, zipf_router
+    dev = torch.device("cuda", 0)
+    c = CONFIGS["mixtral"]
+    w13, w2 = expert_weights(c.n_experts, c.inter, c.hidden, seed=0, device=dev)
+    bank = ExpertBank.from_dense(w13, w2, None, act_dtype=c.act_dtype)
+    del w13, w2
+    torch.cuda.synchronize(dev)
+    torch.cuda.empty_cache()
+    ids, w = zipf_router(tokens, c.n_experts, c.top_k, seed=3)
+    x = hidden_states(tokens, c.hidden, seed=3).to(dev, c.act_dtype)
+    ids, w = ids.to(dev), w.to(dev)
+    for _ in range(3):
+        y = bank(x, ids, w)
+    torch.cuda.synchronize(dev)
+    print(f"prefill profile case ok: T={tokens} |y|={y.float().norm().item():.4f} "
+          f"device MB {torch.cuda.memory_reserved(dev) / 2**20:.0f}")
+    return 0
+
+
 def main():
     args = parse()
+    if args.profile_prefill:
+        return profile_prefill_case()
     if args.setup_reference:
         return setup_reference()
     if args.impl == "reference":
