@@ -63,12 +63,17 @@ constexpr int kDqWarp0 = 7, kDqGroups = 3, kDqGroupWarps = 4;  // 3 groups x 4 l
 constexpr int kWStages = 6, kABufs = 3, kBStages = 3;  // weight slots, TMEM A buffers, B slots
 constexpr int kWSlot = 16384, kSSlot = 512, kBSlot = 32768;
 constexpr int kACols = 128;  // tensor-memory columns per A buffer (128 rows x 256 fp16)
-constexpr int kMaxN = 64;        // tokens per item (the MMA's N)
-static_assert(kMaxN <= 64, "two accumulators of kMaxN columns and three 128-column A buffers "
-                            "fill the 512 tensor-memory columns");
+// Tokens per item (the MMA's N), a template parameter of the kernel:
+//   64: two accumulators of 64 columns + three 128-column A buffers (three
+//       dequant groups), the decode build;
+//  128: two accumulators of 128 columns + two A buffers (two dequant groups),
+//       for calls with many rows per expert: each expert's weights are
+//       streamed and converted once per 128 tokens instead of 64.
+// Either way the 512 tensor-memory columns are full.
+constexpr int kMaxN = 64;
+constexpr int kWideN = 128;
 constexpr int kBRows = 256;      // activation rows one B slot holds (256 rows x 128 B)
 constexpr int kTmemCols = 512;
-constexpr int kTmemA = 2 * kMaxN;  // first tensor-memory column of the A buffers
 constexpr int kKS = 64;          // k per pipeline stage
 
 constexpr int kOffB = 0;
@@ -155,11 +160,16 @@ __device__ __forceinline__ int stages_per_slot(int tier) {
   return tier == kTierINT4 ? 4 : (tier == kTierINT8 ? 2 : 1);
 }
 
-// k-stages of n activation rows one B slot carries: a multiple of 4 (the
-// stages of an INT4 weight slot), so a weight slot never straddles two B
-// slots; one 3D TMA box (n rows x these stages) fills the slot.
+// k-stages of n activation rows one B slot carries.  64-token items: a
+// multiple of 4 (the stages of an INT4 weight slot), so a weight slot never
+// straddles two B slots; one 3D TMA box (n rows x these stages) fills the
+// slot.  128-token items: boxes of 128 rows (rows past the tile are unused),
+// 2 stages per slot, an INT4 weight slot spanning two B slots.
 __host__ __device__ __forceinline__ int b_stages_per_slot(int n) {
   return (kBRows / n) & ~3;
+}
+__host__ __device__ __forceinline__ int b_slot_stages(int mt, int n) {
+  return mt == kWideN ? kBRows / kWideN : b_stages_per_slot(n);
 }
 
 // Everything a warp needs about a work item, computed once per CTA.
@@ -187,6 +197,7 @@ __device__ __forceinline__ void item_coords(const TcParams& p, int item, int n_t
 }
 
 // The fields that follow from (expert, rows, projection, row block).
+template <int MT>
 __device__ __forceinline__ void finish_item(const TcParams& p, Item& it) {
   const int code = __ldg(p.expert_slot + it.e);
   it.tier = code >> 24;
@@ -194,16 +205,17 @@ __device__ __forceinline__ void finish_item(const TcParams& p, Item& it) {
   it.n = max(16, (it.mc + 15) & ~15);
   it.r0 = p.pj[it.prj].gate_up ? it.nb * 64 : it.nb * 128;
   it.sps = stages_per_slot(it.tier);
-  it.per_slot = b_stages_per_slot(it.n);
+  it.per_slot = b_slot_stages(MT, it.n);
 }
 
+template <int MT>
 __device__ __forceinline__ Item make_item(const TcParams& p, int item, int n_tiles) {
   Item it;
   item_coords(p, item, n_tiles, it.prj, it.tile, it.nb);
   it.e = __ldcg(p.tile_info + 3 * it.tile);
   it.m0 = __ldcg(p.tile_info + 3 * it.tile + 1);
   it.mc = __ldcg(p.tile_info + 3 * it.tile + 2);
-  finish_item(p, it);
+  finish_item<MT>(p, it);
   return it;
 }
 
@@ -252,9 +264,10 @@ __device__ __forceinline__ bool wait_progress(const int* ctr, int target, uint32
 
 // The CTA's li-th work item (global index `item`): from the shared table for
 // the first kItemTab, else from global memory.  False for an unknown tier.
+template <int MT>
 __device__ __forceinline__ bool decode_item(const TcParams& p, const Item* tab, int li, int item,
                                             int n_tiles, Item& it) {
-  it = li < kItemTab ? tab[li] : make_item(p, item, n_tiles);
+  it = li < kItemTab ? tab[li] : make_item<MT>(p, item, n_tiles);
   return it.tier == kTierINT4 || it.tier == kTierINT8 || it.tier == kTierBF16;
 }
 
@@ -421,7 +434,12 @@ __device__ __forceinline__ bool mma_slot(const MmaItem& mi, uint32_t abuf, int k
   return true;
 }
 
+template <int MT>
 __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_constant__ TcParams p) {
+  static_assert(MT == kMaxN || MT == kWideN, "tile heights");
+  constexpr int NG = MT == kWideN ? 2 : kDqGroups;  // dequant groups = TMEM A buffers
+  constexpr int kTmemA = 2 * MT;                     // first tensor-memory column of the A buffers
+  static_assert(kTmemA + NG * kACols == kTmemCols, "tensor-memory columns");
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
@@ -449,7 +467,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
       mbar_init(W_full(i), 1);
       mbar_init(W_empty(i), kDqGroupWarps);
     }
-    for (int i = 0; i < kABufs; ++i) {
+    for (int i = 0; i < NG; ++i) {
       mbar_init(A_full(i), kDqGroupWarps);
       mbar_init(A_empty(i), 1);
     }
@@ -474,7 +492,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
   } else if (threadIdx.x == 32 * kWarpB) {
     for (int j = 0; j < 2; ++j) {
       if (j == 0 ? !p.run_gu : !p.run_dn) continue;
-      for (int i = 0; i < 4; ++i) tma_prefetch_desc(&p.pj[j].tm_b[i]);
+      for (int i = 0; i < (MT == kWideN ? 1 : 4); ++i) tma_prefetch_desc(&p.pj[j].tm_b[i]);
     }
   }
   if (warp == kWarpMma) {
@@ -523,7 +541,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
       int rs = 0, ts = 0;
       for (int e = lo; e < hi; ++e) {
         rs += cnt[e];
-        ts += (cnt[e] + kMaxN - 1) / kMaxN;
+        ts += (cnt[e] + MT - 1) / MT;
       }
       int rx = rs, tx = ts;
 #pragma unroll
@@ -542,7 +560,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
         rbase[e] = rx;
         tstart[e] = tx;
         rx += cnt[e];
-        tx += (cnt[e] + kMaxN - 1) / kMaxN;
+        tx += (cnt[e] + MT - 1) / MT;
       }
     }
     __syncthreads();
@@ -561,9 +579,9 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
       }
       const int lt = it.tile - tstart[lo];
       it.e = lo;
-      it.m0 = rbase[lo] + lt * kMaxN;
-      it.mc = min(kMaxN, cnt[lo] - lt * kMaxN);
-      finish_item(p, it);
+      it.m0 = rbase[lo] + lt * MT;
+      it.mc = min(MT, cnt[lo] - lt * MT);
+      finish_item<MT>(p, it);
       items_tab[t] = it;
     }
   } else {
@@ -572,7 +590,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
     const int n_items0 = num_items(p, n_tiles);
     for (int t = threadIdx.x; t < kItemTab; t += kThreads) {
       const int item = static_cast<int>(blockIdx.x) + t * static_cast<int>(gridDim.x);
-      if (item < n_items0) items_tab[t] = make_item(p, item, n_tiles);
+      if (item < n_items0) items_tab[t] = make_item<MT>(p, item, n_tiles);
     }
   }
   const int n_items = num_items(p, n_tiles);
@@ -588,7 +606,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
     int issued = 0;
     for (int item = blockIdx.x, li = 0; item < n_items && !aborted(); item += gridDim.x, ++li) {
       Item it;
-      if (!decode_item(p, items_tab, li, item, n_tiles, it)) {
+      if (!decode_item<MT>(p, items_tab, li, item, n_tiles, it)) {
         if (lane == 0) atomicOr(p.status, EXQ_DEV_BAD_TIER);
         continue;
       }
@@ -648,11 +666,12 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
     int issued = 0;
     for (int item = blockIdx.x, li = 0; item < n_items && !aborted(); item += gridDim.x, ++li) {
       Item it;
-      if (!decode_item(p, items_tab, li, item, n_tiles, it)) continue;
+      if (!decode_item<MT>(p, items_tab, li, item, n_tiles, it)) continue;
       const ProjParams& pj = p.pj[it.prj];
       const int nk = pj.k / kKS;
       const int per_slot = it.per_slot;
-      const uint32_t stage_bytes = static_cast<uint32_t>(it.n) * 128u;
+      const int box_rows = MT == kWideN ? kWideN : it.n;
+      const uint32_t stage_bytes = static_cast<uint32_t>(box_rows) * 128u;
       if (p.link && it.prj == 1) {
         // the tile's mid rows come from nb_gu gate_up items of this launch
         bool ok = true;
@@ -679,7 +698,8 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
         if (elect_one()) {
           // the whole slot in one box: n rows x per_slot stages (stages past k read as zeros)
           mbar_arrive_tx(bar, static_cast<uint32_t>(per_slot) * stage_bytes);
-          tma_load_3d(sB + r.idx * kBSlot, &pj.tm_b[(it.n >> 4) - 1], bar, 0, it.m0, kc0);
+          tma_load_3d(sB + r.idx * kBSlot, &pj.tm_b[MT == kWideN ? 0 : (it.n >> 4) - 1], bar, 0,
+                      it.m0, kc0);
         }
         __syncwarp();
         r.next(kBStages);
@@ -707,7 +727,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
     const uint64_t bdesc0 = smem_desc_sw128(sB);
     for (int item = blockIdx.x, li = 0; item < n_items && !aborted(); item += gridDim.x, ++li) {
       Item it;
-      if (!decode_item(p, items_tab, li, item, n_tiles, it)) continue;
+      if (!decode_item<MT>(p, items_tab, li, item, n_tiles, it)) continue;
       const int ab = count & 1;
       const uint32_t acc_phase = (count >> 1) & 1;
       ++count;
@@ -717,11 +737,12 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
       }
       tc_fence_after();
       MmaItem mi;
-      mi.d = tmem + ab * kMaxN;
+      mi.d = tmem + ab * MT;
       mi.idesc = idesc_f16_m128(it.n);
       mi.nk = p.pj[it.prj].k / kKS;
       mi.per_slot = it.per_slot;
-      mi.stage_desc = static_cast<uint32_t>(it.n) * 8u;  // n rows x 128 B, in 16 B units
+      // rows of one B stage x 128 B, in 16 B units
+      mi.stage_desc = static_cast<uint32_t>(MT == kWideN ? kWideN : it.n) * 8u;
       mi.bdesc0 = bdesc0;
       mi.bar_bfull = B_full(0);
       mi.bar_bempty = B_empty(0);
@@ -742,7 +763,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
         if (!ok) break;
         if (elect_one()) tc_commit(A_empty(ra.idx));
         __syncwarp();
-        ra.next(kABufs);
+        ra.next(NG);
       }
       if (!ok) {
         do_abort();
@@ -762,7 +783,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
     // the barrier after each accumulator wait.
     for (int item = blockIdx.x, li = 0; item < n_items; item += gridDim.x, ++li, ++count) {
       Item it;
-      if (!decode_item(p, items_tab, li, item, n_tiles, it)) {
+      if (!decode_item<MT>(p, items_tab, li, item, n_tiles, it)) {
         --count;
         continue;
       }
@@ -775,7 +796,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
         break;
       }
       tc_fence_after();
-      const uint32_t taddr = tmem + (static_cast<uint32_t>(32 * quarter) << 16) + ab * kMaxN;
+      const uint32_t taddr = tmem + (static_cast<uint32_t>(32 * quarter) << 16) + ab * MT;
       if (pj.gate_up) {
         // rows in blocks of 8: gate rows have bit 3 clear, the matching up row is row ^ 8
         const int g = it.r0 + ((row >> 4) << 3) + (row & 7);
@@ -853,9 +874,10 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
     // combine warps: nothing during the items (the combine below)
   } else {
     // ---------------------------------------------------------- dequant
-    // Group g = (warp - kDqWarp0) / 4 converts weight slots gs = g, g+3, ...
+    // Group g = (warp - kDqWarp0) / 4 converts weight slots gs = g, g+NG, ...
     // (gs counts slots over all items): ring position gs % 6 and A buffer
-    // gs % 3 == g.  The warp's lane quarter is warp % 4 (tensor-memory rule).
+    // gs % NG == g.  The warp's lane quarter is warp % 4 (tensor-memory rule).
+    // With two groups (128-token items) warps 15-18 have no slots.
     const int grp = (warp - kDqWarp0) >> 2;
     const int m = 32 * (warp & 3) + lane;
     const uint32_t tlane = static_cast<uint32_t>(32 * (warp & 3)) << 16;
@@ -864,7 +886,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
     uint32_t gs = 0;  // global slot counter of this CTA
     for (int item = blockIdx.x, li = 0; item < n_items && !aborted(); item += gridDim.x, ++li) {
       Item it;
-      if (!decode_item(p, items_tab, li, item, n_tiles, it)) continue;
+      if (!decode_item<MT>(p, items_tab, li, item, n_tiles, it)) continue;
       const int nk = p.pj[it.prj].k / kKS;
       const int sps = it.sps;
       // gate_up interleaves gate/up rows in blocks of 8 (the epilogue pairs lanes m, m^8)
@@ -872,10 +894,10 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
       const int swz = lw & 7;
       bool ok = true;
       for (int kc0 = 0; kc0 < nk; kc0 += sps, ++gs) {
-        if (static_cast<int>(gs % kDqGroups) != grp) continue;
+        if (static_cast<int>(gs % NG) != grp) continue;
         const int ns = min(sps, nk - kc0);
         const uint32_t wi = gs % kWStages, wph = (gs / kWStages) & 1;
-        const uint32_t aph = (gs / kABufs) & 1;
+        const uint32_t aph = (gs / NG) & 1;
         bool got = mbar_wait(a_empty, aph ^ 1, p.status);
         if (got) got = mbar_wait(W_full(wi), wph, p.status);
         if (!__all_sync(0xffffffffu, got)) {
@@ -1130,7 +1152,7 @@ static bool make_map_nd(CUtensorMap* m, CUtensorMapDataType dt, const void* ptr,
 
 // Fill the per-projection maps.  proj 0 = w13 (rows 2I, k = H), 1 = w2 (rows H, k = I).
 static int build_maps(const exq_moe_weights* w, int proj, const void* act, int64_t n_pos,
-                      ProjParams& p) {
+                      int mt, ProjParams& p) {
   const int64_t I = w->inter, H = w->hidden;
   const int64_t rows = proj == 0 ? 2 * I : H;
   const int64_t k = proj == 0 ? H : I;
@@ -1185,12 +1207,13 @@ static int build_maps(const exq_moe_weights* w, int proj, const void* act, int64
   (void)n8;
   (void)n16;
   // activations stage-major [k/64][n_pos][64]: (element, row, stage); map b has a
-  // box of N = 16(b+1) rows x the stages of one B slot
-  for (int b = 0; b < 4; ++b) {
-    const uint32_t nb = 16u * (b + 1);
+  // box of N = 16(b+1) rows x the stages of one B slot (64-token items), or
+  // one map of 128 rows x 2 stages (128-token items)
+  for (int b = 0; b < (mt == kWideN ? 1 : 4); ++b) {
+    const uint32_t nb = mt == kWideN ? kWideN : 16u * (b + 1);
     const uint64_t d[3] = {64, (uint64_t)n_pos, (uint64_t)(k / 64)};
     const uint64_t s3[2] = {128, (uint64_t)n_pos * 128};
-    const uint32_t bx[3] = {64, nb, (uint32_t)b_stages_per_slot((int)nb)};
+    const uint32_t bx[3] = {64, nb, (uint32_t)b_slot_stages(mt, (int)nb)};
     if (!make_map_nd(&p.tm_b[b], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, act, 3, d, s3, bx,
                      CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B))
       return EXQ_ERR_CUDA;
@@ -1201,28 +1224,30 @@ static int build_maps(const exq_moe_weights* w, int proj, const void* act, int64
   return EXQ_OK;
 }
 
-int launch_tc(const TcParams& p, int max_items, cudaStream_t stream, bool pdl) {
-  static int attr_done[64] = {0};
+int launch_tc(const TcParams& p, int mt, int max_items, cudaStream_t stream, bool pdl) {
+  static int attr_done[2][64] = {{0}};
   static int sms[64] = {0};
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64) dev = 0;
-  if (!attr_done[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(moe_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         kSmemBytes);
+  const int wide = mt == kWideN;
+  if (!attr_done[wide][dev]) {
+    cudaError_t e = cudaFuncSetAttribute(wide ? moe_tc_kernel<kWideN> : moe_tc_kernel<kMaxN>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
     if (e != cudaSuccess) {
       set_error("moe_tc_kernel: cannot reserve %d B of shared memory: %s", kSmemBytes,
                 cudaGetErrorString(e));
       return EXQ_ERR_CUDA;
     }
     sms[dev] = num_sms();
-    attr_done[dev] = 1;
+    attr_done[wide][dev] = 1;
   }
   int grid = sms[dev];
   if (max_items < grid) grid = max_items;
   if (grid < 1) grid = 1;
   const cudaError_t e =
-      launch_pdl(pdl, moe_tc_kernel, dim3(grid), dim3(kThreads), kSmemBytes, stream, p);
+      wide ? launch_pdl(pdl, moe_tc_kernel<kWideN>, dim3(grid), dim3(kThreads), kSmemBytes, stream, p)
+           : launch_pdl(pdl, moe_tc_kernel<kMaxN>, dim3(grid), dim3(kThreads), kSmemBytes, stream, p);
   if (e != cudaSuccess) {
     set_error("moe_tc_kernel: %s", cudaGetErrorString(e));
     return EXQ_ERR_CUDA;
@@ -1263,7 +1288,14 @@ using namespace exq;
 
 namespace {
 
-constexpr int kLayerMT = tc::kMaxN;  // tokens per GEMM tile (the MMA's N)
+// Tokens per GEMM tile (the MMA's N): 128 when the call averages at least 256
+// rows per expert bucket (prefill, expert-parallel receive areas), which halves
+// how often an expert's weights are streamed and converted; else 64, the decode
+// build (a 128-token item holds both accumulators' worth of columns, so
+// narrow decode tiles would pay for it).
+int layer_mt(int64_t n_slots, int64_t n_buckets) {
+  return n_buckets > 0 && n_slots >= 256 * n_buckets ? tc::kWideN : tc::kMaxN;
+}
 
 struct TcWs {
   int32_t* sorted_slot;
@@ -1278,6 +1310,7 @@ struct TcWs {
   __half* mid;
   float* partial;
   int64_t max_tiles;
+  int mt;              // tokens per GEMM tile
   int64_t n_counters;  // ints from tile_done on (one contiguous run)
   size_t bytes;
 };
@@ -1291,7 +1324,8 @@ TcWs carve_tc(void* base, int64_t n_slots, int64_t n_tokens, int n_buckets, int6
     off = align_up(off + bytes, 256);
     return base ? static_cast<char*>(base) + o : nullptr;
   };
-  w.max_tiles = n_slots / kLayerMT + (n_slots < n_buckets ? n_slots : n_buckets) + 1;
+  w.mt = layer_mt(n_slots, n_buckets);
+  w.max_tiles = n_slots / w.mt + (n_slots < n_buckets ? n_slots : n_buckets) + 1;
   w.sorted_slot = reinterpret_cast<int32_t*>(take(4 * n_slots));
   w.pos_of_slot = reinterpret_cast<int32_t*>(take(4 * n_slots));
   w.sorted_w = reinterpret_cast<float*>(take(4 * n_slots));
@@ -1417,7 +1451,7 @@ extern "C" int exq_moe_layer_forward_range(const exq_moe_weights* w, const void*
     rg.spt = spt;
     rg.n_routed = w->n_routed;
     rg.n_buckets = n_total;
-    rg.mt = kLayerMT;
+    rg.mt = ws.mt;
     rg.n = n_slots;
     rg.act = ws.act;
     rg.pos_of_slot = ws.pos_of_slot;
@@ -1442,7 +1476,7 @@ extern "C" int exq_moe_layer_forward_range(const exq_moe_weights* w, const void*
     rp.n_routed = w->n_routed;
     rp.top_k = top_k;
     rp.slots_per_token = spt;
-    rp.mt = kLayerMT;
+    rp.mt = ws.mt;
     rp.sorted_i32 = ws.sorted_slot;
     rp.pos_of_slot = ws.pos_of_slot;
     rp.sorted_w = ws.sorted_w;
@@ -1460,7 +1494,7 @@ extern "C" int exq_moe_layer_forward_range(const exq_moe_weights* w, const void*
   }
   if (!fused && first_stage <= 1 && end_stage > 1) {
     st = tc::launch_prep(hidden_states, act_dtype, H, n_tokens, ws.sorted_slot, spt, n_slots,
-                         ws.ends + n_total, kLayerMT, ws.act, s, chained);
+                         ws.ends + n_total, ws.mt, ws.act, s, chained);
     if (st != EXQ_OK) return st;
     chained = true;
   }
@@ -1470,7 +1504,7 @@ extern "C" int exq_moe_layer_forward_range(const exq_moe_weights* w, const void*
     for (int proj = 0; proj < 2; ++proj) {
       if (!(proj == 0 ? do_gu : do_dn)) continue;
       tc::ProjParams& pj = p.pj[proj];
-      st = tc::build_maps(w, proj, proj == 0 ? ws.act : ws.mid, n_slots, pj);
+      st = tc::build_maps(w, proj, proj == 0 ? ws.act : ws.mid, n_slots, ws.mt, pj);
       if (st != EXQ_OK) return st;
       pj.gate_up = proj == 0;
       pj.nblocks = static_cast<int>(proj == 0 ? I / 64 : H / 128);
@@ -1522,7 +1556,7 @@ extern "C" int exq_moe_layer_forward_range(const exq_moe_weights* w, const void*
     p.n_routed = w->n_routed;
     p.n_buckets = n_total;
     p.n_slots = n_slots;
-    st = tc::launch_tc(p, static_cast<int>(max_items < INT32_MAX ? max_items : INT32_MAX), s,
+    st = tc::launch_tc(p, ws.mt, static_cast<int>(max_items < INT32_MAX ? max_items : INT32_MAX), s,
                        chained);
     if (st != EXQ_OK) return st;
     chained = true;

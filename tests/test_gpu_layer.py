@@ -369,3 +369,30 @@ def test_layer_mixtral_prefill_4096(cuda):
     assert torch.equal(ys, y[sample.to(cuda)])
     ref = oracle_layer(bank, x, ids, w, tokens=sample)
     assert OM.rel_l2(ys, ref) < TOL
+
+
+@pytest.mark.parametrize("cfg,t,tiers", [("mixtral", 1024, None), ("olmoe_mixed", 2048, "mixed"),
+                                         ("qwen3", 4096, None)])
+def test_layer_128_token_tiles(cuda, cfg, t, tiers):
+    """Calls averaging >= 256 rows per expert run 128-token tiles: Mixtral
+    T=1024 (2048 slots, fused routing, the combine in the GEMM launch), OLMoE
+    mixed tiers T=2048 and Qwen3 T=4096 (separate routing).  A token sample
+    against the oracle, the sample run alone bit for bit (64-token tiles
+    there), and the launch chain against separately launched stages."""
+    from exq_b200.synth import CONFIGS, hidden_states, tier_plan, zipf_router
+    c0 = CONFIGS[cfg]
+    tl = tier_plan(c0.n_experts, seed=0) if tiers else None
+    bank, c = _bank(cfg, cuda, tiers=tl)
+    ids, w = zipf_router(t, c.n_experts, c.top_k, seed=90 + t)
+    assert ids.numel() >= 256 * c.n_experts   # the 128-token tile rule
+    x = hidden_states(t, c.hidden, seed=90 + t, dtype=c.act_dtype)
+    xd, idd, wd = x.to(cuda), ids.to(cuda), w.to(cuda)
+    y, y_sep, y_alone = _stage_runs(bank, xd, idd, wd)
+    assert torch.equal(y, y_sep)
+    assert torch.equal(y, y_alone)
+    sample = torch.tensor([0, 1, 7, t // 3, t // 2, t - 2, t - 1])
+    sd = sample.to(cuda)
+    ys = bank(xd[sd], idd[sd], wd[sd])
+    assert torch.equal(ys, y[sd])
+    ref = oracle_layer(bank, x, ids, w, tokens=sample)
+    assert OM.rel_l2(ys, ref) < TOL
