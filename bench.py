@@ -691,6 +691,28 @@ def ep_measure(dev, world, rank, name, steps=50, warmup=5):
         dist.all_reduce(rel, op=dist.ReduceOp.MAX)
         out["rel_l2_vs_one_gpu"] = float(f"{rel.item():.3e}")
         del full
+        # rows this rank's experts receive, and the phases of one peer step
+        # (events on each rank's stream, host synchronised between steps, so
+        # the dispatch phase includes its launch; mean of 20 steps)
+        recv = int(((torch.cat(all_ids) >= rank * per) & (torch.cat(all_ids) < (rank + 1) * per))
+                   .sum().item())
+        ph = torch.zeros(5, device=dev, dtype=torch.float64)
+        if layer.peer is not None:
+            reps = 20
+            for _ in range(reps):
+                ev = [torch.cuda.Event(enable_timing=True) for _ in range(5)]
+                torch.cuda.synchronize(dev)
+                dist.barrier()
+                layer(x, ids, w, events=ev)
+                torch.cuda.synchronize(dev)
+                for i in range(4):
+                    ph[i] += ev[i].elapsed_time(ev[i + 1]) * 1e3 / reps
+        ph[4] = recv
+        allph = [torch.empty_like(ph) for _ in range(world)]
+        dist.all_gather(allph, ph)
+        out["recv_rows"] = [int(v[4].item()) for v in allph]
+        out["phases_us"] = {name_: [round(float(v[i].item()), 1) for v in allph]
+                            for i, name_ in enumerate(("dispatch", "shared", "experts", "combine"))}
     if world == 1 and name == "mixtral":
         out["prefill"] = prefill_measure(layer, c, dev)
     if world > 1 and layer.peer is not None:

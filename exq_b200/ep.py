@@ -272,18 +272,22 @@ class ExpertParallelLayer:
         return self.shared_bank(hidden, ids.contiguous(), w)
 
     def forward(self, hidden: torch.Tensor, topk_ids: torch.Tensor,
-                topk_weights: torch.Tensor, check: bool = False) -> torch.Tensor:
+                topk_weights: torch.Tensor, check: bool = False,
+                events: list | None = None) -> torch.Tensor:
         """[T, H] output for this rank's T tokens (same dtype as ``hidden``).
 
         Expert ids out of range are dropped and flagged in the device status,
         as in the single-GPU layer.  Every rank passes the same activation
         dtype: a rank runs its experts on the rows it receives in the dtype of
         its own ``hidden``.  ``check``: synchronise after the step and raise if
-        a kernel flagged an error (``check_status``)."""
+        a kernel flagged an error (``check_status``).  ``events``: five CUDA
+        events recorded on the current stream around the peer exchange's
+        phases (dispatch, shared experts, local expert stages with the wait
+        for the arrivals, combine with the wait for the returns)."""
         if topk_ids.shape != topk_weights.shape or topk_ids.shape[0] != hidden.shape[0]:
             raise ValueError("topk_ids / topk_weights must be [T, k] for hidden [T, H]")
         if self.peer is not None:
-            y = self._forward_peer(hidden, topk_ids, topk_weights)
+            y = self._forward_peer(hidden, topk_ids, topk_weights, events)
             if check:
                 self.check_status()
             return y
@@ -322,7 +326,7 @@ class ExpertParallelLayer:
             self.check_status()
         return y
 
-    def _forward_peer(self, hidden, topk_ids, topk_weights):
+    def _forward_peer(self, hidden, topk_ids, topk_weights, events=None):
         px, bank, lib = self.peer, self.local_bank, L.lib()
         t, k = topk_ids.shape
         if t * k > px.capacity:
@@ -343,19 +347,25 @@ class ExpertParallelLayer:
             raise ValueError(f"hidden size {h} differs from the exchange's {px.hidden}")
         s = L.stream_of(dev)
         slot_row = torch.empty(t * k, dtype=torch.int32, device=dev)
+        mark = (lambda i: events[i].record()) if events is not None else (lambda i: None)
+        mark(0)
         L.check(lib.exq_ep_dispatch(L.ptr(ids), L.tag(ids), t, k, self.per_rank, self.world,
                                     self.rank, L.ptr(x), L.tag(x), h, px.capacity,
                                     L.ptr(px.peers), L.ptr(slot_row), s), "ep_dispatch")
+        mark(1)
         shared = self.shared_fn(x)
+        mark(2)
         ws = self._ws
         L.check(lib.exq_ep_expert_forward(C.byref(bank.cstruct), L.tag(x), self.world, self.rank,
                                           px.capacity, px.ptr, L.ptr(px.peers), L.ptr(ws),
                                           ws.numel(), s), "ep_expert_forward")
+        mark(3)
         y = torch.empty(t, h, dtype=x.dtype, device=dev)
         L.check(lib.exq_ep_combine_peer(px.ptr, self.world, px.capacity, h, L.tag(x),
                                         L.ptr(slot_row), L.ptr(w), L.tag(w), t, k,
                                         None if shared is None else L.ptr(shared), L.ptr(y), s),
                 "ep_combine_peer")
+        mark(4)
         return y
 
     __call__ = forward
