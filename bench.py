@@ -211,7 +211,8 @@ def cpu_baseline(budget_s=12.0):
     value = total_b / sum(times) / 1e9
     return {"value": round(value, 3), "unit": UNIT, "cores": meta["threads"], "kind": "port",
             "sample": f"{len(times)} full T=256 layer calls (oracle torch fp32 path, dequantised "
-                      f"weights cached), {sum(times):.1f} s, median {1e3 * statistics.median(times):.1f} ms/call"}
+                      f"weights cached), {sum(times):.1f} s, mean {1e3 * sum(times) / len(times):.1f} "
+                      f"ms/call (value), median {1e3 * statistics.median(times):.1f}"}
 
 
 def reference_arm(args):
@@ -230,10 +231,11 @@ def reference_arm(args):
                for _ in range(8)]
     for i in range(args.warmup):
         run(samples[i % 8])
-    tot_t, tot_b = 0.0, 0
+    tot_t, tot_b, per = 0.0, 0, []
     for i in range(args.steps):
         s = samples[i % 8]
-        tot_t += run(s)
+        per.append(run(s))
+        tot_t += per[-1]
         tot_b += nbytes(s)
     value = tot_b / tot_t / 1e9
     line = {
@@ -246,8 +248,9 @@ def reference_arm(args):
         "cpu_baseline": {"value": round(value, 3), "unit": UNIT, "cores": meta["threads"],
                          "kind": "port",
                          "sample": f"each step: {n_tok} of the 256 tokens (seeded), full T=256 "
-                                   f"call = {1e3 * t_full:.0f} ms; rank 0 only, host cores, "
-                                   f"dequantised fp32 weights cached"},
+                                   f"call = {1e3 * t_full:.0f} ms; mean {1e3 * tot_t / args.steps:.1f} "
+                                   f"ms/step (value), median {1e3 * statistics.median(per):.1f}; "
+                                   f"rank 0 only, host cores, dequantised fp32 weights cached"},
         "e2e": {"value": round(value, 3), "unit": UNIT, "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
