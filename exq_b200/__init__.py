@@ -13,12 +13,14 @@ from .kernels import (  # noqa: F401
     moe_int4_full_forward,
     pack_experts_int4,
     pack_int4_weights,
+    router_topk,
     sort_tokens_by_expert,
     unsort_output,
 )
 from .experts import ExpertBank  # noqa: F401
 
 __all__ = [
+    "router_topk",
     "moe_grouped_gemm",
     "sort_tokens_by_expert",
     "moe_int4_forward",

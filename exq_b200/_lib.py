@@ -65,6 +65,7 @@ SIGNATURES = {
     "exq_combine_noalloc": (C.c_int, [vp, C.c_int, i64, i64, vp, vp, C.c_int, i64, i32, vp,
                                       C.c_int, vp]),
     "exq_silu_and_mul": (C.c_int, [vp, vp, C.c_int, i64, i64, vp]),
+    "exq_router_topk": (C.c_int, [vp, C.c_int, i64, i32, i32, i32, vp, vp, vp]),
     "exq_pack_int4": (C.c_int, [vp, C.c_int, i64, i64, i32, vp, vp, vp]),
     "exq_quant_int8": (C.c_int, [vp, C.c_int, i64, i64, vp, vp, vp]),
     "exq_moe_gemm_workspace_bytes": (sz, [i64, i32, i32]),

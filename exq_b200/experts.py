@@ -269,9 +269,22 @@ class ExpertBank:
         """The five stages route -> prep -> gate_up -> down -> weighted combine.
 
         Up to 4096 (token, expert) slots the route and prep stages are one
-        fused launch and gate_up rebuilds its tile list from the ids, so a
-        call is four launches; above that it is five."""
+        fused launch, and gate_up, down and the combine are one GEMM launch
+        that builds its tile list from the ids: two launches per call.  Above
+        that, routing and the activation prep are separate launches (three)."""
         return self.forward_range(hidden_states, topk_ids, topk_weights, 0, 5, out, workspace)
+
+    def forward_from_logits(self, hidden_states: torch.Tensor, router_logits: torch.Tensor,
+                            top_k: int, renormalize: bool = True,
+                            out: torch.Tensor | None = None) -> torch.Tensor:
+        """The layer from router logits [T, n_routed]: the fused router top-k
+        (softmax, top_k, optional renormalisation; ``kernels.router_topk``)
+        feeding the routing stage.  Three launches up to 4096 slots."""
+        from .kernels import router_topk
+        if router_logits.dim() != 2 or router_logits.shape[1] != self.n_routed:
+            raise ValueError(f"router_logits must be [T, {self.n_routed}]")
+        ids, w = router_topk(router_logits, top_k, renormalize)
+        return self.forward(hidden_states, ids, w, out)
 
     def forward_range(self, hidden_states, topk_ids, topk_weights, first: int, end: int,
                       out=None, workspace=None):

@@ -171,7 +171,27 @@ def unsort_output(sorted_output: torch.Tensor, router_indices: torch.Tensor,
     return result
 
 
+def router_topk(router_logits: torch.Tensor, top_k: int, renormalize: bool = True):
+    """``(topk_ids int32 [T, k], topk_weights fp32 [T, k])`` from router logits
+    ``[T, E]`` (fp32/fp16/bf16): softmax, the ``top_k`` largest probabilities
+    (descending; equal ones by lower expert id), divided by their sum when
+    ``renormalize``.  The routing the reference's generated layers compute
+    (exq/codegen/triton_emitter.py:273-276), i.e. SGLang's ``topk_output``
+    (exq/runtime/sglang_backend.py:88-90), in one kernel."""
+    dev = L.require_cuda(router_logits)
+    if router_logits.dim() != 2:
+        raise ValueError("router_logits must be [T, E]")
+    x = router_logits.contiguous()
+    t, e = x.shape
+    ids = torch.empty(t, top_k, dtype=torch.int32, device=dev)
+    w = torch.empty(t, top_k, dtype=torch.float32, device=dev)
+    L.check(L.lib().exq_router_topk(L.ptr(x), L.tag(x), t, e, int(top_k), int(bool(renormalize)),
+                                    L.ptr(ids), L.ptr(w), L.stream_of(dev)), "router_topk")
+    return ids, w
+
+
 __all__ = [
+    "router_topk",
     "moe_grouped_gemm",
     "sort_tokens_by_expert",
     "moe_int4_forward",

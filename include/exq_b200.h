@@ -172,6 +172,21 @@ EXQ_API int exq_combine_noalloc(const void* down_out, int dtype, int64_t n_activ
                                 const void* router_weights, int w_dtype, int64_t n_tokens,
                                 int32_t top_k, void* result, int out_dtype, void* stream);
 
+/* Router top-k, the step before the expert path: the reference's generated
+ * MoE layers compute it as softmax -> torch.topk -> divide by the sum
+ * (exq/codegen/triton_emitter.py:273-276), and SGLang hands the result to
+ * _exq_forward_cuda as topk_output (exq/runtime/sglang_backend.py:88-90).
+ * Per token: p = softmax(logits) in fp32, the top_k largest p in descending
+ * order (equal p: the lower expert id first), and with renormalize != 0 the
+ * selected p divided by their sum (summed in that order).
+ * logits [n_tokens, n_experts] fp32/fp16/bf16, row stride n_experts;
+ * 1 <= n_experts <= 1024; 1 <= top_k <= min(32, n_experts).
+ * Out: topk_ids int32 [n_tokens, top_k], topk_weights fp32 [n_tokens, top_k]
+ * (the ids/weights arguments of exq_moe_layer_forward). */
+EXQ_API int exq_router_topk(const void* logits, int logits_dtype, int64_t n_tokens,
+                            int32_t n_experts, int32_t top_k, int32_t renormalize,
+                            int32_t* topk_ids, float* topk_weights, void* stream);
+
 /* sgl_kernel.silu_and_mul (exq/runtime/sglang_backend.py:138-140):
  * out[m, i] = silu(x[m, i]) * x[m, I + i], fp32 math. */
 EXQ_API int exq_silu_and_mul(const void* input, void* out, int dtype, int64_t m, int64_t inter,

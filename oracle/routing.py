@@ -141,3 +141,23 @@ def silu_and_mul(x: np.ndarray, out_dtype=np.float16) -> np.ndarray:
     i = xf.shape[-1] // 2
     g, u = xf[..., :i], xf[..., i:]
     return (g / (np.float32(1.0) + np.exp(-g)) * u).astype(out_dtype)
+
+
+def router_topk(logits, top_k: int, renormalize: bool = True):
+    """Router top-k as the reference's generated MoE layers compute it
+    (exq/codegen/triton_emitter.py:273-276): ``softmax`` over the experts in
+    fp32, ``torch.topk`` of the probabilities, then the selected weights
+    divided by their sum (the renormalisation; SGLang's ``topk_output`` that
+    exq/runtime/sglang_backend.py:88-90 receives is the same computation).
+    Returns (ids int64 [T, k], weights fp32 [T, k]), weights in descending
+    order.  Equal probabilities are ordered by the lower expert id here (the
+    reference leaves that to torch.topk)."""
+    import torch
+    p = torch.softmax(torch.as_tensor(logits).float(), dim=-1)
+    t, e = p.shape
+    # stable descending order: sort by (-p, expert)
+    order = torch.argsort(-p, dim=-1, stable=True)[:, :top_k]
+    w = torch.gather(p, 1, order)
+    if renormalize:
+        w = w / w.sum(dim=-1, keepdim=True)
+    return order, w

@@ -210,3 +210,62 @@ def test_bad_expert_id_is_flagged_not_faulting(cuda):
     D.dispatch(ids, so, se, ends, 4)
     assert L.read_device_status(cuda) & L.DEV_BAD_EXPERT_ID
     assert ends.cpu().tolist() == [0, 1, 2, 3, 3]   # the bad slot is dropped
+
+
+ROUTER_CASES = [(1, 8, 2, torch.float32), (37, 64, 8, torch.bfloat16), (256, 128, 8, torch.float16),
+                (4096, 8, 2, torch.bfloat16), (100, 160, 6, torch.float32), (9, 1024, 32, torch.float32),
+                (3, 32, 32, torch.float16), (64, 60, 1, torch.float32)]
+
+
+@pytest.mark.parametrize("t,e,k,dt", ROUTER_CASES)
+@pytest.mark.parametrize("renorm", [True, False])
+def test_router_topk_vs_oracle(cuda, t, e, k, dt, renorm):
+    """Fused softmax -> top-k -> renormalise: ids exactly (descending, equal
+    probabilities by lower expert id), weights within 2e-6 relative (CUDA's
+    expf and a different summation order than torch's softmax)."""
+    from exq_b200 import router_topk
+    g = torch.Generator().manual_seed(t + 7 * e + k)
+    logits = (torch.randn(t, e, generator=g) * 2).to(dt)
+    ids, w = router_topk(logits.to(cuda), k, renorm)
+    r_ids, r_w = OR.router_topk(logits.float(), k, renorm)
+    assert ids.dtype == torch.int32 and w.dtype == torch.float32
+    assert torch.equal(ids.cpu().long(), r_ids)
+    torch.testing.assert_close(w.cpu(), r_w, rtol=2e-6, atol=1e-9)
+
+
+def test_router_topk_ties_and_errors(cuda):
+    from exq_b200 import router_topk
+    logits = torch.tensor([[0.5, 1.0, 1.0, 0.2, 1.0], [3.0, 3.0, 3.0, 3.0, 3.0]], device=cuda)
+    ids, w = router_topk(logits, 3, True)
+    assert ids.tolist() == [[1, 2, 4], [0, 1, 2]]
+    torch.testing.assert_close(w[1].cpu(), torch.full((3,), 1 / 3), rtol=1e-6, atol=0)
+    with pytest.raises(ValueError):
+        router_topk(logits, 6, True)            # top_k > n_experts
+    with pytest.raises(ValueError):
+        router_topk(torch.zeros(2, 1025, device=cuda), 2, True)
+    e_ids, e_w = router_topk(torch.zeros(0, 8, device=cuda), 2, True)
+    assert e_ids.shape == (0, 2) and e_w.shape == (0, 2)
+
+
+@pytest.mark.parametrize("cfg,t", [("qwen3", 64), ("mixtral", 16)])
+def test_layer_from_router_logits(cuda, cfg, t):
+    """The layer fed by the fused router equals the layer fed the oracle
+    router's ids and weights (same ids; weights within an ulp)."""
+    from _layer_helpers import oracle_layer
+    from exq_b200 import ExpertBank
+    from exq_b200.synth import CONFIGS, expert_weights, hidden_states
+    from oracle import moe as OM
+    c = CONFIGS[cfg]
+    w13, w2 = expert_weights(c.n_experts, c.inter, c.hidden, seed=3, dtype=torch.float16,
+                             device=cuda)
+    bank = ExpertBank.from_dense(w13, w2, None, act_dtype=c.act_dtype)
+    del w13, w2
+    g = torch.Generator().manual_seed(t)
+    logits = torch.randn(t, c.n_experts, generator=g)
+    x = hidden_states(t, c.hidden, seed=t, dtype=c.act_dtype)
+    y = bank.forward_from_logits(x.to(cuda), logits.to(cuda), c.top_k, True)
+    r_ids, r_w = OR.router_topk(logits, c.top_k, True)
+    ref = oracle_layer(bank, x, r_ids, r_w)
+    assert OM.rel_l2(y, ref) < 5e-3
+    y2 = bank(x.to(cuda), r_ids.to(cuda).int(), r_w.to(cuda))
+    assert OM.rel_l2(y, y2) < 1e-5
