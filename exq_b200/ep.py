@@ -266,10 +266,16 @@ class ExpertParallelLayer:
     def _shared_rows(self, hidden: torch.Tensor) -> torch.Tensor | None:
         if self.shared_bank is None:
             return None
-        s = self.shared_bank.n_routed
-        ids = torch.arange(s, dtype=torch.int32, device=hidden.device).expand(hidden.shape[0], s)
-        w = torch.ones(hidden.shape[0], s, dtype=torch.float32, device=hidden.device)
-        return self.shared_bank(hidden, ids.contiguous(), w)
+        s, t = self.shared_bank.n_routed, hidden.shape[0]
+        # every token to every shared expert with weight 1: built once per
+        # token count (no launches in a step, and stable for graph capture)
+        cache = self.__dict__.setdefault("_shared_args", {})
+        key = (t, hidden.device)
+        if key not in cache:
+            ids = torch.arange(s, dtype=torch.int32, device=hidden.device).expand(t, s).contiguous()
+            cache[key] = (ids, torch.ones(t, s, dtype=torch.float32, device=hidden.device))
+        ids, w = cache[key]
+        return self.shared_bank(hidden, ids, w)
 
     def forward(self, hidden: torch.Tensor, topk_ids: torch.Tensor,
                 topk_weights: torch.Tensor, check: bool = False,
