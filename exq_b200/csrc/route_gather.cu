@@ -139,17 +139,12 @@ __global__ void __launch_bounds__(kRgThreads) route_gather_kernel(const RouteGat
   const int chunk = (n + static_cast<int>(gridDim.x) - 1) / static_cast<int>(gridDim.x);
   const int s0 = min(n, static_cast<int>(blockIdx.x) * chunk), s1 = min(n, s0 + chunk);
 
-  // pass 1: bucket counts of all slots and of the slots before s0 (order-free).
-  // The lanes of a warp holding one bucket add their count once (few buckets,
-  // e.g. shared experts alone, would otherwise serialise on one counter).
-  for (int i0 = 0; i0 < n; i0 += kRgThreads) {
-    const int i = i0 + threadIdx.x;
-    const int e = i < n ? bkt[i] : -1;
-    const unsigned same = __match_any_sync(0xffffffffu, e);
-    const unsigned pre = same & __ballot_sync(0xffffffffu, i < s0);
-    if (e >= 0 && lane == __ffs(same) - 1) {
-      atomicAdd(&cnt_all[e], __popc(same));
-      if (pre) atomicAdd(&cnt_pre[e], __popc(pre));
+  // pass 1: bucket counts of all slots and of the slots before s0 (order-free)
+  for (int i = threadIdx.x; i < n; i += kRgThreads) {
+    const int e = bkt[i];
+    if (e >= 0) {
+      atomicAdd(&cnt_all[e], 1);
+      if (i < s0) atomicAdd(&cnt_pre[e], 1);
     }
   }
   __syncthreads();
