@@ -1288,13 +1288,14 @@ using namespace exq;
 
 namespace {
 
-// Tokens per GEMM tile (the MMA's N): 128 when the call averages at least 256
-// rows per expert bucket (prefill, expert-parallel receive areas), which halves
-// how often an expert's weights are streamed and converted; else 64, the decode
-// build (a 128-token item holds both accumulators' worth of columns, so
-// narrow decode tiles would pay for it).
+// Tokens per GEMM tile (the MMA's N): 128 when the call averages at least 128
+// rows per expert bucket (prefill, expert-parallel receive areas, large decode
+// batches), which halves how often an expert's weights are streamed and
+// converted; else 64, the decode build (at 64 rows per expert the 128-token
+// build is slower: Mixtral T=256 359 against 344 us; at 128 it is faster: T=512
+// 523 against 557 us).
 int layer_mt(int64_t n_slots, int64_t n_buckets) {
-  return n_buckets > 0 && n_slots >= 256 * n_buckets ? tc::kWideN : tc::kMaxN;
+  return n_buckets > 0 && n_slots >= 128 * n_buckets ? tc::kWideN : tc::kMaxN;
 }
 
 struct TcWs {

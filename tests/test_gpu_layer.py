@@ -374,7 +374,7 @@ def test_layer_mixtral_prefill_4096(cuda):
 @pytest.mark.parametrize("cfg,t,tiers", [("mixtral", 1024, None), ("olmoe_mixed", 2048, "mixed"),
                                          ("qwen3", 4096, None)])
 def test_layer_128_token_tiles(cuda, cfg, t, tiers):
-    """Calls averaging >= 256 rows per expert run 128-token tiles: Mixtral
+    """Calls averaging >= 128 rows per expert run 128-token tiles: Mixtral
     T=1024 (2048 slots, fused routing, the combine in the GEMM launch), OLMoE
     mixed tiers T=2048 and Qwen3 T=4096 (separate routing).  A token sample
     against the oracle, the sample run alone bit for bit (64-token tiles
@@ -384,7 +384,7 @@ def test_layer_128_token_tiles(cuda, cfg, t, tiers):
     tl = tier_plan(c0.n_experts, seed=0) if tiers else None
     bank, c = _bank(cfg, cuda, tiers=tl)
     ids, w = zipf_router(t, c.n_experts, c.top_k, seed=90 + t)
-    assert ids.numel() >= 256 * c.n_experts   # the 128-token tile rule
+    assert ids.numel() >= 128 * c.n_experts   # the 128-token tile rule
     x = hidden_states(t, c.hidden, seed=90 + t, dtype=c.act_dtype)
     xd, idd, wd = x.to(cuda), ids.to(cuda), w.to(cuda)
     y, y_sep, y_alone = _stage_runs(bank, xd, idd, wd)
