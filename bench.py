@@ -757,6 +757,55 @@ def prefill_measure(bank, c, dev, tokens=4096, steps=5):
             "peak_kind": "measured bf16 burst" if peak else None}
 
 
+def router_measure(dev, banks, tokens=256, reps=400):
+    """The fused router top-k (softmax, top-8, renormalise over 128 experts)
+    alone and feeding the layer (``ExpertBank.forward_from_logits``), as graph
+    replays over the 8 rotating layers.  The fp32 logits are the synthetic
+    router's (N(0,1) plus the per-expert Zipf(1.1) log-bias), so the routing
+    is the headline's distribution."""
+    import torch
+    from exq_b200 import router_topk
+    from exq_b200.synth import zipf_ranks
+    c = CFG
+    logits = []
+    for i in range(len(banks)):
+        g = torch.Generator().manual_seed(500 + i)
+        lg = torch.randn(tokens, c["n_experts"], generator=g)
+        lg = lg - 1.1 * torch.log(zipf_ranks(c["n_experts"], 500 + i).float())
+        logits.append(lg.to(dev))
+
+    xs = [layer_inputs(dev, tokens, 1, seed0=50 + i)[0][0] for i in range(len(banks))]
+    s = torch.cuda.Stream(dev)
+    s.wait_stream(torch.cuda.current_stream(dev))
+    gr, gl, gi = [], [], []
+    with torch.cuda.stream(s):
+        for bank, lg, x in zip(banks, logits, xs):
+            ids, w = router_topk(lg, c["top_k"], True)
+            bank.forward_from_logits(x, lg, c["top_k"])
+            bank(x, ids, w)
+            g1 = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g1, stream=s):
+                router_topk(lg, c["top_k"], True)
+            g2 = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g2, stream=s):
+                bank.forward_from_logits(x, lg, c["top_k"])
+            g3 = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g3, stream=s):
+                bank(x, ids, w)
+            gr.append(g1)
+            gl.append(g2)
+            gi.append(g3)
+    torch.cuda.current_stream(dev).wait_stream(s)
+    t_r = time_graphs(gr, reps, 20, dev) / reps
+    t_l = time_graphs(gl, reps, 20, dev) / reps
+    t_i = time_graphs(gi, reps, 20, dev) / reps
+    return {"tokens": tokens, "experts": c["n_experts"], "top_k": c["top_k"],
+            "logits": "fp32, Zipf(1.1)-biased", "router_us": round(t_r * 1e6, 2),
+            "layer_from_logits_us": round(t_l * 1e6, 2),
+            "layer_from_router_ids_us": round(t_i * 1e6, 2),
+            "gpu_launches_per_layer": 3}
+
+
 def tier_expert_bytes(tier, hidden, inter):
     """Stored bytes of one expert (gate_up + down) in a tier: INT4 nibbles +
     group-128 fp16 scales, INT8 bytes + per-output-row fp16 scales, or BF16."""
@@ -990,7 +1039,9 @@ def main():
         cpu = cpu_baseline()
 
     cfgs = None
+    router = None
     if world == 1 and not args.no_configs:
+        router = router_measure(dev, banks)
         cfgs = configs_measure(dev)
 
     ep = {}
@@ -1031,6 +1082,8 @@ def main():
         "clocks": clk.summary(),
         "sweep": sweep,
     }
+    if router is not None:
+        line["router"] = router
     if cfgs is not None:
         line["configs"] = cfgs
     if ref_gpu is not None:

@@ -76,6 +76,9 @@ SIGNATURES = {
                                         vp, sz, vp]),
     "exq_moe_layer_forward_range": (C.c_int, [vp, vp, C.c_int, i64, vp, C.c_int, vp, C.c_int, i32,
                                               vp, vp, sz, vp, i32, i32]),
+    "exq_moe_layer_from_logits_workspace_bytes": (sz, [i64, i32, i32, i32, i64, i64]),
+    "exq_moe_layer_forward_from_logits": (C.c_int, [vp, vp, C.c_int, i64, vp, C.c_int, i32, i32,
+                                                    vp, vp, sz, vp]),
 }
 
 _lock = threading.Lock()

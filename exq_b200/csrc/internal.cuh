@@ -158,6 +158,13 @@ uint32_t* device_status_ptr();
 // Views into a layer workspace (exq_moe_layer_forward_range) for a caller that
 // replaces the combine stage: the fp32 down partials [n_slots, hidden] by
 // sorted position and the slot -> sorted position map (-1: no expert).
+// Router top-k (router.cu): argument check and launch (an ordinary launch;
+// the kernel lets a programmatic successor launch early).
+int check_router_args(int logits_dtype, int64_t n_tokens, int32_t n_experts, int32_t top_k);
+cudaError_t launch_router_topk(const void* logits, int dtype, int64_t n_tokens, int n_experts,
+                               int top_k, int renormalize, int32_t* ids, float* weights,
+                               cudaStream_t s);
+
 void layer_partials(void* workspace, int64_t n_slots, int64_t n_tokens, int n_buckets,
                     int64_t hidden, int64_t inter, const float** partial,
                     const int32_t** pos_of_slot);

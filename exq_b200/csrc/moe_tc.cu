@@ -1373,12 +1373,15 @@ extern "C" int exq_moe_layer_forward(const exq_moe_weights* weights, const void*
                                      workspace_bytes, stream, 0, EXQ_LAYER_STAGES);
 }
 
-extern "C" int exq_moe_layer_forward_range(const exq_moe_weights* w, const void* hidden_states,
-                                           int act_dtype, int64_t n_tokens, const void* topk_ids,
-                                           int ids_dtype, const void* topk_weights, int w_dtype,
-                                           int32_t top_k, void* out, void* workspace,
-                                           size_t workspace_bytes, void* stream,
-                                           int32_t first_stage, int32_t end_stage) {
+// The layer's stages [first_stage, end_stage).  chained_start: the call's
+// first launch may be programmatic, because the kernel before it on the
+// stream is this library's router (which lets it launch early and completes
+// before the routing kernel reads the ids).
+static int layer_forward(const exq_moe_weights* w, const void* hidden_states, int act_dtype,
+                         int64_t n_tokens, const void* topk_ids, int ids_dtype,
+                         const void* topk_weights, int w_dtype, int32_t top_k, void* out,
+                         void* workspace, size_t workspace_bytes, void* stream,
+                         int32_t first_stage, int32_t end_stage, bool chained_start) {
   EXQ_CHECK_ARG(w, "moe_layer: weights is null");
   EXQ_CHECK_ARG(0 <= first_stage && first_stage <= end_stage && end_stage <= EXQ_LAYER_STAGES,
                 "moe_layer: stage range [%d, %d) outside [0, %d)", first_stage, end_stage,
@@ -1425,8 +1428,9 @@ extern "C" int exq_moe_layer_forward_range(const exq_moe_weights* w, const void*
   if (!status) return EXQ_ERR_CUDA;
   int st = EXQ_OK;
   // Launch programmatically (overlapping the previous kernel's tail) only after
-  // a kernel of this call: the first launch may follow a copy or an event wait.
-  bool chained = false;
+  // a kernel of this call or the router: the first launch may otherwise follow
+  // a copy or an event wait.
+  bool chained = chained_start;
 
   // gate_up and down run as one launch when both are asked for; with the
   // combine too, the down items sum each token's slots (no separate combine)
@@ -1566,4 +1570,61 @@ extern "C" int exq_moe_layer_forward_range(const exq_moe_weights* w, const void*
     return launch_combine_partials(ws.partial, H, ws.pos_of_slot, topk_weights, w_dtype, top_k,
                                    n_tokens, spt, out, act_dtype, s, chained);
   return EXQ_OK;
+}
+
+extern "C" int exq_moe_layer_forward_range(const exq_moe_weights* w, const void* hidden_states,
+                                           int act_dtype, int64_t n_tokens, const void* topk_ids,
+                                           int ids_dtype, const void* topk_weights, int w_dtype,
+                                           int32_t top_k, void* out, void* workspace,
+                                           size_t workspace_bytes, void* stream,
+                                           int32_t first_stage, int32_t end_stage) {
+  return layer_forward(w, hidden_states, act_dtype, n_tokens, topk_ids, ids_dtype, topk_weights,
+                       w_dtype, top_k, out, workspace, workspace_bytes, stream, first_stage,
+                       end_stage, false);
+}
+
+extern "C" size_t exq_moe_layer_from_logits_workspace_bytes(int64_t n_tokens, int32_t top_k,
+                                                            int32_t n_shared,
+                                                            int32_t n_experts_total,
+                                                            int64_t hidden, int64_t inter) {
+  const size_t layer = exq_moe_layer_workspace_bytes(n_tokens, top_k, n_shared, n_experts_total,
+                                                     hidden, inter);
+  if (layer == 0 && n_tokens > 0) return 0;
+  return align_up(layer, 256) + 2 * align_up(static_cast<size_t>(n_tokens) * top_k * 4, 256);
+}
+
+extern "C" int exq_moe_layer_forward_from_logits(const exq_moe_weights* w,
+                                                 const void* hidden_states, int act_dtype,
+                                                 int64_t n_tokens, const void* router_logits,
+                                                 int logits_dtype, int32_t top_k,
+                                                 int32_t renormalize, void* out, void* workspace,
+                                                 size_t workspace_bytes, void* stream) {
+  EXQ_CHECK_ARG(w, "moe_layer: weights is null");
+  const int st = check_router_args(logits_dtype, n_tokens, w->n_routed, top_k);
+  if (st != EXQ_OK) return st;
+  const size_t need = exq_moe_layer_from_logits_workspace_bytes(
+      n_tokens, top_k, w->n_shared, w->n_routed + w->n_shared, w->hidden, w->inter);
+  if (!workspace || workspace_bytes < need) {
+    set_error("moe_layer_from_logits: workspace of %zu bytes needed", need);
+    return EXQ_ERR_WORKSPACE;
+  }
+  if (n_tokens == 0) return EXQ_OK;
+  EXQ_CHECK_ARG(router_logits, "moe_layer_from_logits: router_logits is null");
+  // the router's ids and weights after the layer's own workspace
+  const size_t layer = align_up(exq_moe_layer_workspace_bytes(n_tokens, top_k, w->n_shared,
+                                                               w->n_routed + w->n_shared,
+                                                               w->hidden, w->inter), 256);
+  char* base = static_cast<char*>(workspace);
+  int32_t* ids = reinterpret_cast<int32_t*>(base + layer);
+  float* wts = reinterpret_cast<float*>(base + layer +
+                                        align_up(static_cast<size_t>(n_tokens) * top_k * 4, 256));
+  const cudaError_t e = launch_router_topk(router_logits, logits_dtype, n_tokens, w->n_routed,
+                                           top_k, renormalize, ids, wts,
+                                           static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) {
+    set_error("router_topk_kernel: %s", cudaGetErrorString(e));
+    return EXQ_ERR_CUDA;
+  }
+  return layer_forward(w, hidden_states, act_dtype, n_tokens, ids, EXQ_I32, wts, EXQ_F32, top_k,
+                       out, workspace, layer, stream, 0, EXQ_LAYER_STAGES, true);
 }

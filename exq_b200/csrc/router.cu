@@ -28,6 +28,9 @@ __global__ void __launch_bounds__(32 * kRouterWarps)
                        int top_k, int renormalize, int32_t* __restrict__ ids,
                        float* __restrict__ weights) {
   const int lane = threadIdx.x & 31;
+  // a routing kernel chained after this one may launch now: it waits for
+  // this grid's completion (griddepcontrol.wait) before it reads the ids
+  pdl_trigger();
   const int64_t warps = static_cast<int64_t>(gridDim.x) * kRouterWarps;
   for (int64_t t = blockIdx.x * static_cast<int64_t>(kRouterWarps) + (threadIdx.x >> 5);
        t < n_tokens; t += warps) {
@@ -113,13 +116,26 @@ cudaError_t launch_router(const void* logits, int dtype, int64_t n_tokens, int n
 }
 
 }  // namespace
-}  // namespace exq
 
-using namespace exq;
+cudaError_t launch_router_topk(const void* logits, int dtype, int64_t n_tokens, int n_experts,
+                               int top_k, int renormalize, int32_t* ids, float* weights,
+                               cudaStream_t s) {
+  const int per = (n_experts + 31) / 32;
+  if (per <= 1)
+    return launch_router<1>(logits, dtype, n_tokens, n_experts, top_k, renormalize, ids, weights, s);
+  if (per <= 2)
+    return launch_router<2>(logits, dtype, n_tokens, n_experts, top_k, renormalize, ids, weights, s);
+  if (per <= 4)
+    return launch_router<4>(logits, dtype, n_tokens, n_experts, top_k, renormalize, ids, weights, s);
+  if (per <= 8)
+    return launch_router<8>(logits, dtype, n_tokens, n_experts, top_k, renormalize, ids, weights, s);
+  if (per <= 16)
+    return launch_router<16>(logits, dtype, n_tokens, n_experts, top_k, renormalize, ids, weights,
+                             s);
+  return launch_router<32>(logits, dtype, n_tokens, n_experts, top_k, renormalize, ids, weights, s);
+}
 
-extern "C" int exq_router_topk(const void* logits, int logits_dtype, int64_t n_tokens,
-                               int32_t n_experts, int32_t top_k, int32_t renormalize,
-                               int32_t* topk_ids, float* topk_weights, void* stream) {
+int check_router_args(int logits_dtype, int64_t n_tokens, int32_t n_experts, int32_t top_k) {
   EXQ_CHECK_ARG(logits_dtype == EXQ_F32 || logits_dtype == EXQ_F16 || logits_dtype == EXQ_BF16,
                 "router_topk: logits must be fp32, fp16 or bf16");
   EXQ_CHECK_ARG(n_tokens >= 0, "router_topk: n_tokens < 0");
@@ -127,29 +143,23 @@ extern "C" int exq_router_topk(const void* logits, int logits_dtype, int64_t n_t
                 "router_topk: n_experts=%d outside 1..%d", n_experts, kRouterMaxExperts);
   EXQ_CHECK_ARG(top_k >= 1 && top_k <= kRouterMaxTopK && top_k <= n_experts,
                 "router_topk: top_k=%d outside 1..min(%d, n_experts)", top_k, kRouterMaxTopK);
+  return EXQ_OK;
+}
+
+}  // namespace exq
+
+using namespace exq;
+
+extern "C" int exq_router_topk(const void* logits, int logits_dtype, int64_t n_tokens,
+                               int32_t n_experts, int32_t top_k, int32_t renormalize,
+                               int32_t* topk_ids, float* topk_weights, void* stream) {
+  const int st = check_router_args(logits_dtype, n_tokens, n_experts, top_k);
+  if (st != EXQ_OK) return st;
   if (n_tokens == 0) return EXQ_OK;
   EXQ_CHECK_ARG(logits && topk_ids && topk_weights, "router_topk: null pointer");
-  auto s = static_cast<cudaStream_t>(stream);
-  const int per = (n_experts + 31) / 32;
-  cudaError_t e;
-  if (per <= 1)
-    e = launch_router<1>(logits, logits_dtype, n_tokens, n_experts, top_k, renormalize, topk_ids,
-                         topk_weights, s);
-  else if (per <= 2)
-    e = launch_router<2>(logits, logits_dtype, n_tokens, n_experts, top_k, renormalize, topk_ids,
-                         topk_weights, s);
-  else if (per <= 4)
-    e = launch_router<4>(logits, logits_dtype, n_tokens, n_experts, top_k, renormalize, topk_ids,
-                         topk_weights, s);
-  else if (per <= 8)
-    e = launch_router<8>(logits, logits_dtype, n_tokens, n_experts, top_k, renormalize, topk_ids,
-                         topk_weights, s);
-  else if (per <= 16)
-    e = launch_router<16>(logits, logits_dtype, n_tokens, n_experts, top_k, renormalize, topk_ids,
-                          topk_weights, s);
-  else
-    e = launch_router<32>(logits, logits_dtype, n_tokens, n_experts, top_k, renormalize, topk_ids,
-                          topk_weights, s);
+  const cudaError_t e = launch_router_topk(logits, logits_dtype, n_tokens, n_experts, top_k,
+                                           renormalize, topk_ids, topk_weights,
+                                           static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) {
     set_error("router_topk_kernel: %s", cudaGetErrorString(e));
     return EXQ_ERR_CUDA;

@@ -277,14 +277,33 @@ class ExpertBank:
     def forward_from_logits(self, hidden_states: torch.Tensor, router_logits: torch.Tensor,
                             top_k: int, renormalize: bool = True,
                             out: torch.Tensor | None = None) -> torch.Tensor:
-        """The layer from router logits [T, n_routed]: the fused router top-k
-        (softmax, top_k, optional renormalisation; ``kernels.router_topk``)
-        feeding the routing stage.  Three launches up to 4096 slots."""
-        from .kernels import router_topk
-        if router_logits.dim() != 2 or router_logits.shape[1] != self.n_routed:
+        """The layer from router logits [T, n_routed] (fp32/fp16/bf16): the
+        fused router top-k (softmax, top_k, optional renormalisation, as
+        ``kernels.router_topk``) feeding the routing stage in one C call,
+        ``exq_moe_layer_forward_from_logits``.  Up to 4096 slots that is three
+        launches, the routing kernel chained programmatically after the
+        router."""
+        dev = L.require_cuda(hidden_states, router_logits)
+        if hidden_states.dtype not in (torch.float16, torch.bfloat16):
+            raise ValueError("hidden_states must be fp16 or bf16")
+        x = hidden_states.contiguous()
+        lg = router_logits.contiguous()
+        t = x.shape[0]
+        if x.dim() != 2 or x.shape[1] != self.hidden:
+            raise ValueError("hidden_states must be [T, hidden]")
+        if lg.dim() != 2 or lg.shape != (t, self.n_routed):
             raise ValueError(f"router_logits must be [T, {self.n_routed}]")
-        ids, w = router_topk(router_logits, top_k, renormalize)
-        return self.forward(hidden_states, ids, w, out)
+        need = int(L.lib().exq_moe_layer_from_logits_workspace_bytes(
+            t, top_k, self.n_shared, self.n_total, self.hidden, self.inter))
+        if self._ws is None or self._ws.numel() < need:
+            self._ws = L.workspace(dev, need)
+        if out is None:
+            out = torch.empty(t, self.hidden, dtype=x.dtype, device=dev)
+        L.check(L.lib().exq_moe_layer_forward_from_logits(
+            C.byref(self.cstruct), L.ptr(x), L.tag(x), t, L.ptr(lg), L.tag(lg), int(top_k),
+            int(bool(renormalize)), L.ptr(out), L.ptr(self._ws), self._ws.numel(),
+            L.stream_of(dev)), "moe_layer_forward_from_logits")
+        return out
 
     def forward_range(self, hidden_states, topk_ids, topk_weights, first: int, end: int,
                       out=None, workspace=None):

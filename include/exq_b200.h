@@ -300,6 +300,24 @@ EXQ_API int exq_moe_layer_forward_range(const exq_moe_weights* weights,
                                         void* out, void* workspace, size_t workspace_bytes,
                                         void* stream, int32_t first_stage, int32_t end_stage);
 
+/* The layer from router logits: exq_router_topk (softmax -> top_k -> optional
+ * renormalisation over the n_routed experts; the step SGLang performs before
+ * _exq_forward_cuda, exq/runtime/sglang_backend.py:88-90) feeding
+ * exq_moe_layer_forward, in one call.  logits [n_tokens, n_routed]
+ * fp32/fp16/bf16.  The router's int32 ids and fp32 weights live in the
+ * workspace (exq_moe_layer_from_logits_workspace_bytes), after the layer's
+ * own.  The routing launch is chained programmatically to the router. */
+EXQ_API size_t exq_moe_layer_from_logits_workspace_bytes(int64_t n_tokens, int32_t top_k,
+                                                         int32_t n_shared,
+                                                         int32_t n_experts_total, int64_t hidden,
+                                                         int64_t inter);
+EXQ_API int exq_moe_layer_forward_from_logits(const exq_moe_weights* weights,
+                                              const void* hidden_states, int act_dtype,
+                                              int64_t n_tokens, const void* router_logits,
+                                              int logits_dtype, int32_t top_k,
+                                              int32_t renormalize, void* out, void* workspace,
+                                              size_t workspace_bytes, void* stream);
+
 /* ------------------------------------------------ expert parallelism over peer memory
  *
  * No counterpart in the reference.  The exchange without NCCL or a host sync:
