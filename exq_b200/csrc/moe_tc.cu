@@ -6,7 +6,7 @@
 // exq/runtime/sglang_backend.py:117-156) for experts that mix BF16, INT8 and
 // INT4 weight tiers.
 //
-// One persistent CTA per SM (608 threads, 19 warps):
+// One persistent CTA per SM (672 threads, 21 warps):
 //   warp 0       weight producer: one TMA per 16 KB slot brings 128 weight rows
 //                x 256 k (INT4; INT8 128 k, 16-bit 64 k) into a 6-slot smem
 //                ring, plus one TMA for the INT4 group scales of the slot
