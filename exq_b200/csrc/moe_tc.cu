@@ -28,14 +28,21 @@
 //                256 k, INT8 128 k, 16-bit 64 k) into fp16 (scale applied) in
 //                registers, 64 k at a time, and writes them to its lanes of the
 //                A buffer with tcgen05.st
-// A work item is (expert, 128-row block of the projection, up to 64 tokens
+//   warps 19-20  combine: stage the slot positions and weights of this CTA's
+//                tokens, wait until every CTA's down items are stored, then
+//                (with warps 3-18) sum each token's partial rows
+// A work item is (expert, 128-row block of the projection, up to MT tokens
 // of that expert): every weight byte is dequantised once per item and all the
-// expert's tokens ride in the MMA's N dimension.
+// expert's tokens ride in the MMA's N dimension.  gate_up items come first,
+// then down items; a down item's activation producer waits on its tile's count
+// of stored gate_up row blocks (both projections in one launch).
 //
-// Tensor memory (512 columns): accumulators at [0,64) and [64,128); three A
-// buffers of 128 columns (128 rows x 256 fp16) at [128,512).  Tiles hold at
-// most 64 tokens so that the third A buffer fits: it lets the dequantisers
-// run one weight slot further ahead of the MMA.
+// Tensor memory (512 columns), MT = 64: accumulators at [0,64) and [64,128);
+// three A buffers of 128 columns (128 rows x 256 fp16) at [128,512); the third
+// A buffer lets the dequantisers run one weight slot further ahead of the MMA.
+// MT = 128 (calls with many rows per expert): accumulators at [0,128) and
+// [128,256), two A buffers at [256,512), two dequant groups (warps 15-18 have
+// no slots).
 //
 // K order.  Inside every 8-element octet the k order is permuted to
 // [0,4,1,5,2,6,3,7] identically for weights and activations (a dot product
