@@ -806,6 +806,62 @@ def router_measure(dev, banks, tokens=256, reps=400):
             "gpu_launches_per_layer": 3}
 
 
+def offload_measure(dev, tokens_list=(8, 64), gpu_slots=64, calls=64):
+    """The two-tier expert store (``OffloadedExpertBank``) on one Qwen3 layer:
+    128 INT4 experts in pinned host memory, ``gpu_slots`` HBM entries; 8
+    seeded batches cycled, all routed with the same per-expert Zipf(1.1)
+    popularity (one layer's router); eager calls (the host reads the routing
+    to decide the copies), CUDA events around the whole run, beside the same
+    calls on the resident bank."""
+    import torch
+    from exq_b200 import ExpertBank
+    from exq_b200.offload import OffloadedExpertBank
+    from exq_b200.synth import expert_weights, hidden_states, zipf_ranks
+    c = CFG
+    bias = -1.1 * torch.log(zipf_ranks(c["n_experts"], 900).float())
+
+    def batch(t, i):
+        g = torch.Generator().manual_seed(1000 * t + i)
+        p = torch.softmax(torch.randn(t, c["n_experts"], generator=g) + bias, -1)
+        w, ids = torch.topk(p, c["top_k"], -1)
+        w = w / w.sum(-1, keepdim=True)
+        ids = ids.to(torch.int32)
+        x = hidden_states(t, c["hidden"], seed=i).to(dev)
+        return x, ids.to(dev), w.to(dev), ids
+    w13, w2 = expert_weights(c["n_experts"], c["inter"], c["hidden"], seed=900, device=dev)
+    ref = ExpertBank.from_dense(w13, w2, None, act_dtype=torch.float16)
+    src = ExpertBank.from_dense(w13, w2, None, act_dtype=torch.float16)
+    del w13, w2
+    off = OffloadedExpertBank(src, gpu_slots=gpu_slots)
+    out = {"gpu_slots": gpu_slots, "cpu_experts": len(off.host), "per_T": {}}
+    for t in tokens_list:
+        inp = [batch(t, i) for i in range(8)]
+        res = {}
+        for name, bank in (("resident", ref), ("offloaded", off)):
+            for i in range(8):
+                x, ids, w, ids_h = inp[i]
+                bank(x, ids, w) if name == "resident" else bank(x, ids, w, ids_host=ids_h)
+            torch.cuda.synchronize(dev)
+            b0, h0, m0 = off.bytes_copied, off.pool.hits, off.pool.misses
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for i in range(calls):
+                x, ids, w, ids_h = inp[i % 8]
+                bank(x, ids, w) if name == "resident" else bank(x, ids, w, ids_host=ids_h)
+            e1.record()
+            torch.cuda.synchronize(dev)
+            sec = e0.elapsed_time(e1) / 1e3
+            res[name + "_us"] = round(sec / calls * 1e6, 1)
+            if name == "offloaded":
+                n = off.pool.hits - h0 + off.pool.misses - m0
+                res["hit_rate"] = round((off.pool.hits - h0) / max(n, 1), 3)
+                res["h2d_GBps"] = round((off.bytes_copied - b0) / sec / 1e9, 1)
+        out["per_T"][str(t)] = res
+    del ref, src, off
+    torch.cuda.empty_cache()
+    return out
+
+
 def tier_expert_bytes(tier, hidden, inter):
     """Stored bytes of one expert (gate_up + down) in a tier: INT4 nibbles +
     group-128 fp16 scales, INT8 bytes + per-output-row fp16 scales, or BF16."""
@@ -1043,6 +1099,7 @@ def main():
     if world == 1 and not args.no_configs:
         router = router_measure(dev, banks)
         cfgs = configs_measure(dev)
+        cfgs["offload_qwen3"] = offload_measure(dev)
 
     ep = {}
     if not args.no_ep:

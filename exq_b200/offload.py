@@ -36,7 +36,8 @@ class SlotPool:
     """Least-recently-used assignment of experts to ``n_slots`` pool entries.
 
     ``assign(needed)`` returns ``(placement, loads)``: the entry of every
-    needed expert, and the (expert, entry) pairs that must be copied in.
+    needed expert, and the (expert, entry) pairs that must be copied in; the
+    experts it evicted are in ``evicted``.
     Experts needed by the same call are never evicted for one another; more
     needed experts than entries raise ``ValueError``."""
 
@@ -56,6 +57,7 @@ class SlotPool:
                              f"{self.n_slots}")
         keep = set(needed)
         placement, loads = {}, []
+        self.evicted = []
         for e in needed:
             if e in self.where:
                 self.where.move_to_end(e)
@@ -70,6 +72,7 @@ class SlotPool:
             else:
                 victim = next(v for v in self.where if v not in keep)
                 slot = self.where.pop(victim)
+                self.evicted.append(victim)
             self.where[e] = slot
             placement[e] = slot
             loads.append((e, slot))
@@ -130,6 +133,8 @@ class OffloadedExpertBank:
         del w13, s13, w2, s2
         self.copy_stream = copy_stream or torch.cuda.Stream(dev)
         self.bytes_copied = 0
+        self._dirty = False      # expert_slot on the device differs from _slot_host
+        self._pending = False    # copies queued since the compute stream last waited
 
     def _build_cstruct(self):
         b = self.bank
@@ -165,17 +170,20 @@ class OffloadedExpertBank:
                     for dst, src in zip(self.gpu, self.host[e]):
                         dst[slot].copy_(src, non_blocking=True)
                         queued += src.numel() * src.element_size()
-        for e, slot in placement.items():
+        for e in self.pool.evicted:
+            self._slot_host[e] = -1
+        for e, slot in loads:
             self._slot_host[e] = (TIER_NAMES["INT4"] << 24) | slot
-        for e in list(self.host):
-            if not self.pool.resident(e):
-                self._slot_host[e] = -1
+        self._dirty = self._dirty or bool(loads)
         self.bytes_copied += queued
+        self._pending = self._pending or bool(loads)
         return queued
 
     def sync_prefetches(self) -> None:
         """Order the compute stream after every copy queued so far."""
-        torch.cuda.current_stream(self.device).wait_stream(self.copy_stream)
+        if self._pending:
+            torch.cuda.current_stream(self.device).wait_stream(self.copy_stream)
+            self._pending = False
 
     @property
     def stats(self) -> dict:
@@ -193,8 +201,10 @@ class OffloadedExpertBank:
         one synchronisation)."""
         ids_h = ids_host if ids_host is not None else topk_ids.to("cpu")
         self.prefetch(torch.unique(ids_h.reshape(-1)).tolist())
-        slot = torch.tensor(self._slot_host, dtype=torch.int32).pin_memory()
-        self.bank.expert_slot.copy_(slot, non_blocking=True)
+        if self._dirty:   # ordered on the compute stream after the kernels that read it
+            slot = torch.tensor(self._slot_host, dtype=torch.int32).pin_memory()
+            self.bank.expert_slot.copy_(slot, non_blocking=True)
+            self._dirty = False
         self.sync_prefetches()
         return self.bank.forward(hidden_states, topk_ids, topk_weights, out)
 

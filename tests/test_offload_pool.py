@@ -12,6 +12,7 @@ def test_pool_places_reuses_and_evicts_least_recently_used():
     place, loads = p.assign([9, 2])               # 9 hits, 2 loads into the free entry
     assert loads == [(2, place[2])] and len(set(place.values())) == 2
     place, loads = p.assign([7])                  # full: evicts 4, the least recently used
+    assert p.evicted == [4]
     assert not p.resident(4) and p.resident(9) and p.resident(2) and p.resident(7)
     assert p.hits == 1 and p.misses == 4
     assert sorted(p.where.values()) == [0, 1, 2]
