@@ -209,6 +209,37 @@ class ExpertBank:
         cs.expert_slot = self.expert_slot.data_ptr()
         self.cstruct = cs
 
+    # ------------------------------------------------------------ on-disk cache
+    _CACHE_VERSION = 1
+
+    def save(self, path) -> None:
+        """Write the packed tiers (the HBM storage format, byte for byte) and
+        the expert map to ``path`` (``torch.save``), so a later process loads
+        them without re-packing (the reference re-packs every layer on its
+        first call, exq/runtime/sglang_backend.py:32-60)."""
+        storage = {name: tuple(None if t is None else t.detach().to("cpu") for t in st)
+                   for name, st in self.storage.items() if st is not None}
+        torch.save({"version": self._CACHE_VERSION, "hidden": self.hidden, "inter": self.inter,
+                    "act_dtype": str(self.act_dtype).replace("torch.", ""),
+                    "n_routed": self.n_routed, "n_shared": self.n_shared,
+                    "tiers": list(self.tiers), "index": {k: list(v) for k, v in self.index.items()},
+                    "storage": storage}, path)
+
+    @classmethod
+    def load(cls, path, device="cuda") -> "ExpertBank":
+        """A bank written by ``save``, on ``device``."""
+        d = torch.load(path, map_location="cpu", weights_only=True)
+        if d.get("version") != cls._CACHE_VERSION:
+            raise ValueError(f"{path}: not an expert-bank cache of version {cls._CACHE_VERSION}")
+        bank = cls(hidden=d["hidden"], inter=d["inter"], act_dtype=getattr(torch, d["act_dtype"]),
+                   n_routed=d["n_routed"], n_shared=d["n_shared"], tiers=list(d["tiers"]))
+        dev = torch.device(device)
+        bank.storage = {name: tuple(None if t is None else t.to(dev) for t in st)
+                        for name, st in d["storage"].items()}
+        bank.index = {k: list(v) for k, v in d["index"].items()}
+        bank._finalize(dev)
+        return bank
+
     # ------------------------------------------------------------ inspection
     def expert_reference_format(self, e: int):
         """Expert ``e`` in the reference's layouts: INT4 -> (packed, scales [N, K/128])

@@ -75,3 +75,16 @@ def test_offloaded_bank_graph_of_resident_calls_and_errors(cuda):
     bad = torch.tensor([int4[:3]], dtype=torch.int32)
     with pytest.raises(ValueError):
         small(x[:1], bad.to(cuda), torch.full((1, 3), 1 / 3, device=cuda))
+
+
+def test_bank_cache_round_trip_on_gpu(cuda, tmp_path):
+    """A mixed-tier bank with a shared expert, saved and loaded: the same
+    outputs bit for bit."""
+    from exq_b200 import ExpertBank
+    from exq_b200.synth import hidden_states, zipf_router
+    ref, _, tiers, c = _banks(cuda, shared=True)
+    ref.save(tmp_path / "bank.pt")
+    got = ExpertBank.load(tmp_path / "bank.pt", device=cuda)
+    ids, w = zipf_router(24, 16, 8, seed=6)
+    x = hidden_states(24, c.hidden, seed=6).to(cuda)
+    assert torch.equal(got(x, ids.to(cuda), w.to(cuda)), ref(x, ids.to(cuda), w.to(cuda)))
