@@ -60,6 +60,8 @@ SIGNATURES = {
     "exq_ep_dispatch": (C.c_int, [vp, C.c_int, i64, i32, i32, i32, i32, vp, C.c_int, i64, i64, vp,
                                   vp, vp]),
     "exq_ep_expert_forward": (C.c_int, [vp, C.c_int, i32, i32, i64, vp, vp, vp, sz, vp]),
+    "exq_ep_expert_forward_shared": (C.c_int, [vp, C.c_int, i32, i32, i64, vp, vp, vp, i64, i32,
+                                               vp, vp, sz, vp]),
     "exq_ep_combine_peer": (C.c_int, [vp, i32, i64, i64, C.c_int, vp, vp, C.c_int, i64, i32, vp,
                                       vp, vp]),
     "exq_combine_noalloc": (C.c_int, [vp, C.c_int, i64, i64, vp, vp, C.c_int, i64, i32, vp,

@@ -67,14 +67,19 @@ struct EpLayout {
   int64_t ids, ones, recv, back, bytes;
 };
 
+// Receive side: n_ranks + 1 blocks of cap rows (ids, weights 1.0, rows):
+// block s holds what source rank s sent, block n_ranks this rank's own tokens
+// for its shared experts (exq_ep_expert_forward_shared).  Return side:
+// n_ranks blocks, block d written by expert rank d.
 __host__ __device__ inline EpLayout ep_layout(int n_ranks, int64_t cap, int64_t row_bytes) {
+  const int64_t rows_in = static_cast<int64_t>(n_ranks + 1) * cap;
   const int64_t rows = static_cast<int64_t>(n_ranks) * cap;
   auto up = [](int64_t x) { return (x + 255) / 256 * 256; };
   EpLayout l;
   l.ids = kEpHeaderBytes;
-  l.ones = l.ids + up(4 * rows);
-  l.recv = l.ones + up(4 * rows);
-  l.back = l.recv + up(rows * row_bytes);
+  l.ones = l.ids + up(4 * rows_in);
+  l.recv = l.ones + up(4 * rows_in);
+  l.back = l.recv + up(rows_in * row_bytes);
   l.bytes = l.back + up(rows * row_bytes);
   return l;
 }
@@ -364,6 +369,48 @@ __global__ void __launch_bounds__(kEpThreads) ep_return_kernel(
   }
 }
 
+// This rank's own block (block n_ranks of the receive area): token t's row
+// for its shared expert s at entry n_shared * t + s, id n_local + s; the
+// block's other entries get id -1 (no expert).
+template <typename T>
+__global__ void __launch_bounds__(kEpThreads) ep_own_block_kernel(
+    const T* __restrict__ x, int64_t n_tokens, int n_shared, int n_local, int64_t H, int cap,
+    T* __restrict__ rows, int32_t* __restrict__ ids) {
+  const int64_t used = n_tokens * n_shared;
+  const int64_t oct = H / 8;
+  for (int64_t r = blockIdx.x; r < cap; r += gridDim.x) {
+    if (r >= used) {
+      if (threadIdx.x == 0) ids[r] = -1;
+      continue;
+    }
+    const int64_t t = r / n_shared;
+    const int s = static_cast<int>(r - t * n_shared);
+    if (threadIdx.x == 0) ids[r] = n_local + s;
+    const uint4* src = reinterpret_cast<const uint4*>(x + t * H);
+    uint4* dst = reinterpret_cast<uint4*>(rows + r * H);
+    for (int64_t c = threadIdx.x; c < oct; c += kEpThreads) dst[c] = src[c];
+  }
+}
+
+// Shared-expert output of this rank's tokens from the own block's fp32
+// partials: out[t] = (0 + p(t, 0)) + p(t, 1) + ... in expert order, rounded
+// once: what the layer's combine gives for the shared experts with weight 1.
+template <typename T>
+__global__ void __launch_bounds__(kEpThreads) ep_shared_sum_kernel(
+    const float* __restrict__ partial, const int32_t* __restrict__ pos_of_slot, int64_t base,
+    int64_t n_tokens, int n_shared, int64_t H, T* __restrict__ out) {
+  for (int64_t t = blockIdx.x; t < n_tokens; t += gridDim.x) {
+    for (int64_t h = threadIdx.x; h < H; h += kEpThreads) {
+      float acc = 0.f;
+      for (int s = 0; s < n_shared; ++s) {
+        const int pos = pos_of_slot[base + t * n_shared + s];
+        if (pos >= 0) acc = __fadd_rn(acc, __ldg(partial + static_cast<int64_t>(pos) * H + h));
+      }
+      out[t * H + h] = from_f32<T>(acc);
+    }
+  }
+}
+
 __global__ void ep_fill_kernel(float* p, int64_t n, float v) {
   for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x)
@@ -496,7 +543,7 @@ extern "C" int exq_ep_buffer_init(void* buffer, int32_t n_ranks, int64_t capacit
   EXQ_CHECK_ARG(buffer, "ep_buffer_init: buffer is null");
   auto s = static_cast<cudaStream_t>(stream);
   const EpLayout l = ep_layout(n_ranks, capacity, 2 * hidden_size);
-  const int64_t rows = static_cast<int64_t>(n_ranks) * capacity;
+  const int64_t rows = static_cast<int64_t>(n_ranks + 1) * capacity;  // with the own block
   uint8_t* b = static_cast<uint8_t*>(buffer);
   if (cudaMemsetAsync(b, 0, kEpHeaderBytes, s) != cudaSuccess ||
       cudaMemsetAsync(b + l.ids, 0xFF, 4 * rows, s) != cudaSuccess) {
@@ -643,6 +690,80 @@ extern "C" int exq_ep_expert_forward(const exq_moe_weights* weights, int dtype, 
         partial, pos, H, static_cast<int>(rows), static_cast<int>(capacity), n_ranks, rank,
         reinterpret_cast<uint8_t* const*>(peers), l.back);
   EXQ_CHECK_LAUNCH("ep_return_kernel");
+  return EXQ_OK;
+}
+
+extern "C" int exq_ep_expert_forward_shared(const exq_moe_weights* weights, int dtype,
+                                            int32_t n_ranks, int32_t rank, int64_t capacity,
+                                            void* buffer, void* const* peers, const void* hidden,
+                                            int64_t n_tokens, int32_t n_shared, void* shared_out,
+                                            void* workspace, size_t workspace_bytes,
+                                            void* stream) {
+  EXQ_CHECK_ARG(weights && buffer && peers, "ep_expert_forward_shared: null pointer");
+  EXQ_CHECK_ARG(is_act(dtype), "ep_expert_forward_shared: dtype must be fp16 or bf16");
+  EXQ_CHECK_ARG(weights->n_shared == 0 && n_shared >= 1 && n_shared < weights->n_routed,
+                "ep_expert_forward_shared: the bank holds the local experts, then the %d shared "
+                "ones, all as routed experts", n_shared);
+  const int64_t H = weights->hidden;
+  EXQ_CHECK_ARG(ep_sizes_ok(n_ranks, capacity, H) && 0 <= rank && rank < n_ranks,
+                "ep_expert_forward_shared: bad sizes (rank %d of %d, capacity %lld)", rank,
+                n_ranks, (long long)capacity);
+  EXQ_CHECK_ARG(n_tokens >= 0 && n_tokens * n_shared <= capacity,
+                "ep_expert_forward_shared: %lld tokens x %d shared experts exceed the %lld rows "
+                "of the own block", (long long)n_tokens, n_shared, (long long)capacity);
+  EXQ_CHECK_ARG(n_tokens == 0 || (hidden && shared_out), "ep_expert_forward_shared: null pointer");
+  uint32_t* st = device_status_ptr();
+  if (!st) return EXQ_ERR_CUDA;
+  auto s = static_cast<cudaStream_t>(stream);
+  uint8_t* b = static_cast<uint8_t*>(buffer);
+  const EpLayout l = ep_layout(n_ranks, capacity, 2 * H);
+  const int64_t peer_rows = static_cast<int64_t>(n_ranks) * capacity;
+  const int64_t rows = peer_rows + capacity;  // the peers' blocks and the own block
+  const int n_local = weights->n_routed - n_shared;
+  {
+    const int grid = static_cast<int>(capacity < 2 * num_sms() ? capacity : 2 * num_sms());
+    int32_t* ids = reinterpret_cast<int32_t*>(b + l.ids) + peer_rows;
+    if (dtype == EXQ_F16)
+      ep_own_block_kernel<__half><<<grid, kEpThreads, 0, s>>>(
+          static_cast<const __half*>(hidden), n_tokens, n_shared, n_local, H,
+          static_cast<int>(capacity), reinterpret_cast<__half*>(b + l.recv) + peer_rows * H, ids);
+    else
+      ep_own_block_kernel<__nv_bfloat16><<<grid, kEpThreads, 0, s>>>(
+          static_cast<const __nv_bfloat16*>(hidden), n_tokens, n_shared, n_local, H,
+          static_cast<int>(capacity), reinterpret_cast<__nv_bfloat16*>(b + l.recv) + peer_rows * H,
+          ids);
+    EXQ_CHECK_LAUNCH("ep_own_block_kernel");
+  }
+  ep_wait_arrivals_kernel<<<1, kEpMaxRanks, 0, s>>>(reinterpret_cast<uint32_t*>(b), n_ranks, st,
+                                                     g_ep_wait_ns);
+  EXQ_CHECK_LAUNCH("ep_wait_arrivals_kernel");
+  // one layer call: the received rows for the local experts and this rank's
+  // own tokens for the shared experts
+  int r = exq_moe_layer_forward_range(weights, b + l.recv, dtype, rows, b + l.ids, EXQ_I32,
+                                      b + l.ones, EXQ_F32, 1, b + l.back, workspace,
+                                      workspace_bytes, stream, 0, 4);
+  if (r != EXQ_OK) return r;
+  const float* partial = nullptr;
+  const int32_t* pos = nullptr;
+  layer_partials(workspace, rows, rows, weights->n_routed, H, weights->inter, &partial, &pos);
+  const int grid = static_cast<int>(peer_rows < 2 * num_sms() ? peer_rows : 2 * num_sms());
+  const int sgrid = static_cast<int>(n_tokens < 2 * num_sms() ? (n_tokens > 0 ? n_tokens : 1)
+                                                                 : 2 * num_sms());
+  if (dtype == EXQ_F16) {
+    ep_return_kernel<__half><<<grid, kEpThreads, 0, s>>>(
+        partial, pos, H, static_cast<int>(peer_rows), static_cast<int>(capacity), n_ranks, rank,
+        reinterpret_cast<uint8_t* const*>(peers), l.back);
+    ep_shared_sum_kernel<__half><<<sgrid, kEpThreads, 0, s>>>(
+        partial, pos, peer_rows, n_tokens, n_shared, H, static_cast<__half*>(shared_out));
+  } else {
+    ep_return_kernel<__nv_bfloat16><<<grid, kEpThreads, 0, s>>>(
+        partial, pos, H, static_cast<int>(peer_rows), static_cast<int>(capacity), n_ranks, rank,
+        reinterpret_cast<uint8_t* const*>(peers), l.back);
+    ep_shared_sum_kernel<__nv_bfloat16><<<sgrid, kEpThreads, 0, s>>>(
+        partial, pos, peer_rows, n_tokens, n_shared, H,
+        static_cast<__nv_bfloat16*>(shared_out));
+  }
+  EXQ_CHECK_LAUNCH("ep_return_kernel / ep_shared_sum_kernel");
   return EXQ_OK;
 }
 

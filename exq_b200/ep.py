@@ -12,12 +12,16 @@ no host synchronisation (so it can be captured in a CUDA graph):
 1. ``exq_ep_dispatch`` groups this rank's (token, expert) slots by destination
    and stores each hidden row and local expert id straight into the
    destination's receive block over NVLink, then raises an arrival flag there;
-2. the shared experts (replicated) run on the rank's own tokens meanwhile;
-3. ``exq_ep_expert_forward`` waits for every arrival flag, runs the local
-   experts on the fixed-size receive area (unused rows have id -1 and cost no
-   GEMM work) and stores each output row back into its source's return block,
-   raising a return flag there;
-4. ``exq_ep_combine_peer`` waits for every return flag, applies the router
+2. ``exq_ep_expert_forward_shared`` puts the rank's own tokens into its own
+   receive block (one row per token and shared expert), waits for every
+   arrival flag, runs one layer launch over the received rows (local experts)
+   and the own block (the shared experts, replicated on every rank), stores
+   each received row's output back into its source's return block, raising a
+   return flag there, and sums the shared experts' rows per token.  Without
+   shared experts (or with ``fold_shared=False``) the shared experts run as a
+   call of their own after the dispatch and ``exq_ep_expert_forward`` serves
+   the received rows only;
+3. ``exq_ep_combine_peer`` waits for every return flag, applies the router
    weights and sums each token's slots plus the shared output.
 Each destination reserves ``max_tokens * top_k`` rows per source, so no
 count exchange is needed; a call with more tokens is refused on the host.
@@ -182,7 +186,8 @@ class ExpertParallelLayer:
 
     def __init__(self, local_bank, n_routed: int, group=None, shared_bank=None,
                  local_fn=None, combine_fn=None, shared_fn=None, pack_fn=None,
-                 max_tokens: int | None = None, top_k: int | None = None):
+                 max_tokens: int | None = None, top_k: int | None = None,
+                 fold_shared: bool = True):
         self.group = group
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
@@ -201,6 +206,7 @@ class ExpertParallelLayer:
         self.pack_fn = pack_fn or _cuda_pack
         self.peer = None
         self._ws = None
+        self.fold = None
         if max_tokens is not None:
             if top_k is None or top_k <= 0 or max_tokens <= 0 or local_bank is None:
                 raise ValueError("the peer exchange needs max_tokens > 0, top_k > 0 and a bank")
@@ -209,10 +215,19 @@ class ExpertParallelLayer:
                                  "pass the shared experts as shared_bank")
             self.peer = PeerExchange(group, max_tokens * top_k, local_bank.hidden,
                                      local_bank.device)
+            # shared experts folded into the expert launch: one bank with the
+            # local experts, then the shared ones, over the received rows and
+            # this rank's own block (one row per token and shared expert)
+            self.fold = None
+            if (fold_shared and shared_bank is not None and shared_fn is None
+                    and shared_bank.n_shared == 0 and shared_bank.n_routed <= top_k):
+                from .experts import ExpertBank
+                self.fold = ExpertBank.merged(local_bank, shared_bank)
+            bank = self.fold or local_bank
+            rows = (self.world + (1 if self.fold is not None else 0)) * self.peer.capacity
             # the layer's own workspace, sized once: a captured step keeps
             # pointing at it whatever else the bank is called on
-            self._ws = L.workspace(local_bank.device,
-                                   local_bank.workspace_bytes(self.world * self.peer.capacity, 1))
+            self._ws = L.workspace(local_bank.device, bank.workspace_bytes(rows, 1))
 
     def close(self) -> None:
         """Release the peer buffers (collective)."""
@@ -359,12 +374,20 @@ class ExpertParallelLayer:
                                     self.rank, L.ptr(x), L.tag(x), h, px.capacity,
                                     L.ptr(px.peers), L.ptr(slot_row), s), "ep_dispatch")
         mark(1)
-        shared = self.shared_fn(x)
-        mark(2)
         ws = self._ws
-        L.check(lib.exq_ep_expert_forward(C.byref(bank.cstruct), L.tag(x), self.world, self.rank,
-                                          px.capacity, px.ptr, L.ptr(px.peers), L.ptr(ws),
-                                          ws.numel(), s), "ep_expert_forward")
+        if self.fold is not None:
+            shared = torch.empty(t, h, dtype=x.dtype, device=dev)
+            mark(2)
+            L.check(lib.exq_ep_expert_forward_shared(
+                C.byref(self.fold.cstruct), L.tag(x), self.world, self.rank, px.capacity, px.ptr,
+                L.ptr(px.peers), L.ptr(x), t, self.shared_bank.n_routed, L.ptr(shared),
+                L.ptr(ws), ws.numel(), s), "ep_expert_forward_shared")
+        else:
+            shared = self.shared_fn(x)
+            mark(2)
+            L.check(lib.exq_ep_expert_forward(C.byref(bank.cstruct), L.tag(x), self.world,
+                                              self.rank, px.capacity, px.ptr, L.ptr(px.peers),
+                                              L.ptr(ws), ws.numel(), s), "ep_expert_forward")
         mark(3)
         y = torch.empty(t, h, dtype=x.dtype, device=dev)
         L.check(lib.exq_ep_combine_peer(px.ptr, self.world, px.capacity, h, L.tag(x),

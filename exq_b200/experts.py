@@ -209,6 +209,35 @@ class ExpertBank:
         cs.expert_slot = self.expert_slot.data_ptr()
         self.cstruct = cs
 
+    @classmethod
+    def merged(cls, first: "ExpertBank", second: "ExpertBank") -> "ExpertBank":
+        """One bank whose routed experts are ``first``'s, then ``second``'s
+        (ids offset by ``first.n_routed``); neither may hold shared experts.
+        A tier only one of them holds is shared, not copied; a tier both hold
+        is concatenated."""
+        if first.n_shared or second.n_shared:
+            raise ValueError("merged banks hold routed experts only")
+        if (first.hidden, first.inter, first.act_dtype) != (second.hidden, second.inter,
+                                                            second.act_dtype):
+            raise ValueError("merged banks need the same hidden, inter and activation dtype")
+        bank = cls(hidden=first.hidden, inter=first.inter, act_dtype=first.act_dtype,
+                   n_routed=first.n_routed + second.n_routed, n_shared=0,
+                   tiers=list(first.tiers) + list(second.tiers))
+        for name in TIER_NAMES:
+            a, b = first.storage.get(name), second.storage.get(name)
+            ia = list(first.index.get(name, []))
+            ib = [e + first.n_routed for e in second.index.get(name, [])]
+            if a is None and b is None:
+                continue
+            if a is None or b is None:
+                bank.storage[name] = a if b is None else b
+            else:
+                bank.storage[name] = tuple(None if x is None else torch.cat([x, y], 0)
+                                           for x, y in zip(a, b))
+            bank.index[name] = ia + ib
+        bank._finalize(first.device)
+        return bank
+
     # ------------------------------------------------------------ on-disk cache
     _CACHE_VERSION = 1
 

@@ -390,6 +390,23 @@ EXQ_API int exq_ep_expert_forward(const exq_moe_weights* weights, int dtype, int
                                   void* const* peers, void* workspace, size_t workspace_bytes,
                                   void* stream);
 
+/* exq_ep_expert_forward with the shared experts folded in.  `weights` holds
+ * this rank's routed experts followed by the n_shared shared experts, all as
+ * routed experts (n_shared field 0).  This rank's n_tokens rows of `hidden`
+ * go into its own block of the receive area (block n_ranks), one row per
+ * (token, shared expert), and the layer runs once on the received rows and
+ * that block; the received rows' outputs return to their sources as in
+ * exq_ep_expert_forward, and shared_out [n_tokens, hidden] (`dtype`) receives
+ * the shared experts' summed output, rounded once (the `base` of
+ * exq_ep_combine_peer).  n_tokens * n_shared <= capacity.  workspace:
+ * exq_moe_layer_workspace_bytes((n_ranks + 1) * capacity, 1, 0, n_routed,
+ * hidden, inter). */
+EXQ_API int exq_ep_expert_forward_shared(const exq_moe_weights* weights, int dtype,
+                                         int32_t n_ranks, int32_t rank, int64_t capacity,
+                                         void* buffer, void* const* peers, const void* hidden,
+                                         int64_t n_tokens, int32_t n_shared, void* shared_out,
+                                         void* workspace, size_t workspace_bytes, void* stream);
+
 /* Waits for every rank's return flag, then
  * out[t] = base[t] + sum_j weights[t, j] * returned[slot_row[t*k + j]]
  * as exq_ep_combine (base may be NULL). */

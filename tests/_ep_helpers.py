@@ -112,12 +112,14 @@ def _gpu_step_inputs(step, rank, world, t, case, e, h, k, dev):
     return x, ids.to(dev), w.to(dev)
 
 
-def gpu_worker(rank, world, port, mode="nccl", max_tokens=64):
+def gpu_worker(rank, world, port, mode="nccl", max_tokens=64, shared=False):
     """EP on `world` GPUs vs the whole layer on one GPU (Mixtral-like, bf16),
     over four steps: spread routing, a rank with no tokens, every slot to rank
     0's experts, spread again.  mode "peer": the peer-memory exchange (receive
     area of world * max_tokens * top_k rows), also checked bit for bit against
-    the NCCL exchange when world > 1."""
+    the NCCL exchange when world > 1.  shared: two always-on BF16 shared
+    experts; the peer exchange then folds them into its expert launch, checked
+    bit for bit against the same exchange with them run apart."""
     from exq_b200 import ExpertBank
     from exq_b200 import _lib as L
     from exq_b200.ep import ExpertParallelLayer, build_rank_banks
@@ -128,13 +130,23 @@ def gpu_worker(rank, world, port, mode="nccl", max_tokens=64):
     try:
         e, h, inter, k = 8, 512, 256, 2
         w13, w2 = expert_weights(e, inter, h, seed=0, device=dev)
-        local, _ = build_rank_banks(w13, w2, world, rank, act_dtype=torch.bfloat16)
-        full = ExpertBank.from_dense(w13, w2, None, act_dtype=torch.bfloat16)
+        sw13 = sw2 = None
+        if shared:
+            sw13, sw2 = expert_weights(2, inter, h, seed=5, device=dev)
+        local, sh = build_rank_banks(w13, w2, world, rank, act_dtype=torch.bfloat16,
+                                     shared_w13=sw13, shared_w2=sw2)
+        full = ExpertBank.from_dense(w13, w2, None, act_dtype=torch.bfloat16, shared_w13=sw13,
+                                     shared_w2=sw2)
+        apart = None
         if mode == "peer":
-            layer = ExpertParallelLayer(local, e, max_tokens=max_tokens, top_k=k)
-            nccl = ExpertParallelLayer(local, e) if world > 1 else None
+            layer = ExpertParallelLayer(local, e, shared_bank=sh, max_tokens=max_tokens, top_k=k)
+            assert (layer.fold is not None) == shared
+            if shared:
+                apart = ExpertParallelLayer(local, e, shared_bank=sh, max_tokens=max_tokens,
+                                            top_k=k, fold_shared=False)
+            nccl = ExpertParallelLayer(local, e, shared_bank=sh) if world > 1 else None
         else:
-            layer, nccl = ExpertParallelLayer(local, e), None
+            layer, nccl = ExpertParallelLayer(local, e, shared_bank=sh), None
         L.read_device_status(dev, clear=True)
         steps = [(48, "spread"), (0 if rank == 0 else 17, "spread"), (64, "one_rank"),
                  (48, "spread")]
@@ -145,6 +157,9 @@ def gpu_worker(rank, world, port, mode="nccl", max_tokens=64):
             if nccl is not None:
                 y2 = nccl(x, ids, w)
                 assert torch.equal(y, y2), f"rank {rank} step {step}: peer != NCCL exchange"
+            if apart is not None:
+                y3 = apart(x, ids, w)
+                assert torch.equal(y, y3), f"rank {rank} step {step}: folded != apart"
             if t:
                 ref = full(x, ids, w)
                 torch.cuda.synchronize(dev)
@@ -155,6 +170,8 @@ def gpu_worker(rank, world, port, mode="nccl", max_tokens=64):
         assert status == 0, f"rank {rank}: device status {status:#x}"
         if mode == "peer":
             layer.close()
+            if apart is not None:
+                apart.close()
         dist.barrier()
     except BaseException:
         # print before the process group teardown, which may abort the process

@@ -54,6 +54,23 @@ def test_ep_peer_one_gpu_matches_single_gpu(max_tokens):
 
 
 @pytest.mark.gpu
+@pytest.mark.parametrize("max_tokens", [64, 2100])
+def test_ep_peer_one_gpu_with_shared_experts_folded(max_tokens):
+    """Two BF16 shared experts folded into the expert launch (own receive
+    block): bit for bit the exchange with the shared experts run apart, and
+    the whole layer on one GPU within tolerance (one-rank group)."""
+    mp.spawn(EH.gpu_worker, args=(1, _free_port(), "peer", max_tokens, True), nprocs=1,
+             join=True)
+
+
+@pytest.mark.gpu
+def test_ep_peer_two_gpus_with_shared_experts_folded():
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    mp.spawn(EH.gpu_worker, args=(2, _free_port(), "peer", 64, True), nprocs=2, join=True)
+
+
+@pytest.mark.gpu
 def test_ep_peer_step_replays_from_a_cuda_graph():
     """A peer-memory step captured once in a CUDA graph and replayed with new
     inputs equals the eager call (one-rank group, one GPU)."""

@@ -88,7 +88,9 @@ def test_ep_entry_points_validate_on_host(lib_path):
     up = lambda v: (v + 255) // 256 * 256  # noqa: E731
     p, cap, h = 2, 512, 4096
     rows = p * cap
-    assert lib.exq_ep_buffer_bytes(p, cap, h) == 1024 + 2 * up(4 * rows) + 2 * up(rows * 2 * h)
+    rows_in = rows + cap   # the receive side also holds this rank's own block
+    assert lib.exq_ep_buffer_bytes(p, cap, h) == (1024 + 2 * up(4 * rows_in) + up(rows_in * 2 * h)
+                                                  + up(rows * 2 * h))
     for bad in [(0, cap, h), (65, cap, h), (p, 0, h), (p, cap, 7), (64, 1 << 25, h)]:
         assert lib.exq_ep_buffer_bytes(*bad) == 0
     assert lib.exq_ep_buffer_init(None, p, cap, h, None) == -1
