@@ -712,6 +712,8 @@ extern "C" int exq_ep_expert_forward_shared(const exq_moe_weights* weights, int 
                 "ep_expert_forward_shared: %lld tokens x %d shared experts exceed the %lld rows "
                 "of the own block", (long long)n_tokens, n_shared, (long long)capacity);
   EXQ_CHECK_ARG(n_tokens == 0 || (hidden && shared_out), "ep_expert_forward_shared: null pointer");
+  EXQ_CHECK_ARG(reinterpret_cast<uintptr_t>(hidden) % 16 == 0,
+                "ep_expert_forward_shared: hidden must be 16-byte aligned");
   uint32_t* st = device_status_ptr();
   if (!st) return EXQ_ERR_CUDA;
   auto s = static_cast<cudaStream_t>(stream);
