@@ -88,3 +88,25 @@ def test_bank_cache_round_trip_on_gpu(cuda, tmp_path):
     ids, w = zipf_router(24, 16, 8, seed=6)
     x = hidden_states(24, c.hidden, seed=6).to(cuda)
     assert torch.equal(got(x, ids.to(cuda), w.to(cuda)), ref(x, ids.to(cuda), w.to(cuda)))
+
+
+def test_offloaded_bank_zero_tokens_and_prefetch_ahead(cuda):
+    """No tokens; experts prefetched ahead of the call they serve count as
+    hits in that call."""
+    from exq_b200.offload import OffloadedExpertBank
+    from exq_b200.synth import hidden_states
+    ref, src, tiers, c = _banks(cuda)
+    int4 = [e for e, t in enumerate(tiers) if t == "INT4"]
+    off = OffloadedExpertBank(src, gpu_slots=3)
+    y0 = off(torch.zeros(0, c.hidden, dtype=torch.float16, device=cuda),
+             torch.zeros(0, 2, dtype=torch.int32, device=cuda),
+             torch.zeros(0, 2, device=cuda))
+    assert y0.shape == (0, c.hidden)
+    off.prefetch(int4[:2])
+    misses = off.stats["misses"]
+    ids = torch.tensor([[int4[0], int4[1]]] * 3, dtype=torch.int32)
+    w = torch.full((3, 2), 0.5)
+    x = hidden_states(3, c.hidden, seed=1).to(cuda)
+    y = off(x, ids.to(cuda), w.to(cuda), ids_host=ids)
+    assert off.stats["misses"] == misses and off.stats["hits"] >= 2
+    assert torch.equal(y, ref(x, ids.to(cuda), w.to(cuda)))

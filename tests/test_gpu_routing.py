@@ -271,3 +271,29 @@ def test_layer_from_router_logits(cuda, cfg, t):
     assert OM.rel_l2(y, ref) < 5e-3
     y2 = bank(x.to(cuda), r_ids.to(cuda).int(), r_w.to(cuda))
     assert OM.rel_l2(y, y2) < 1e-5
+
+
+def test_layer_from_logits_edges(cuda):
+    """Zero tokens; bf16 logits without renormalisation (OLMoE-style routing)
+    against the oracle router feeding the oracle layer."""
+    from _layer_helpers import oracle_layer
+    from exq_b200 import ExpertBank
+    from exq_b200.synth import CONFIGS, expert_weights, hidden_states
+    from oracle import moe as OM
+    c = CONFIGS["olmoe"]
+    w13, w2 = expert_weights(c.n_experts, c.inter, c.hidden, seed=4, dtype=torch.float16,
+                             device=cuda)
+    bank = ExpertBank.from_dense(w13, w2, None, act_dtype=torch.float16)
+    del w13, w2
+    y0 = bank.forward_from_logits(torch.zeros(0, c.hidden, dtype=torch.float16, device=cuda),
+                                  torch.zeros(0, c.n_experts, device=cuda), c.top_k)
+    assert y0.shape == (0, c.hidden)
+    g = torch.Generator().manual_seed(12)
+    logits = torch.randn(19, c.n_experts, generator=g).to(torch.bfloat16)
+    x = hidden_states(19, c.hidden, seed=12)
+    y = bank.forward_from_logits(x.to(cuda), logits.to(cuda), c.top_k, renormalize=False)
+    r_ids, r_w = OR.router_topk(logits.float(), c.top_k, False)
+    ref = oracle_layer(bank, x, r_ids, r_w)
+    assert OM.rel_l2(y, ref) < 5e-3
+    with pytest.raises(ValueError):
+        bank.forward_from_logits(x.to(cuda), logits[:, :10].to(cuda), c.top_k)
