@@ -88,6 +88,14 @@ int launch_route(RouteParams& p, int mode, cudaStream_t stream, bool pdl = false
 // One layer call's routing fused with the activation gather (route_gather.cu).
 constexpr int kRouteGatherMaxBuckets = 1024;
 constexpr int64_t kRouteGatherMaxSlots = 4096;
+// Layer calls up to this many slots route and gather in one multi-CTA kernel
+// (its shared memory holds three ints per slot: 197 KB at the limit).  Above
+// kRouteGatherMaxSlots only calls averaging at most
+// kRouteGatherFusedMaxRowsPerBucket rows per expert take it: with a few deep
+// experts (Mixtral prefill, 1024 rows each) the separate routing and gather
+// kernels are faster.
+constexpr int64_t kRouteGatherFusedMaxSlots = 16384;
+constexpr int64_t kRouteGatherFusedMaxRowsPerBucket = 512;
 
 struct RouteGatherParams {
   const void* ids;      // [T, top_k] expert ids

@@ -1444,7 +1444,10 @@ static int layer_forward(const exq_moe_weights* w, const void* hidden_states, in
   const bool do_gu = first_stage <= 2 && end_stage > 2;
   const bool do_dn = first_stage <= 3 && end_stage > 3;
   // decode-sized calls route and gather in one kernel (stage 0; stage 1 is empty)
-  const bool fused = n_slots <= kRouteGatherMaxSlots && n_total <= kRouteGatherMaxBuckets;
+  const bool fused = n_total <= kRouteGatherMaxBuckets &&
+                     (n_slots <= kRouteGatherMaxSlots ||
+                      (n_slots <= kRouteGatherFusedMaxSlots &&
+                       n_slots <= kRouteGatherFusedMaxRowsPerBucket * n_total));
   // decode-sized calls: the GEMM launch also does the combine (its CTAs split
   // the tokens once every item is stored); larger ones launch it apart
   const bool fuse_combine = do_dn && first_stage <= 4 && end_stage > 4 && fused &&

@@ -139,18 +139,33 @@ __global__ void __launch_bounds__(kRgThreads) route_gather_kernel(const RouteGat
   const int chunk = (n + static_cast<int>(gridDim.x) - 1) / static_cast<int>(gridDim.x);
   const int s0 = min(n, static_cast<int>(blockIdx.x) * chunk), s1 = min(n, s0 + chunk);
 
-  // pass 1: bucket counts of all slots and of the slots before s0 (order-free)
-  for (int i = threadIdx.x; i < n; i += kRgThreads) {
-    const int e = bkt[i];
-    if (e >= 0) {
-      atomicAdd(&cnt_all[e], 1);
-      if (i < s0) atomicAdd(&cnt_pre[e], 1);
+  // pass 1: bucket counts of all slots and of the slots before s0 (order-free).
+  // With few buckets (large calls of a few experts) the lanes of a warp that
+  // hold one bucket add their count once, instead of all contending for it.
+  if (nb <= 32) {
+    for (int i0 = 0; i0 < n; i0 += kRgThreads) {
+      const int i = i0 + threadIdx.x;
+      const int e = i < n ? bkt[i] : -1;
+      const unsigned same = __match_any_sync(0xffffffffu, e);
+      const unsigned pre = same & __ballot_sync(0xffffffffu, i < s0);
+      if (e >= 0 && lane == __ffs(same) - 1) {
+        atomicAdd(&cnt_all[e], __popc(same));
+        if (pre) atomicAdd(&cnt_pre[e], __popc(pre));
+      }
+    }
+  } else {
+    for (int i = threadIdx.x; i < n; i += kRgThreads) {
+      const int e = bkt[i];
+      if (e >= 0) {
+        atomicAdd(&cnt_all[e], 1);
+        if (i < s0) atomicAdd(&cnt_pre[e], 1);
+      }
     }
   }
   __syncthreads();
 
   // pass 2: bucket bases and tile starts (one scan of (tiles << 16 | rows):
-  // both stay below 2^16, n <= 4096)
+  // both stay below 2^16, n <= 16384)
   int carry = 0, tile_carry = 0;
   for (int c0 = 0; c0 < nb; c0 += kRgThreads) {
     const int e = c0 + threadIdx.x;
@@ -258,7 +273,7 @@ __global__ void __launch_bounds__(kRgThreads) route_gather_kernel(const RouteGat
 }  // namespace
 
 int launch_route_gather(RouteGatherParams& p, cudaStream_t stream, bool pdl) {
-  if (p.n_buckets < 1 || p.n_buckets > kRouteGatherMaxBuckets || p.n > kRouteGatherMaxSlots) {
+  if (p.n_buckets < 1 || p.n_buckets > kRouteGatherMaxBuckets || p.n > kRouteGatherFusedMaxSlots) {
     set_error("route_gather: %d buckets / %lld slots outside the fused path", p.n_buckets,
               (long long)p.n);
     return EXQ_ERR_UNSUPPORTED;
@@ -271,16 +286,17 @@ int launch_route_gather(RouteGatherParams& p, cudaStream_t stream, bool pdl) {
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev >= 0 && dev < 64 && !attr_set[dev]) {
-    const size_t mx = route_gather_smem_bytes(kRouteGatherMaxBuckets, kRouteGatherMaxSlots);
+    const size_t mx = route_gather_smem_bytes(kRouteGatherMaxBuckets, kRouteGatherFusedMaxSlots);
     cudaFuncSetAttribute(route_gather_kernel<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          static_cast<int>(mx));
     cudaFuncSetAttribute(route_gather_kernel<__nv_bfloat16>,
                          cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(mx));
     attr_set[dev] = true;
   }
-  // at least one sorted position per CTA, at most two CTAs per SM
+  // at least one sorted position per CTA; two CTAs per SM while two fit in
+  // shared memory, else one (no CTA waits for another, so more would only queue)
   int64_t grid = p.n;
-  const int64_t cap = 2 * static_cast<int64_t>(num_sms());
+  const int64_t cap = (smem > 110 * 1024 ? 1 : 2) * static_cast<int64_t>(num_sms());
   if (grid > cap) grid = cap;
   cudaError_t e;
   if (p.act_dtype == EXQ_F16)

@@ -328,7 +328,7 @@ class ExpertBank:
                 workspace: torch.Tensor | None = None) -> torch.Tensor:
         """The five stages route -> prep -> gate_up -> down -> weighted combine.
 
-        Up to 4096 (token, expert) slots the route and prep stages are one
+        Up to 16384 (token, expert) slots the route and prep stages are one
         fused launch, and gate_up, down and the combine are one GEMM launch
         that builds its tile list from the ids: two launches per call.  Above
         that, routing and the activation prep are separate launches (three)."""
@@ -340,7 +340,7 @@ class ExpertBank:
         """The layer from router logits [T, n_routed] (fp32/fp16/bf16): the
         fused router top-k (softmax, top_k, optional renormalisation, as
         ``kernels.router_topk``) feeding the routing stage in one C call,
-        ``exq_moe_layer_forward_from_logits``.  Up to 4096 slots that is three
+        ``exq_moe_layer_forward_from_logits``.  Up to 16384 slots that is three
         launches, the routing kernel chained programmatically after the
         router."""
         dev = L.require_cuda(hidden_states, router_logits)

@@ -273,8 +273,9 @@ typedef struct exq_moe_weights {
  * does); topk_ids [n_tokens, top_k] int32/int64, where a negative id marks an
  * unused slot (no expert) and an id >= n_routed is dropped and flagged
  * (EXQ_DEV_BAD_EXPERT_ID); topk_weights [n_tokens, top_k] f32/f16/bf16.  Up
- * to 4096 slots: two launches (route fused with prep; the GEMM launch with
- * the combine at its end); above: route, prep, GEMM, combine.  No host
+ * to 16384 slots and 1024 experts: two launches (route fused with prep; the
+ * GEMM launch with the combine at its end); above: route, prep, GEMM, and
+ * the combine apart when the GEMM launch cannot stage it.  No host
  * synchronisation. */
 EXQ_API size_t exq_moe_layer_workspace_bytes(int64_t n_tokens, int32_t top_k, int32_t n_shared,
                                              int32_t n_experts_total, int64_t hidden,
@@ -291,7 +292,7 @@ EXQ_API int exq_moe_layer_forward(const exq_moe_weights* weights, const void* hi
  * so a caller may run them separately on one stream (per-kernel timing) with
  * identical arguments, each stage once and in order after stage 0;
  * exq_moe_layer_forward = stages [0, 5).  Stages 2 and 3 in one range are one
- * launch; with stage 4 too (up to 4096 slots), the combine runs in it. */
+ * launch; with stage 4 too (up to 16384 slots), the combine runs in it. */
 #define EXQ_LAYER_STAGES 5
 EXQ_API int exq_moe_layer_forward_range(const exq_moe_weights* weights,
                                         const void* hidden_states, int act_dtype,

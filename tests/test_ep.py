@@ -44,17 +44,17 @@ def test_ep_nccl_two_gpus_matches_single_gpu():
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("max_tokens", [64, 2100])
+@pytest.mark.parametrize("max_tokens", [64, 2100, 8300])
 def test_ep_peer_one_gpu_matches_single_gpu(max_tokens):
     """The peer-memory exchange with one rank: dispatch, flags, the local layer
     on the padded receive area, the return and the combine on one GPU.  With
-    max_tokens 2100 the receive area (4200 rows) is above the fused routing
+    max_tokens 8300 the receive area (16600 rows) is above the fused routing
     limit, so the layer takes its separate route and prep kernels."""
     mp.spawn(EH.gpu_worker, args=(1, _free_port(), "peer", max_tokens), nprocs=1, join=True)
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("max_tokens", [64, 2100])
+@pytest.mark.parametrize("max_tokens", [64, 2100, 4200])
 def test_ep_peer_one_gpu_with_shared_experts_folded(max_tokens):
     """Two BF16 shared experts folded into the expert launch (own receive
     block): bit for bit the exchange with the shared experts run apart, and

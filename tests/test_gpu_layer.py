@@ -151,17 +151,17 @@ def test_layer_mixtral_long_k_vs_oracle(cuda):
 
 @pytest.mark.parametrize("tiers", [None, "mixed"])
 def test_layer_above_fused_routing_limit(cuda, tiers):
-    """More than 4096 slots (Qwen3 shape, 600 tokens x top-8 = 4800): the
+    """More than 16384 slots (Qwen3 shape, 2100 tokens x top-8 = 16800): the
     routing runs as the single-CTA sort plus the separate activation prep, the
     GEMM builds no tile list of its own; checked on a token sample, all tiers."""
     from exq_b200.synth import CONFIGS, hidden_states, tier_plan, zipf_router
     c0 = CONFIGS["qwen3"]
     bank, c = _bank("qwen3", cuda, tiers=tier_plan(c0.n_experts, seed=4) if tiers else None)
-    ids, w = zipf_router(600, 128, 8, seed=21)
-    x = hidden_states(600, c.hidden, seed=21)
-    assert ids.numel() > 4096
+    ids, w = zipf_router(2100, 128, 8, seed=21)
+    x = hidden_states(2100, c.hidden, seed=21)
+    assert ids.numel() > 16384
     y = bank(x.to(cuda), ids.to(cuda), w.to(cuda)).cpu()
-    sample = torch.tensor([0, 3, 299, 300, 598, 599])
+    sample = torch.tensor([0, 3, 1049, 1050, 2098, 2099])
     ref = oracle_layer(bank, x, ids, w, tokens=sample)
     assert OM.rel_l2(y[sample], ref) < TOL
 
@@ -396,3 +396,27 @@ def test_layer_128_token_tiles(cuda, cfg, t, tiers):
     assert torch.equal(ys, y[sd])
     ref = oracle_layer(bank, x, ids, w, tokens=sample)
     assert OM.rel_l2(ys, ref) < TOL
+
+
+
+@pytest.mark.parametrize("t,e", [(600, 128), (1800, 128), (1100, 16), (2048, 4)])
+def test_layer_fused_routing_between_4096_and_16384_slots(cuda, t, e):
+    """4096 < slots <= 16384: up to 512 rows per expert on average, the
+    multi-CTA routing kernel with the gather (few buckets: per-warp aggregated
+    counts) and the GEMM building its tile list from the ids; deeper experts
+    (2048 tokens over 4 experts) the separate routing and gather kernels.  A
+    token sample against the oracle, the sample alone bit for bit, and the
+    launch chain against separately launched stages."""
+    from exq_b200.synth import hidden_states, zipf_router
+    bank, c = _bank("qwen3", cuda, n_experts=e)
+    ids, w = zipf_router(t, e, 4 if e <= 16 else 8, seed=t)
+    assert 4096 < ids.numel() <= 16384
+    x = hidden_states(t, c.hidden, seed=t)
+    xd, idd, wd = x.to(cuda), ids.to(cuda), w.to(cuda)
+    y, y_sep, y_alone = _stage_runs(bank, xd, idd, wd)
+    assert torch.equal(y, y_sep) and torch.equal(y, y_alone)
+    sample = torch.tensor([0, 5, t // 2, t - 1])
+    sd = sample.to(cuda)
+    assert torch.equal(bank(xd[sd], idd[sd], wd[sd]), y[sd])
+    ref = oracle_layer(bank, x, ids, w, tokens=sample)
+    assert OM.rel_l2(y[sd], ref) < TOL
