@@ -934,6 +934,73 @@ def stack_measure(dev, name, tokens, n_layers, tiers_fn=None, reps=20, warmup=3)
             "gpu_launches_per_stack": 2 * n_layers}
 
 
+def api_measure(dev, n_sets=4, tokens=(1, 8, 64, 256), reps=200):
+    """The per-projection API, `kernels.moe_int4_forward` (the warp-MMA
+    grouped GEMM of csrc/moe_gemm.cu in place of the Triton
+    `_moe_gemm_int4_kernel`, exq/kernels/moe_int4_kernel.py:245-327), on the
+    Qwen3 gate_up projection (128 experts x [1536, 2048], INT4 g128, sort and
+    gather included), beside the layer path's routing + gate_up launches
+    (stages 0-2: `route_gather_kernel` then the tcgen05 `moe_tc_kernel`, mid
+    rows after SiLU*mul) on the same weights.  Four weight sets rotate (0.8 GB
+    of packed gate_up weights, above L2); CUDA graph replays.  `weight_gbps`:
+    the touched experts' packed gate_up bytes per call over the call's time."""
+    import torch
+    from exq_b200 import ExpertBank
+    from exq_b200 import kernels as K
+    from exq_b200.synth import expert_weights
+    c = CFG
+    sets = []
+    for li in range(n_sets):
+        w13, w2 = expert_weights(c["n_experts"], c["inter"], c["hidden"], seed=300 + li,
+                                 dtype=torch.float16, device=dev)
+        packed, scales = K.pack_experts_int4(w13)
+        bank = ExpertBank.from_dense(w13, w2, None, act_dtype=torch.float16)
+        del w13, w2
+        sets.append((packed, scales, bank))
+    torch.cuda.synchronize(dev)
+    rows = 2 * c["inter"]
+    per_expert = rows * c["hidden"] // 2 + rows * (c["hidden"] // 128) * 2
+    peak, peak_kind = measured_peak()
+    out = {"projection": f"gate_up [{c['n_experts']}, {rows}, {c['hidden']}] INT4 g128",
+           "api": "kernels.moe_int4_forward (moe_gemm_kernel, mma.sync)",
+           "layer": "ExpertBank stages 0-2 (route_gather_kernel + moe_tc_kernel, tcgen05)",
+           "peak_kind": peak_kind, "per_T": {}}
+    for t in tokens:
+        inp = layer_inputs(dev, t, n_sets, seed0=40)
+        touched = statistics.mean(len(set(ci.reshape(-1).tolist())) for (_, _, _, ci) in inp)
+        g_api, g_lay = [], []
+        s = torch.cuda.Stream(dev)
+        s.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(s):
+            for (packed, scales, bank), (x, ids, w, _) in zip(sets, inp):
+                K.moe_int4_forward(x, packed, scales, ids, c["n_experts"])   # warm (workspace, descriptors)
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g, stream=s):
+                    K.moe_int4_forward(x, packed, scales, ids, c["n_experts"])
+                g_api.append(g)
+                bank.reserve(t, c["top_k"])
+                mid = torch.empty(t, c["hidden"], dtype=torch.float16, device=dev)
+                bank.forward_range(x, ids, w, 0, 3, out=mid)
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g, stream=s):
+                    bank.forward_range(x, ids, w, 0, 3, out=mid)
+                g_lay.append(g)
+        torch.cuda.current_stream(dev).wait_stream(s)
+        torch.cuda.synchronize(dev)
+        r = {"experts_touched": round(touched, 1)}
+        for key, gs in (("api", g_api), ("layer", g_lay)):
+            us = time_graphs(gs, reps, 10, dev) / reps * 1e6
+            gbps = touched * per_expert / (us * 1e-6) / 1e9
+            r[key] = {"us": round(us, 2), "weight_gbps": round(gbps, 1),
+                      "frac": round(gbps / peak, 3)}
+        r["layer_speedup"] = round(r["api"]["us"] / r["layer"]["us"], 2)
+        out["per_T"][str(t)] = r
+        del g_api, g_lay
+    del sets
+    torch.cuda.empty_cache()
+    return out
+
+
 def configs_measure(dev):
     """The BASELINE configs beside the headline (C2): C1 (OLMoE layer, 16
     tokens), C3 (16-layer mixed BF16/INT8/INT4 stack, 64 tokens, one grouped
@@ -1096,10 +1163,12 @@ def main():
 
     cfgs = None
     router = None
+    api = None
     if world == 1 and not args.no_configs:
         router = router_measure(dev, banks)
         cfgs = configs_measure(dev)
         cfgs["offload_qwen3"] = offload_measure(dev)
+        api = api_measure(dev)
 
     ep = {}
     if not args.no_ep:
@@ -1133,8 +1202,8 @@ def main():
         "e2e": {"value": round(e2e_val, 1), "unit": UNIT, "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "steps": e2e_steps,
                 "us_per_layer": round(1e6 * t_e2e / e2e_steps, 2)},
-        # route+gather and the GEMM launch per layer call (the separate
-        # activation-prep launch only runs above 4096 slots)
+        # route+gather and the GEMM launch per layer call (separate routing
+        # and activation-prep launches only for calls above 4096 slots)
         "gpu_launches": (2 if c["tokens"] * c["top_k"] <= 4096 else 3) * args.steps,
         "clocks": clk.summary(),
         "sweep": sweep,
@@ -1143,6 +1212,8 @@ def main():
         line["router"] = router
     if cfgs is not None:
         line["configs"] = cfgs
+    if api is not None:
+        line["api"] = api
     if ref_gpu is not None:
         line["reference_gpu"] = ref_gpu
     if ep:
