@@ -1046,41 +1046,67 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
 
 // Activation prep: A[pos, :] = fp16(hidden[token(pos), :]) with every octet of
 // k permuted to [0,4,1,5,2,6,3,7].  Positions at or past *routed_total + mt
-// are read by no GEMM tile and are left alone.
+// are read by no GEMM tile and are left alone (the grid is sized for all
+// positions, but only that many rows are live: an expert-parallel receive
+// area is mostly padding).  Blocks take kPrepRows rows at a time, threads the
+// 16-byte chunks of a row; a thread's loads of the kPrepRows rows are in
+// flight together.
+constexpr int kPrepRows = 4;
+constexpr int kPrepThreads = 256;
+
 template <typename T>
-__global__ void prep_act_kernel(const T* __restrict__ hidden, int64_t hid, int64_t n_tokens,
-                                const int32_t* sorted_slot, int spt, int64_t n_pos,
-                                const int32_t* routed_total, int mt, __half* __restrict__ out) {
+__device__ __forceinline__ uint4 prep_octet(uint4 v) {
+  uint32_t w[4] = {v.x, v.y, v.z, v.w};
+  if (!std::is_same<T, __half>::value) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const __nv_bfloat162 b = *reinterpret_cast<__nv_bfloat162*>(&w[j]);
+      const float2 f = __bfloat1622float2(b);
+      __half2 hf = __floats2half2_rn(f.x, f.y);
+      w[j] = *reinterpret_cast<uint32_t*>(&hf);
+    }
+  }
+  uint4 r;
+  r.x = prmt(w[0], w[2], 0x5410u);  // (k0, k4)
+  r.y = prmt(w[0], w[2], 0x7632u);  // (k1, k5)
+  r.z = prmt(w[1], w[3], 0x5410u);  // (k2, k6)
+  r.w = prmt(w[1], w[3], 0x7632u);  // (k3, k7)
+  return r;
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kPrepThreads) prep_act_kernel(
+    const T* __restrict__ hidden, int64_t hid, int64_t n_tokens, const int32_t* sorted_slot,
+    int spt, int64_t n_pos, const int32_t* routed_total, int mt, __half* __restrict__ out) {
   pdl_wait();
   pdl_trigger();
-  const int64_t octs = hid / 8;
-  const int64_t lim = min(n_pos, static_cast<int64_t>(*routed_total) + mt);
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < lim * octs;
-       i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t pos = i / octs, o = i - pos * octs;
-    const int32_t slot = sorted_slot[pos];
-    const int64_t tok = slot / spt;
-    if (slot < 0 || tok >= n_tokens) {  // unused position (dropped slot): zero row
-      reinterpret_cast<uint4*>(out)[((o >> 3) * n_pos + pos) * 8 + (o & 7)] = make_uint4(0, 0, 0, 0);
-      continue;
-    }
-    const uint4 v = reinterpret_cast<const uint4*>(hidden + tok * hid)[o];
-    uint32_t w[4] = {v.x, v.y, v.z, v.w};
-    if (!std::is_same<T, __half>::value) {
+  const int octs = static_cast<int>(hid / 8);
+  const int lim = static_cast<int>(min(n_pos, static_cast<int64_t>(*routed_total) + mt));
+  uint4* dst = reinterpret_cast<uint4*>(out);
+  for (int r0 = blockIdx.x * kPrepRows; r0 < lim; r0 += gridDim.x * kPrepRows) {
+    const uint4* src[kPrepRows];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const __nv_bfloat162 b = *reinterpret_cast<__nv_bfloat162*>(&w[j]);
-        const float2 f = __bfloat1622float2(b);
-        __half2 hf = __floats2half2_rn(f.x, f.y);
-        w[j] = *reinterpret_cast<uint32_t*>(&hf);
+    for (int u = 0; u < kPrepRows; ++u) {
+      const int pos = r0 + u;
+      const int32_t slot = pos < lim ? sorted_slot[pos] : -1;
+      const int tok = slot >= 0 ? slot / spt : -1;  // slot < 0: a dropped slot (zero row)
+      src[u] = tok >= 0 && tok < n_tokens
+                   ? reinterpret_cast<const uint4*>(hidden + static_cast<int64_t>(tok) * hid)
+                   : nullptr;
+    }
+    for (int o = threadIdx.x; o < octs; o += kPrepThreads) {
+      uint4 v[kPrepRows];
+#pragma unroll
+      for (int u = 0; u < kPrepRows; ++u) v[u] = src[u] ? __ldg(src[u] + o) : make_uint4(0, 0, 0, 0);
+#pragma unroll
+      for (int u = 0; u < kPrepRows; ++u) {
+        const int pos = r0 + u;
+        if (pos >= lim) break;
+        // stage-major [hid / 64][n_pos][64]
+        dst[((static_cast<int64_t>(o) >> 3) * n_pos + pos) * 8 + (o & 7)] =
+            src[u] ? prep_octet<T>(v[u]) : make_uint4(0, 0, 0, 0);
       }
     }
-    uint4 r;
-    r.x = prmt(w[0], w[2], 0x5410u);  // (k0, k4)
-    r.y = prmt(w[0], w[2], 0x7632u);  // (k1, k5)
-    r.z = prmt(w[1], w[3], 0x5410u);  // (k2, k6)
-    r.w = prmt(w[1], w[3], 0x7632u);  // (k3, k7)
-    reinterpret_cast<uint4*>(out)[((o >> 3) * n_pos + pos) * 8 + (o & 7)] = r;  // stage-major
   }
 }
 
@@ -1267,16 +1293,17 @@ int launch_prep(const void* hidden, int act_dtype, int64_t hid, int64_t n_tokens
                 const int32_t* sorted_slot, int spt, int64_t n_pos, const int32_t* routed_total,
                 int mt, __half* out, cudaStream_t stream, bool pdl) {
   if (n_pos == 0) return EXQ_OK;
-  const int64_t work = n_pos * (hid / 8);
-  int64_t grid = (work + 255) / 256;
-  if (grid > 65535) grid = 65535;
+  // row groups, at most eight blocks per SM (grid-stride beyond)
+  int64_t grid = (n_pos + kPrepRows - 1) / kPrepRows;
+  if (grid > 8 * num_sms()) grid = 8 * num_sms();
   cudaError_t e;
   if (act_dtype == EXQ_F16)
-    e = launch_pdl(pdl, prep_act_kernel<__half>, dim3((int)grid), dim3(256), 0, stream,
+    e = launch_pdl(pdl, prep_act_kernel<__half>, dim3((int)grid), dim3(kPrepThreads), 0, stream,
                    static_cast<const __half*>(hidden), hid, n_tokens, sorted_slot, spt, n_pos,
                    routed_total, mt, out);
   else
-    e = launch_pdl(pdl, prep_act_kernel<__nv_bfloat16>, dim3((int)grid), dim3(256), 0, stream,
+    e = launch_pdl(pdl, prep_act_kernel<__nv_bfloat16>, dim3((int)grid), dim3(kPrepThreads), 0,
+                   stream,
                    static_cast<const __nv_bfloat16*>(hidden), hid, n_tokens, sorted_slot, spt, n_pos,
                    routed_total, mt, out);
   if (e != cudaSuccess) {

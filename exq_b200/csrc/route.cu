@@ -20,6 +20,22 @@ constexpr int kRouteThreads = 1024;
 constexpr int kRouteWarps = kRouteThreads / 32;
 constexpr int kMaxBuckets = 1024;
 
+// Token and slot of layer slot i = t * spt + j.  In 32 bits (launch_route
+// keeps n below 2^30): a 64-bit division is a long software routine, and this
+// runs for every slot on one CTA.  One slot per token (expert-parallel
+// receive areas) needs no division.
+__device__ __forceinline__ void split_slot(int64_t i, int spt, int64_t* t, int* j) {
+  if (spt == 1) {
+    *t = i;
+    *j = 0;
+    return;
+  }
+  const int ii = static_cast<int>(i);
+  const int tt = ii / spt;
+  *t = tt;
+  *j = ii - tt * spt;
+}
+
 // Bucket and value of element i (bucket < 0: element skipped).
 __device__ __forceinline__ int route_bucket(const RouteParams& p, int mode, int64_t i,
                                             int64_t* value) {
@@ -35,8 +51,9 @@ __device__ __forceinline__ int route_bucket(const RouteParams& p, int mode, int6
     return e;
   }
   if (mode == kRouteLayer) {
-    const int64_t t = i / p.slots_per_token;
-    const int j = static_cast<int>(i - t * p.slots_per_token);
+    int64_t t;
+    int j;
+    split_slot(i, p.slots_per_token, &t, &j);
     *value = i;
     if (j >= p.top_k) return p.n_routed + (j - p.top_k);  // shared expert
     const int64_t e = load_index(p.ids, p.ids_dtype, t * p.top_k + j);
@@ -241,8 +258,9 @@ __global__ void __launch_bounds__(kRouteThreads, 1) route_kernel(RouteParams p, 
           p.sorted_i32[pos] = static_cast<int32_t>(val);
           if (p.pos_of_slot) p.pos_of_slot[val] = pos;
           if (p.sorted_w) {
-            const int64_t t = val / p.slots_per_token;
-            const int j = static_cast<int>(val - t * p.slots_per_token);
+            int64_t t;
+            int j;
+            split_slot(val, p.slots_per_token, &t, &j);
             p.sorted_w[pos] =
                 j < p.top_k ? load_as_f32(p.topk_w, p.w_dtype, t * p.top_k + j) : 1.0f;
           }
