@@ -89,7 +89,7 @@ int launch_route(RouteParams& p, int mode, cudaStream_t stream, bool pdl = false
 constexpr int kRouteGatherMaxBuckets = 1024;
 constexpr int64_t kRouteGatherMaxSlots = 4096;
 // Layer calls up to this many slots route and gather in one multi-CTA kernel
-// (its shared memory holds three ints per slot: 197 KB at the limit).  Above
+// (its shared memory holds two ints per slot: 131 KB at the limit).  Above
 // kRouteGatherMaxSlots only calls averaging at most
 // kRouteGatherFusedMaxRowsPerBucket rows per expert take it: with a few deep
 // experts (Mixtral prefill, 1024 rows each) the separate routing and gather

@@ -28,10 +28,22 @@ constexpr int kRgThreads = 256;
 constexpr int kRgWarps = kRgThreads / 32;
 
 size_t route_gather_smem_bytes(int n_buckets, int64_t n) {
-  return sizeof(int) * (static_cast<size_t>(4) * n_buckets + 34 + 3 * n);
+  return sizeof(int) * (static_cast<size_t>(4) * n_buckets + 34 + 2 * n);
 }
 
 namespace {
+
+// (token, slot in token) of slot i; one slot per token (expert-parallel
+// receive areas) needs no division
+__device__ __forceinline__ void rg_split(int i, int spt, int* t, int* j) {
+  if (spt == 1) {
+    *t = i;
+    *j = 0;
+  } else {
+    *t = i / spt;
+    *j = i - *t * spt;
+  }
+}
 
 __device__ __forceinline__ int rg_exclusive_scan(int v, int* tmp, int* excl) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -93,7 +105,6 @@ __global__ void __launch_bounds__(kRgThreads) route_gather_kernel(const RouteGat
   int* tmp = tstart + nb;            // [33] scan scratch, [33] routed total
   int* bkt = tmp + 34;               // [n] bucket of every slot (-1: dropped)
   int* slot_pos = bkt + n;           // [chunk] sorted position of this CTA's slots (-1: dropped)
-  float* wslot = reinterpret_cast<float*>(slot_pos + n);  // [n] router weight of every slot
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
 
   pdl_wait();
@@ -103,21 +114,21 @@ __global__ void __launch_bounds__(kRgThreads) route_gather_kernel(const RouteGat
   // bucket of every slot; the id loads of 8 slots are issued before any is used
   for (int i0 = threadIdx.x; i0 < n; i0 += 8 * kRgThreads) {
     int64_t v[8];
-    float wv[8];
 #pragma unroll
     for (int u = 0; u < 8; ++u) {
       const int i = i0 + u * kRgThreads;
-      const int t = i / p.spt, j = i - t * p.spt;
+      int t, j;
+      rg_split(i, p.spt, &t, &j);
       const bool routed = i < n && j < p.top_k;
       const int64_t src = routed ? static_cast<int64_t>(t) * p.top_k + j : 0;
       v[u] = load_index(p.ids, p.ids_dtype, src);
-      wv[u] = load_as_f32(p.topk_w, p.w_dtype, src);
     }
 #pragma unroll
     for (int u = 0; u < 8; ++u) {
       const int i = i0 + u * kRgThreads;
       if (i >= n) break;
-      const int t = i / p.spt, j = i - t * p.spt;
+      int t, j;
+      rg_split(i, p.spt, &t, &j);
       int e;
       if (j >= p.top_k) {
         e = p.n_routed + (j - p.top_k);  // always-on shared expert
@@ -127,7 +138,6 @@ __global__ void __launch_bounds__(kRgThreads) route_gather_kernel(const RouteGat
         if (v[u] >= p.n_routed && blockIdx.x == 0) atomicOr(p.status, EXQ_DEV_BAD_EXPERT_ID);
       }
       bkt[i] = e;
-      wslot[i] = j < p.top_k ? wv[u] : 1.0f;  // shared experts weigh 1
     }
   }
   __syncthreads();
@@ -221,7 +231,12 @@ __global__ void __launch_bounds__(kRgThreads) route_gather_kernel(const RouteGat
     const int pos = slot_pos[i - s0];
     p.pos_of_slot[i] = pos;
     if (pos >= 0) {
-      p.sorted_w[pos] = wslot[i];
+      // the router weight of this CTA's slots only; shared experts weigh 1
+      int t, j;
+      rg_split(i, p.spt, &t, &j);
+      p.sorted_w[pos] =
+          j < p.top_k ? load_as_f32(p.topk_w, p.w_dtype, static_cast<int64_t>(t) * p.top_k + j)
+                      : 1.0f;
       if (p.sorted_slot) p.sorted_slot[pos] = i;
     }
   }
@@ -229,32 +244,33 @@ __global__ void __launch_bounds__(kRgThreads) route_gather_kernel(const RouteGat
   for (int64_t i = static_cast<int64_t>(blockIdx.x) * kRgThreads + threadIdx.x; i < p.n_counters;
        i += static_cast<int64_t>(gridDim.x) * kRgThreads)
     p.counters[i] = 0;
-  // row copies, slot by slot: each thread issues 8 independent 16-byte loads
-  // before storing
+  // row copies: threads take the 16-byte chunks of a row, kU rows at a time
+  // (a thread's loads of the kU rows are in flight together); a dropped slot
+  // has no row
   const int octs = static_cast<int>(p.hidden_size / 8);
   const T* hid = static_cast<const T*>(p.hidden);
-  const int total = (s1 - s0) * octs;
+  uint4* act = reinterpret_cast<uint4*>(p.act);
   constexpr int kU = 8;
-  for (int i0 = threadIdx.x; i0 < total; i0 += kU * kRgThreads) {
-    uint4 v[kU];
-#pragma unroll
-    for (int u = 0; u < kU; ++u) {  // unconditional loads (row 0 stands in for unused ones)
-      const int idx = i0 + u * kRgThreads;
-      const int r = idx / octs;
-      const bool used = idx < total && slot_pos[r] >= 0;
-      const int64_t tok = used ? (s0 + r) / p.spt : 0;
-      v[u] = __ldg(reinterpret_cast<const uint4*>(hid + tok * p.hidden_size) + (used ? idx - r * octs : 0));
-    }
+  for (int r0 = 0; r0 < s1 - s0; r0 += kU) {
+    const uint4* src[kU];
+    int pos[kU];
 #pragma unroll
     for (int u = 0; u < kU; ++u) {
-      const int idx = i0 + u * kRgThreads;
-      if (idx < total) {
-        const int r = idx / octs, pos = slot_pos[r];
-        if (pos < 0) continue;  // a dropped slot has no row
+      const int r = r0 + u;
+      pos[u] = r < s1 - s0 ? slot_pos[r] : -1;
+      int t = 0, j = 0;
+      if (pos[u] >= 0) rg_split(s0 + r, p.spt, &t, &j);
+      src[u] = reinterpret_cast<const uint4*>(hid + static_cast<int64_t>(t) * p.hidden_size);
+    }
+    for (int o = threadIdx.x; o < octs; o += kRgThreads) {
+      uint4 v[kU];
+#pragma unroll
+      for (int u = 0; u < kU; ++u) v[u] = pos[u] >= 0 ? __ldg(src[u] + o) : make_uint4(0, 0, 0, 0);
+#pragma unroll
+      for (int u = 0; u < kU; ++u) {
         // act is stage-major [H/64][n][64]
-        const int o = idx - r * octs;
-        reinterpret_cast<uint4*>(p.act)[(static_cast<int64_t>(o >> 3) * n + pos) * 8 + (o & 7)] =
-            permute_octet<T>(v[u]);
+        if (pos[u] >= 0)
+          act[(static_cast<int64_t>(o >> 3) * n + pos[u]) * 8 + (o & 7)] = permute_octet<T>(v[u]);
       }
     }
   }
