@@ -64,6 +64,9 @@ def parse():
                     help="small case for ncu: one layer of the bench workload, 3 eager calls")
     ap.add_argument("--profile-prefill", action="store_true",
                     help="small case for ncu: the C4 prefill layer (T=4096), 3 eager calls")
+    ap.add_argument("--profile-ep-recv", type=int, default=0, metavar="N",
+                    help="small case for ncu: one rank's C5 expert-parallel layer call at N "
+                         "ranks (padded receive area), 3 eager calls")
     ap.add_argument("--no-ref-gpu", action="store_true",
                     help="skip the reference's own GPU path (Triton GEMMs + exq_dispatch_cuda)")
     ap.add_argument("--setup-reference", action="store_true",
@@ -1058,10 +1061,49 @@ def profile_prefill_case(tokens=4096):
     return 0
 
 
+def profile_ep_recv_case(n_ranks=8, cap=1536):
+    """One rank's DeepSeek-V2-Lite expert-parallel layer call at `n_ranks`
+    ranks, on one GPU: the receive area of (n_ranks + 1) blocks of `cap` rows
+    (the own block holding 256 tokens x 2 shared experts), 64 / n_ranks local
+    INT4 experts and the 2 BF16 shared ones, each peer block filled with the
+    row counts of a Zipf step (rest -1), called three times eagerly.  The
+    capture target for the routing launches of a mostly padded receive area."""
+    import torch
+    from exq_b200 import ExpertBank
+    from exq_b200.synth import CONFIGS, expert_weights, hidden_states
+    dev = torch.device("cuda", 0)
+    c = CONFIGS["dsv2_lite"]
+    nl = 64 // n_ranks
+    w13, w2 = expert_weights(nl + 2, c.inter, c.hidden, seed=1, device=dev)
+    bank = ExpertBank.from_dense(w13, w2, ["INT4"] * nl + ["BF16"] * 2, act_dtype=torch.bfloat16)
+    del w13, w2
+    rows = (n_ranks + 1) * cap
+    g = torch.Generator().manual_seed(3)
+    ids = torch.full((rows, 1), -1, dtype=torch.int32)
+    for blk in range(n_ranks):   # a block's filled rows come first
+        n = int(torch.randint(110, 290, (1,), generator=g))
+        ids[blk * cap: blk * cap + n, 0] = torch.randint(0, nl, (n,), generator=g).int()
+    ids[n_ranks * cap: n_ranks * cap + 512, 0] = torch.tensor([nl, nl + 1] * 256, dtype=torch.int32)
+    x = hidden_states(rows, c.hidden, seed=3).to(dev, torch.bfloat16)
+    w = torch.ones(rows, 1, device=dev)
+    ids = ids.to(dev)
+    out = torch.empty(rows, c.hidden, dtype=torch.bfloat16, device=dev)
+    bank.reserve(rows, 1)
+    torch.cuda.synchronize(dev)
+    for _ in range(3):   # stages 0-3: routing, gather, gate_up, down (no combine)
+        bank.forward_range(x, ids, w, 0, 4, out=out)
+    torch.cuda.synchronize(dev)
+    print(f"ep receive-area profile case ok: {n_ranks} ranks, {rows} rows, "
+          f"{int((ids >= 0).sum())} filled")
+    return 0
+
+
 def main():
     args = parse()
     if args.profile_prefill:
         return profile_prefill_case()
+    if args.profile_ep_recv:
+        return profile_ep_recv_case(args.profile_ep_recv)
     if args.setup_reference:
         return setup_reference()
     if args.impl == "reference":
