@@ -870,9 +870,14 @@ __global__ void __launch_bounds__(kThreads, 1) moe_tc_kernel(const __grid_consta
       }
     }
     if (p.fuse_combine) {
-      // every partial row of this CTA's items is stored: count the CTA
+      // every partial row of this CTA's items is stored: count the CTA.  The
+      // routing kernel zeroes the count, and a CTA without items gets here
+      // without having waited for it (its activation producer waits only per
+      // item): an add before that zero would be lost and the combine below
+      // would wait for a count that never comes.
       named_barrier(kEpiBar, 128);
       if (et == 0) {
+        pdl_wait();
         __threadfence();
         atomicAdd(p.dn_done, 1);
       }
