@@ -505,10 +505,12 @@ def launch_timing(banks, inputs, dev, reps=40):
     s = torch.cuda.Stream(dev)
     s.wait_stream(torch.cuda.current_stream(dev))
     ev_graphs = []
+    outs = []   # the graphs write into these: they must outlive the replays
     with torch.cuda.stream(s):
         for bank, (x, ids, w, _) in zip(banks, inputs):
             bank.reserve(x.shape[0], ids.shape[1])
             out = torch.empty(x.shape[0], bank.hidden, dtype=x.dtype, device=dev)
+            outs.append(out)
             evs = [torch.cuda.Event(enable_timing=True, external=True)
                    for _ in range(len(LAUNCHES) + 1)]
             g = torch.cuda.CUDAGraph()
@@ -781,9 +783,11 @@ def router_measure(dev, banks, tokens=256, reps=400):
     s = torch.cuda.Stream(dev)
     s.wait_stream(torch.cuda.current_stream(dev))
     gr, gl, gi = [], [], []
+    routed = []   # the layer graphs read these: they must outlive the replays
     with torch.cuda.stream(s):
         for bank, lg, x in zip(banks, logits, xs):
             ids, w = router_topk(lg, c["top_k"], True)
+            routed.append((ids, w))
             bank.forward_from_logits(x, lg, c["top_k"])
             bank(x, ids, w)
             g1 = torch.cuda.CUDAGraph()
@@ -972,6 +976,7 @@ def api_measure(dev, n_sets=4, tokens=(1, 8, 64, 256), reps=200):
         inp = layer_inputs(dev, t, n_sets, seed0=40)
         touched = statistics.mean(len(set(ci.reshape(-1).tolist())) for (_, _, _, ci) in inp)
         g_api, g_lay = [], []
+        mids = []   # the layer graphs write into these: they must outlive the replays
         s = torch.cuda.Stream(dev)
         s.wait_stream(torch.cuda.current_stream(dev))
         with torch.cuda.stream(s):
@@ -983,6 +988,7 @@ def api_measure(dev, n_sets=4, tokens=(1, 8, 64, 256), reps=200):
                 g_api.append(g)
                 bank.reserve(t, c["top_k"])
                 mid = torch.empty(t, c["hidden"], dtype=torch.float16, device=dev)
+                mids.append(mid)
                 bank.forward_range(x, ids, w, 0, 3, out=mid)
                 g = torch.cuda.CUDAGraph()
                 with torch.cuda.graph(g, stream=s):
